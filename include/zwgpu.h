@@ -1,0 +1,144 @@
+/*
+ * zwgpu: B200 (sm_100a) attention engine for zwhisper, plain C ABI.
+ *
+ * Replaces the CPU attention routine of the reference, `ops.attentionEx`
+ * (src/ops.zig:562-590), its MHA wrapper `ops.attention` (src/ops.zig:593-605) and the
+ * scratch sizers (src/ops.zig:545-560), and adds device-resident entry points for the
+ * four call sites: encoder self-attention (src/encoder.zig:167), decoder causal
+ * self-attention (src/decoder.zig:184) and cross-attention (src/decoder.zig:191), and
+ * Qwen2 grouped-query attention over a transposed key cache (src/llm.zig:178-202).
+ *
+ * Conventions (those of the reference's C ABI, include/zwhisper.h:33-75):
+ *   - every function returns int: ZWG_OK (0), ZWG_ERROR (2), ZWG_TIMEOUT (4, a device-side
+ *     wait gave up; the context stays usable); nothing traps or aborts;
+ *   - the caller owns every buffer; entry points taking device pointers allocate nothing
+ *     and take caller-sized workspace, like the reference's caller-sized scratch;
+ *   - a context is per device and per calling thread: calls on one context are not
+ *     re-entrant (the reference's handles are not thread-safe either, src/capi.zig:3-4).
+ *     Run one host thread per device for multi-GPU sharding.
+ * Strides and sizes are in elements. "bf16" buffers are uint16_t bit patterns.
+ */
+#ifndef ZWGPU_H
+#define ZWGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define ZWG_API __attribute__((visibility("default")))
+#else
+#define ZWG_API
+#endif
+
+#define ZWG_OK 0
+#define ZWG_ERROR 2
+#define ZWG_TIMEOUT 4
+
+/* Mirror of AttnShape (src/ops.zig:477-492). Query head h reads kv head
+ * h / (n_head / n_head_kv). With causal set, query i sees keys j <= n_kv - n_q + i.
+ * kt_stride == 0: keys are rows k[n_kv][kv_stride]; otherwise keys are kept transposed as
+ * k[n_head_kv][d][kt_stride] (src/llm.zig:27-28), as in the reference's optional kt_stride. */
+typedef struct zwg_attn_shape {
+    size_t n_q;
+    size_t n_kv;
+    size_t n_head;
+    size_t n_head_kv;
+    size_t d;
+    size_t q_stride;
+    size_t kv_stride;
+    size_t out_stride;
+    int32_t causal;
+    size_t kt_stride;
+} zwg_attn_shape;
+
+/* A batch of independent items (windows or sequences) sharing one shape; item b's
+ * buffers start at base + b * *_batch_stride (elements). No reference counterpart: the
+ * reference runs one window or sequence per call. */
+typedef struct zwg_batch {
+    size_t n_batch;
+    size_t q_batch_stride;
+    size_t k_batch_stride;
+    size_t v_batch_stride;
+    size_t out_batch_stride;
+} zwg_batch;
+
+/* Library version (the reference's zw_version, include/zwhisper.h:73, returns 3). */
+ZWG_API int zwg_version(void);
+
+/* Bind the calling thread to `device`, creating that device's context on first use
+ * (stream, error word). Counterpart of the device set-up that zw_open adds
+ * (src/capi.zig:59-79). */
+ZWG_API int zwg_init(int device);
+
+/* Release the calling thread's device context and its cached buffers. */
+ZWG_API int zwg_shutdown(void);
+
+/* Copy the last error message of the calling thread (NUL terminated, truncated to len).
+ * Returns the full message length. */
+ZWG_API size_t zwg_last_error(char* buf, size_t len);
+
+/* Number of CUDA devices visible (0 when none). */
+ZWG_API int zwg_device_count(void);
+
+/* ---- drop-in, host pointers, synchronous (parity path) ------------------------------ */
+
+/* ops.attentionEx (src/ops.zig:562): q[n_q][q_stride], k, v[n_kv][kv_stride],
+ * out[n_q][out_stride], all host f32. Fills out before returning. The reference's
+ * scratch argument is not needed: device staging is owned by the context. */
+ZWG_API int zwg_attention(const zwg_attn_shape* sh, const float* q, const float* k, const float* v,
+                  float* out);
+
+/* ops.attention (src/ops.zig:593): MHA with q, k, v, out all [rows][n_state]. */
+ZWG_API int zwg_attention_mha(const float* q, const float* k, const float* v, size_t n_q, size_t n_kv,
+                      size_t n_state, size_t n_head, int32_t causal, float* out);
+
+/* The same call over a batch of host items, pipelined (copies overlap compute). */
+ZWG_API int zwg_attention_batch_host(const zwg_attn_shape* sh, const zwg_batch* b, const float* q,
+                             const float* k, const float* v, float* out);
+
+/* ---- device pointers, stream ordered (throughput path) ------------------------------- */
+
+/* Workspace bytes zwg_attention_dev needs for this shape and batch (ops.attentionScratchEx,
+ * src/ops.zig:545-556, sizes the reference's scratch the same way: per shape). */
+ZWG_API size_t zwg_attention_workspace(const zwg_attn_shape* sh, const zwg_batch* b);
+
+/* ops.attentionEx over a batch, f32 operands and accumulation, device pointers. Decode-like
+ * shapes (n_q * n_head / n_head_kv <= 8 rows per kv head) run the split-K kernel;
+ * others run the tiled kernel. `stream` is a cudaStream_t; NULL means the legacy default
+ * stream, as in the CUDA runtime. The device entry points below take `stream` the same way. */
+ZWG_API int zwg_attention_dev(const zwg_attn_shape* sh, const zwg_batch* b, const float* q,
+                      const float* k, const float* v, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Encoder self-attention on tcgen05 tensor cores (src/encoder.zig:167): bf16 q, k, v
+ * [n_batch][n_ctx][n_head*64], non-causal, d = 64, f32 softmax and accumulation,
+ * f32 out [n_batch][n_ctx][n_head*64]. Rows of 16-byte aligned buffers are required
+ * (TMA): q/k/v base addresses 16-byte aligned and n_head*64*2 bytes per row. */
+ZWG_API int zwg_enc_attn_bf16(size_t n_batch, size_t n_ctx, size_t n_head, const uint16_t* q,
+                      const uint16_t* k, const uint16_t* v, float* out, void* stream);
+
+/* f32 -> bf16 (round to nearest even) of n elements, device pointers; the producer step
+ * a projection epilogue would fuse. */
+ZWG_API int zwg_f32_to_bf16(const float* x, uint16_t* y, size_t n, void* stream);
+
+/* Qwen2 rotary embedding and cache append (src/llm.zig:182-190, 221-238): NeoX RoPE at
+ * positions n_past.. on q[n][n_head*d] (in place) and k[n][n_head_kv*d], then
+ * cache_kt[h][p][n_past+i] = k_rot[i][h*d+p] and cache_v[(n_past+i)][:] = v[i][:].
+ * cos/sin tables are [n_ctx][d/2] f32 (computed in f64 on the host, src/llm.zig:128-137).
+ * Batched: item b's q, k, v, cache_kt and cache_v start at b * the given strides. */
+ZWG_API int zwg_rope_kt_append(size_t n_batch, size_t n, size_t n_past, size_t n_head, size_t n_head_kv,
+                       size_t d, size_t n_ctx, float* q, const float* k, const float* v,
+                       float* cache_kt, float* cache_v, const float* cos_tab,
+                       const float* sin_tab, size_t q_bstride, size_t kv_bstride,
+                       size_t cache_bstride, void* stream);
+
+/* Synchronize the device and report the context's device-side error word, if set. */
+ZWG_API int zwg_sync(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,272 @@
+"""Parity of the CUDA attention path against the CPU oracle (oracle/attention.py, a
+restatement of src/ops.zig:464-605), called through the C ABI.
+
+Tolerances: the f32 kernels (tiled flash kernel, split-K decode kernel) are held to the
+reference's own unit-test tolerance, abs 1e-4 (src/ops.zig:700); the bf16 tensor-core
+encoder kernel to the north-star tolerance, max-abs 2e-3 with rel 1e-3, against a float64
+reference on the same bf16-rounded inputs.
+"""
+import numpy as np
+import pytest
+
+from oracle import attention as A
+from tests.conftest import has_gpu
+
+pytestmark = pytest.mark.gpu
+
+F32_ATOL = 1e-4
+BF16_ATOL, BF16_RTOL = 2e-3, 1e-3
+
+
+def rnd(rng, n, lo=-0.5, hi=0.5):
+    return (rng.random(n, dtype=np.float32) * (hi - lo) + lo).astype(np.float32)
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not has_gpu():
+        pytest.fail("needs a CUDA device")
+    from zwhisper_b200 import ops as o
+    return o
+
+
+def run_both(ops, sh_o, q, k, v):
+    sh = ops.AttnShape(**sh_o.__dict__)
+    got = ops.attention_ex(q, k, v, sh)
+    want = A.attention_ex(q, k, v, sh_o)
+    return got, want
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_reference_unit_case(ops, causal):
+    """The reference's own test shape (src/ops.zig:655-704): n_q=70, n_kv=90, 2 heads of
+    d=32, values uniform in [-0.5, 0.5); checked against the naive loop and the oracle."""
+    rng = np.random.default_rng(9)
+    n_q, n_kv, H, d = 70, 90, 2, 32
+    ns = H * d
+    q, k, v = rnd(rng, n_q * ns), rnd(rng, n_kv * ns), rnd(rng, n_kv * ns)
+    got = ops.attention(q, k, v, n_q, n_kv, ns, H, causal)
+    naive = A.naive_attention(q, k, v, n_q, n_kv, ns, H, causal)
+    np.testing.assert_allclose(got, naive, atol=F32_ATOL, rtol=0)
+    want = A.attention(q, k, v, n_q, n_kv, ns, H, causal)
+    np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("n_q,n_kv", [(1, 1), (1, 17), (3, 65), (1, 1499), (5, 5), (64, 64), (65, 130), (200, 333)])
+@pytest.mark.parametrize("d", [32, 64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_odd_shapes_mha(ops, n_q, n_kv, d, causal):
+    rng = np.random.default_rng(n_q * 1000 + n_kv + d)
+    H = 3
+    ns = H * d
+    q, k, v = rnd(rng, n_q * ns), rnd(rng, n_kv * ns), rnd(rng, n_kv * ns)
+    got, want = run_both(ops, A.mha_shape(n_q, n_kv, ns, H, causal), q, k, v)
+    np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("H,Hkv,d", [(14, 2, 64), (12, 2, 128), (4, 4, 64), (8, 1, 32)])
+@pytest.mark.parametrize("n_q", [1, 2, 9, 256])
+def test_gqa_transposed_keys(ops, H, Hkv, d, n_q):
+    """Qwen2 attention call (src/llm.zig:191-202): keys kept transposed in a cache of
+    n_ctx columns, GQA, causal; columns past n_kv hold finite junk as the contract allows."""
+    rng = np.random.default_rng(H * 100 + d + n_q)
+    n_ctx = 640
+    n_kv = 300 + n_q
+    kvw = Hkv * d
+    q = rnd(rng, n_q * H * d)
+    kt = rnd(rng, Hkv * d * n_ctx)
+    v = rnd(rng, n_kv * kvw)
+    sh = A.AttnShape(n_q, n_kv, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
+    got, want = run_both(ops, sh, q, kt, v)
+    np.testing.assert_allclose(got, want, atol=F32_ATOL, rtol=0)
+
+
+def test_strided_rows_and_untouched_columns(ops):
+    """Rows wider than the heads: only head columns of `out` are written."""
+    rng = np.random.default_rng(3)
+    n_q, n_kv, H, d = 7, 50, 2, 64
+    sh = A.AttnShape(n_q, n_kv, H, H, d, H * d + 16, H * d + 32, H * d + 8, False)
+    q = rnd(rng, n_q * sh.q_stride)
+    k = rnd(rng, n_kv * sh.kv_stride)
+    v = rnd(rng, n_kv * sh.kv_stride)
+    out = np.full(n_q * sh.out_stride, 7.0, np.float32)
+    ops.attention_ex(q, k, v, ops.AttnShape(**sh.__dict__), out=out)
+    want = A.attention_ex(q, k, v, sh, out=np.full(n_q * sh.out_stride, 7.0, np.float32))
+    np.testing.assert_allclose(out, want, atol=F32_ATOL, rtol=0)
+
+
+def test_empty(ops):
+    sh = ops.mha_shape(3, 0, 128, 2, False)
+    out = ops.attention_ex(np.ones(3 * 128, np.float32), np.zeros(0, np.float32), np.zeros(0, np.float32), sh)
+    assert np.all(out == 0)
+    sh = ops.mha_shape(0, 5, 128, 2, False)
+    ops.attention_ex(np.zeros(0, np.float32), np.ones(5 * 128, np.float32), np.ones(5 * 128, np.float32), sh)
+
+
+def test_errors(ops):
+    from zwhisper_b200._lib import ZwgError
+    with pytest.raises(ValueError):
+        ops.attention_ex(np.zeros(10 * 64, np.float32), np.zeros(5 * 64, np.float32), np.zeros(5 * 64, np.float32),
+                         ops.mha_shape(10, 5, 64, 1, True))
+    with pytest.raises(ValueError):
+        ops.AttnShape(1, 1, 3, 2, 64, 192, 128, 192, False)
+        ops.attention_ex(np.zeros(192, np.float32), np.zeros(128, np.float32), np.zeros(128, np.float32),
+                         ops.AttnShape(1, 1, 3, 2, 64, 192, 128, 192, False))
+    with pytest.raises(ZwgError):
+        sh = ops.AttnShape(1, 4, 2, 2, 30, 60, 60, 60, False)  # d not a multiple of 4
+        ops.attention_ex(np.zeros(60, np.float32), np.zeros(240, np.float32), np.zeros(240, np.float32), sh)
+
+
+# ---- device-resident batched paths at the BASELINE configs ---------------------------------
+
+def test_decoder_step_config1(ops, gpu):
+    """Whisper base.en decoder attention step (config 1): 32 windows, 8 heads of 64, self
+    attention over a cache filled to 224 of 448 (causal, n_q=1) and cross attention over
+    1500 precomputed keys; K/V N(0,1)."""
+    import torch
+    rng = np.random.default_rng(11)
+    B, H, d, n_text, n_audio = 32, 8, 64, 448, 1500
+    ns = H * d
+    q = rng.standard_normal((B, 1, ns), dtype=np.float32) * 0.5
+    ck = rng.standard_normal((B, n_text, ns), dtype=np.float32)
+    cv = rng.standard_normal((B, n_text, ns), dtype=np.float32)
+    xk = rng.standard_normal((B, n_audio, ns), dtype=np.float32)
+    xv = rng.standard_normal((B, n_audio, ns), dtype=np.float32)
+    tq = torch.from_numpy(q).to(gpu)
+    out = torch.empty_like(tq)
+    # self: n_kv = 224 rows of a 448-row cache (batch stride = whole cache)
+    sh = ops.mha_shape(1, 224, ns, H, True)
+    tck, tcv = torch.from_numpy(ck).to(gpu), torch.from_numpy(cv).to(gpu)
+    ops.attention_dev(tq, tck, tcv, sh, out, n_batch=B, batch_strides=(ns, n_text * ns, n_text * ns, ns))
+    got = out.cpu().numpy()
+    for b in range(0, B, 7):
+        want = A.attention_ex(q[b].reshape(-1), ck[b, :224].reshape(-1), cv[b, :224].reshape(-1),
+                              A.mha_shape(1, 224, ns, H, True))
+        np.testing.assert_allclose(got[b].reshape(-1), want, atol=F32_ATOL, rtol=0)
+    # cross
+    sh = ops.mha_shape(1, n_audio, ns, H, False)
+    txk, txv = torch.from_numpy(xk).to(gpu), torch.from_numpy(xv).to(gpu)
+    ops.attention_dev(tq, txk, txv, sh, out, n_batch=B)
+    got = out.cpu().numpy()
+    for b in range(0, B, 5):
+        want = A.attention_ex(q[b].reshape(-1), xk[b].reshape(-1), xv[b].reshape(-1), A.mha_shape(1, n_audio, ns, H, False))
+        np.testing.assert_allclose(got[b].reshape(-1), want, atol=F32_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("H,Hkv,d,n_kv", [(14, 2, 64, 2001), (14, 2, 64, 2256), (12, 2, 128, 2512), (12, 2, 128, 2001)])
+def test_qwen_decode_batched(ops, gpu, H, Hkv, d, n_kv):
+    """Qwen2 decode attention (configs 3 and 4): one query token per sequence over the
+    transposed key cache of n_ctx = 2560 columns."""
+    import torch
+    rng = np.random.default_rng(n_kv + d)
+    B, n_ctx = 6, 2560
+    kvw = Hkv * d
+    q = rng.standard_normal((B, H * d), dtype=np.float32)
+    kt = rng.standard_normal((B, Hkv, d, n_ctx), dtype=np.float32)
+    v = rng.standard_normal((B, n_ctx, kvw), dtype=np.float32)
+    sh = ops.AttnShape(1, n_kv, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
+    tq, tk, tv = (torch.from_numpy(x).to(gpu) for x in (q, kt, v))
+    out = torch.empty_like(tq)
+    ops.attention_dev(tq, tk, tv, sh, out, n_batch=B)
+    got = out.cpu().numpy()
+    sho = A.AttnShape(1, n_kv, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
+    for b in range(B):
+        want = A.attention_ex(q[b], kt[b].reshape(-1), v[b].reshape(-1), sho)
+        np.testing.assert_allclose(got[b], want, atol=F32_ATOL, rtol=0)
+
+
+def test_qwen_prefill_chunk(ops, gpu):
+    """A 256-token prefill chunk at position 1744 (the last chunk of a 2000-token prompt,
+    src/llm.zig:257-266) over the transposed cache: causal GQA, n_q = 256."""
+    import torch
+    rng = np.random.default_rng(5)
+    B, H, Hkv, d, n_ctx = 2, 14, 2, 64, 2048
+    n_q, n_kv = 256, 2000
+    kvw = Hkv * d
+    q = rng.standard_normal((B, n_q, H * d), dtype=np.float32)
+    kt = rng.standard_normal((B, Hkv, d, n_ctx), dtype=np.float32)
+    v = rng.standard_normal((B, n_ctx, kvw), dtype=np.float32)
+    sh = ops.AttnShape(n_q, n_kv, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
+    tq, tk, tv = (torch.from_numpy(x).to(gpu) for x in (q, kt, v))
+    out = torch.empty_like(tq)
+    ops.attention_dev(tq, tk, tv, sh, out, n_batch=B)
+    got = out.cpu().numpy()
+    sho = A.AttnShape(n_q, n_kv, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
+    want = A.attention_ex(q[1].reshape(-1), kt[1].reshape(-1), v[1].reshape(-1), sho)
+    np.testing.assert_allclose(got[1].reshape(-1), want, atol=F32_ATOL, rtol=0)
+
+
+def test_rope_kt_append_bit_exact(ops, gpu):
+    """RoPE + transposed-key scatter + value append equal the reference's f32 operations
+    bit for bit (src/llm.zig:182-190, 221-238)."""
+    import torch
+    from oracle import qwen
+    rng = np.random.default_rng(8)
+    B, n, n_past, H, Hkv, d, n_ctx = 3, 5, 17, 14, 2, 64, 64
+    kvw = Hkv * d
+    cos_t, sin_t = ops.rope_tables(n_ctx, d, 1e6)
+    q = rng.standard_normal((B, n, H * d), dtype=np.float32)
+    k = rng.standard_normal((B, n, kvw), dtype=np.float32)
+    v = rng.standard_normal((B, n, kvw), dtype=np.float32)
+    kt0 = np.zeros((B, Hkv, d, n_ctx), np.float32)
+    vc0 = np.zeros((B, n_ctx, kvw), np.float32)
+    tq, tk, tv, tkt, tvc = (torch.from_numpy(x.copy()).to(gpu) for x in (q, k, v, kt0, vc0))
+    tcos, tsin = torch.from_numpy(cos_t).to(gpu), torch.from_numpy(sin_t).to(gpu)
+    ops.rope_kt_append(tq, tk, tv, tkt, tvc, tcos, tsin, n_past, H, Hkv, d, n_ctx, n_batch=B)
+    for b in range(B):
+        wq, wkt, wvc = qwen.rope_and_append(q[b], k[b], v[b], kt0[b].copy(), vc0[b].copy(), cos_t, sin_t, n_past, H, Hkv, d)
+        assert np.array_equal(tq[b].cpu().numpy(), wq)
+        assert np.array_equal(tkt[b].cpu().numpy(), wkt)
+        assert np.array_equal(tvc[b].cpu().numpy(), wvc)
+
+
+# ---- encoder tensor-core kernel --------------------------------------------------------------
+
+def bf16_round(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+@pytest.mark.parametrize("B,n_ctx,H", [(1, 128, 1), (2, 1500, 6), (1, 300, 2), (3, 1500, 12)])
+def test_encoder_tc_bf16(ops, gpu, B, n_ctx, H):
+    """Encoder self-attention (configs 0 and 2) on tcgen05: bf16 operands, f32 softmax and
+    accumulation. Checked against float64 attention of the same bf16 inputs."""
+    import torch
+    rng = np.random.default_rng(B * 7 + n_ctx + H)
+    ns = H * 64
+    shape = (B, n_ctx, ns)
+    q = rng.standard_normal(shape, dtype=np.float32)
+    k = rng.standard_normal(shape, dtype=np.float32)
+    v = rng.standard_normal(shape, dtype=np.float32)
+    tq, tk, tv = (torch.from_numpy(x).to(gpu).to(torch.bfloat16) for x in (q, k, v))
+    out = ops.enc_attn_bf16(tq, tk, tv, H)
+    ops.sync()
+    got = out.cpu().numpy()
+    qb, kb, vb = (t.float().cpu().numpy() for t in (tq, tk, tv))
+
+    def heads(x):
+        return x.reshape(B, n_ctx, H, 64).transpose(0, 2, 1, 3)
+
+    want = A.attention_batched(heads(qb), heads(kb), heads(vb), causal=False)
+    want = want.transpose(0, 2, 1, 3).reshape(shape)
+    np.testing.assert_allclose(got, want, atol=BF16_ATOL, rtol=BF16_RTOL)
+
+
+def test_encoder_tc_vs_f32_oracle(ops, gpu):
+    """The bf16 kernel against the f32 oracle on f32 inputs of encoder magnitude (LN output
+    times N(0, 0.02^2) weights scaled to unit variance): the error budget of bf16 rounding
+    of Q, K, V stays inside the north-star tolerance."""
+    import torch
+    rng = np.random.default_rng(21)
+    n_ctx, H = 1500, 6
+    ns = H * 64
+    q = rng.standard_normal(n_ctx * ns, dtype=np.float32)
+    k = rng.standard_normal(n_ctx * ns, dtype=np.float32)
+    v = rng.standard_normal(n_ctx * ns, dtype=np.float32)
+    tq, tk, tv = (torch.from_numpy(x).to(gpu).view(1, n_ctx, ns) for x in (q, k, v))
+    bq, bk, bv = (ops.f32_to_bf16(t.contiguous()) for t in (tq, tk, tv))
+    got = ops.enc_attn_bf16(bq, bk, bv, H).cpu().numpy().reshape(-1)
+    want = A.attention(q, k, v, n_ctx, n_ctx, ns, H, False)
+    err = np.abs(got - want)
+    np.testing.assert_allclose(got, want, atol=BF16_ATOL, rtol=BF16_RTOL)
+    assert err.max() < BF16_ATOL

@@ -1,0 +1,110 @@
+"""ctypes binding of libzwgpu.so (include/zwgpu.h).
+
+The library is required: importing the bindings raises if it is missing, so no caller
+can silently run without the CUDA path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzwgpu.so")
+
+ZWG_OK = 0
+ZWG_ERROR = 2
+ZWG_TIMEOUT = 4
+
+c_size = ctypes.c_size_t
+c_ptr = ctypes.c_void_p
+
+
+class AttnShapeC(ctypes.Structure):
+    """zwg_attn_shape (include/zwgpu.h), the C mirror of AttnShape (src/ops.zig:477-492)."""
+
+    _fields_ = [
+        ("n_q", c_size), ("n_kv", c_size), ("n_head", c_size), ("n_head_kv", c_size), ("d", c_size),
+        ("q_stride", c_size), ("kv_stride", c_size), ("out_stride", c_size), ("causal", ctypes.c_int32),
+        ("kt_stride", c_size),
+    ]
+
+
+class BatchC(ctypes.Structure):
+    """zwg_batch (include/zwgpu.h)."""
+
+    _fields_ = [
+        ("n_batch", c_size), ("q_batch_stride", c_size), ("k_batch_stride", c_size),
+        ("v_batch_stride", c_size), ("out_batch_stride", c_size),
+    ]
+
+
+# name -> (restype, argtypes); every symbol include/zwgpu.h declares
+SIGNATURES = {
+    "zwg_version": (ctypes.c_int, []),
+    "zwg_init": (ctypes.c_int, [ctypes.c_int]),
+    "zwg_shutdown": (ctypes.c_int, []),
+    "zwg_last_error": (c_size, [ctypes.c_char_p, c_size]),
+    "zwg_device_count": (ctypes.c_int, []),
+    "zwg_attention": (ctypes.c_int, [ctypes.POINTER(AttnShapeC), c_ptr, c_ptr, c_ptr, c_ptr]),
+    "zwg_attention_mha": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_size, c_size, c_size, c_size, ctypes.c_int32, c_ptr]),
+    "zwg_attention_batch_host": (ctypes.c_int, [ctypes.POINTER(AttnShapeC), ctypes.POINTER(BatchC), c_ptr, c_ptr,
+                                                c_ptr, c_ptr]),
+    "zwg_attention_workspace": (c_size, [ctypes.POINTER(AttnShapeC), ctypes.POINTER(BatchC)]),
+    "zwg_attention_dev": (ctypes.c_int, [ctypes.POINTER(AttnShapeC), ctypes.POINTER(BatchC), c_ptr, c_ptr, c_ptr,
+                                         c_ptr, c_ptr, c_size, c_ptr]),
+    "zwg_enc_attn_bf16": (ctypes.c_int, [c_size, c_size, c_size, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "zwg_f32_to_bf16": (ctypes.c_int, [c_ptr, c_ptr, c_size, c_ptr]),
+    "zwg_rope_kt_append": (ctypes.c_int, [c_size, c_size, c_size, c_size, c_size, c_size, c_size, c_ptr, c_ptr,
+                                          c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_size, c_size, c_ptr]),
+    "zwg_sync": (ctypes.c_int, []),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class ZwgError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"zwgpu error {code}: {msg}")
+        self.code = code
+
+
+def load():
+    """Load libzwgpu.so; raise if it is missing (no fallback path exists)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m zwhisper_b200.build`")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = ctypes.create_string_buffer(512)
+    lib.zwg_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != ZWG_OK:
+        raise ZwgError(rc, last_error())
+
+
+_bound = threading.local()
+
+
+def ensure_init(device: int) -> None:
+    """Bind the calling thread to `device` (zwg_init), once per thread and device."""
+    lib = load()
+    if getattr(_bound, "device", None) != device:
+        check(lib.zwg_init(device))
+        _bound.device = device

@@ -1,0 +1,380 @@
+// C-ABI layer of libzwgpu (declared in include/zwgpu.h): per-device contexts, argument
+// checks mirroring the reference's asserts (src/ops.zig:564-568), host-pointer drop-in
+// entry points and device-pointer batched entry points.
+#include "../../include/zwgpu.h"
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+namespace {
+
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    bool ensure(size_t bytes) {
+        if (bytes <= cap) return true;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+        size_t want = std::max(bytes, (size_t)256);
+        if (cudaMalloc(&ptr, want) != cudaSuccess) return false;
+        cap = want;
+        return true;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+};
+
+struct Ctx {
+    int device = -1;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;  // second stream for pipelined host batches
+    int* err = nullptr;           // device error word
+    DevBuf q[2], k[2], v[2], out[2], ws[2];
+};
+
+std::mutex g_mu;
+Ctx* g_ctx[64] = {};
+thread_local Ctx* t_cur = nullptr;
+thread_local std::string t_err;
+
+int fail(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    return ZWG_ERROR;
+}
+
+int cuda_fail(const char* what, cudaError_t e) {
+    return fail("%s: %s", what, cudaGetErrorString(e));
+}
+
+Ctx* cur() {
+    if (!t_cur) fail("zwg_init was not called on this thread");
+    return t_cur;
+}
+
+// Elements spanned by `rows` rows of `width` elements at `stride`.
+size_t span(size_t rows, size_t stride, size_t width) { return rows ? (rows - 1) * stride + width : 0; }
+
+int check_shape(const zwg_attn_shape* sh) {
+    if (!sh) return fail("null shape");
+    if (sh->n_head == 0 || sh->n_head_kv == 0 || sh->n_head % sh->n_head_kv)
+        return fail("n_head (%zu) must be a positive multiple of n_head_kv (%zu)", sh->n_head, sh->n_head_kv);
+    if (sh->d == 0 || sh->d % 4 || sh->d > 256) return fail("d = %zu: need a multiple of 4 up to 256", sh->d);
+    if (sh->q_stride < sh->n_head * sh->d || sh->out_stride < sh->n_head * sh->d)
+        return fail("q/out stride smaller than n_head * d");
+    if (sh->kv_stride < sh->n_head_kv * sh->d) return fail("kv stride smaller than n_head_kv * d");
+    if (sh->causal && sh->n_kv < sh->n_q) return fail("causal attention needs n_kv >= n_q (%zu < %zu)", sh->n_kv, sh->n_q);
+    if (sh->kt_stride && sh->kt_stride < sh->n_kv) return fail("kt_stride %zu < n_kv %zu", sh->kt_stride, sh->n_kv);
+    if (sh->kt_stride % 4) return fail("kt_stride must be a multiple of 4");
+    if (sh->n_kv > (1u << 30) || sh->n_q > (1u << 30)) return fail("sequence too long");
+    return ZWG_OK;
+}
+
+struct Extents {
+    size_t q, k, v, out;
+};
+
+Extents extents(const zwg_attn_shape* sh) {
+    Extents e;
+    e.q = span(sh->n_q, sh->q_stride, sh->n_head * sh->d);
+    e.k = sh->kt_stride ? sh->n_head_kv * sh->d * sh->kt_stride : span(sh->n_kv, sh->kv_stride, sh->n_head_kv * sh->d);
+    e.v = span(sh->n_kv, sh->kv_stride, sh->n_head_kv * sh->d);
+    e.out = span(sh->n_q, sh->out_stride, sh->n_head * sh->d);
+    return e;
+}
+
+bool use_decode(const zwg_attn_shape* sh) {
+    const size_t rows = sh->n_q * (sh->n_head / sh->n_head_kv);
+    return zwg::decode_supported(sh->d, rows, sh->kt_stride);
+}
+
+struct Plan {
+    bool decode;
+    int n_splits, chunk;
+    size_t ws_bytes;
+};
+
+Plan plan_for(const zwg_attn_shape* sh, size_t n_batch, int sm_count) {
+    Plan pl{};
+    pl.decode = use_decode(sh);
+    if (pl.decode) {
+        zwg::decode_plan(n_batch, sh->n_head_kv, sh->n_kv, sh->kt_stride != 0, sm_count, &pl.n_splits, &pl.chunk);
+        const size_t rows = sh->n_q * (sh->n_head / sh->n_head_kv);
+        pl.ws_bytes = zwg::decode_workspace_floats(n_batch, sh->n_head_kv, rows, pl.n_splits, sh->d) * sizeof(float);
+    }
+    return pl;
+}
+
+int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
+            const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st) {
+    const size_t nb = b ? b->n_batch : 1;
+    if (nb == 0 || sh->n_q == 0) return ZWG_OK;
+    const Plan pl = plan_for(sh, nb, c->sm_count);
+    int rc;
+    if (pl.decode) {
+        if (ws_bytes < pl.ws_bytes) return fail("workspace too small: %zu < %zu bytes", ws_bytes, pl.ws_bytes);
+        if (((uintptr_t)k | (uintptr_t)v | (uintptr_t)q) & 15)
+            return fail("decode kernel needs 16-byte aligned q, k, v");
+        if ((sh->kv_stride | sh->q_stride) % 4) return fail("decode kernel needs strides that are multiples of 4");
+        zwg::DecodeParams p{};
+        p.q = q; p.k = k; p.v = v; p.out = out; p.ws = (float*)ws;
+        p.n_q = sh->n_q; p.n_kv = sh->n_kv; p.n_head = sh->n_head; p.n_head_kv = sh->n_head_kv; p.d = sh->d;
+        p.q_stride = sh->q_stride; p.kv_stride = sh->kv_stride; p.out_stride = sh->out_stride;
+        p.kt_stride = sh->kt_stride; p.causal = sh->causal ? 1 : 0;
+        p.n_splits = pl.n_splits; p.chunk = pl.chunk;
+        if (b) { p.q_bs = b->q_batch_stride; p.k_bs = b->k_batch_stride; p.v_bs = b->v_batch_stride; p.out_bs = b->out_batch_stride; }
+        if (p.k_bs % 4 || p.v_bs % 4 || p.q_bs % 4) return fail("decode kernel needs batch strides that are multiples of 4");
+        rc = zwg::decode_f32_launch(p, nb, st);
+    } else {
+        zwg::FlashParams p{};
+        p.q = q; p.k = k; p.v = v; p.out = out;
+        p.n_q = sh->n_q; p.n_kv = sh->n_kv; p.n_head = sh->n_head; p.n_head_kv = sh->n_head_kv; p.d = sh->d;
+        p.q_stride = sh->q_stride; p.kv_stride = sh->kv_stride; p.out_stride = sh->out_stride;
+        p.kt_stride = sh->kt_stride; p.causal = sh->causal ? 1 : 0;
+        if (b) { p.q_bs = b->q_batch_stride; p.k_bs = b->k_batch_stride; p.v_bs = b->v_batch_stride; p.out_bs = b->out_batch_stride; }
+        if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 3) return fail("f32 buffers must be 4-byte aligned");
+        rc = zwg::flash_f32_launch(p, nb, st);
+    }
+    if (rc) return cuda_fail("kernel launch", cudaGetLastError());
+    return ZWG_OK;
+}
+
+int sync_and_check(Ctx* c, cudaStream_t st) {
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail("stream synchronize", e);
+    int h = 0;
+    e = cudaMemcpy(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail("error word read", e);
+    if (h) {
+        cudaMemset(c->err, 0, sizeof(int));
+        if (h == zwg::kErrTimeout) {
+            fail("a device-side wait timed out");
+            return ZWG_TIMEOUT;
+        }
+        return fail("device error code %d", h);
+    }
+    return ZWG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int zwg_version(void) { return 1; }
+
+int zwg_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+int zwg_init(int device) {
+    int n = zwg_device_count();
+    if (device < 0 || device >= n || device >= 64) return fail("device %d not available (%d visible)", device, n);
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail("cudaSetDevice", e);
+    if (!g_ctx[device]) {
+        Ctx* c = new Ctx();
+        c->device = device;
+        cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+        if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaMalloc(&c->err, sizeof(int))) != cudaSuccess ||
+            (e = cudaMemset(c->err, 0, sizeof(int))) != cudaSuccess) {
+            delete c;
+            return cuda_fail("context set-up", e);
+        }
+        g_ctx[device] = c;
+    }
+    t_cur = g_ctx[device];
+    return ZWG_OK;
+}
+
+int zwg_shutdown(void) {
+    Ctx* c = t_cur;
+    if (!c) return ZWG_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    cudaStreamSynchronize(c->side);
+    for (int i = 0; i < 2; i++) {
+        c->q[i].release(); c->k[i].release(); c->v[i].release(); c->out[i].release(); c->ws[i].release();
+    }
+    cudaFree(c->err);
+    cudaStreamDestroy(c->stream);
+    cudaStreamDestroy(c->side);
+    g_ctx[c->device] = nullptr;
+    delete c;
+    t_cur = nullptr;
+    return ZWG_OK;
+}
+
+size_t zwg_last_error(char* buf, size_t len) {
+    if (buf && len) {
+        size_t n = std::min(len - 1, t_err.size());
+        memcpy(buf, t_err.data(), n);
+        buf[n] = 0;
+    }
+    return t_err.size();
+}
+
+int zwg_sync(void) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail("device synchronize", e);
+    return sync_and_check(c, c->stream);
+}
+
+size_t zwg_attention_workspace(const zwg_attn_shape* sh, const zwg_batch* b) {
+    if (check_shape(sh) != ZWG_OK) return 0;
+    int sms = 148;
+    if (t_cur) sms = t_cur->sm_count;
+    return plan_for(sh, b ? b->n_batch : 1, sms).ws_bytes;
+}
+
+int zwg_attention_dev(const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
+                      const float* v, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    int rc = check_shape(sh);
+    if (rc) return rc;
+    if (sh->n_q && (!q || !out)) return fail("null q/out");
+    if (sh->n_kv && (!k || !v)) return fail("null k/v");
+    cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
+    return run_dev(c, sh, b, q, k, v, out, workspace, workspace_bytes, st);
+}
+
+// Host-pointer path: stage inputs, run, copy the written head columns back.
+static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
+                     const float* v, float* out) {
+    const Extents ex = extents(sh);
+    const size_t nb = b ? b->n_batch : 1;
+    if (nb == 0 || sh->n_q == 0) return ZWG_OK;
+    const size_t qbs = b ? b->q_batch_stride : 0, kbs = b ? b->k_batch_stride : 0;
+    const size_t vbs = b ? b->v_batch_stride : 0, obs = b ? b->out_batch_stride : 0;
+    // items per chunk: bounded device staging, two chunks in flight on two streams
+    const size_t item_bytes = (ex.q + ex.k + ex.v + ex.out) * sizeof(float);
+    size_t per = std::max<size_t>(1, (size_t)(512u << 20) / std::max<size_t>(item_bytes, 1));
+    per = std::min(per, nb);
+    if (nb > 1 && per == nb) per = (nb + 1) / 2;
+    const zwg_attn_shape& s = *sh;
+    cudaStream_t streams[2] = {c->stream, c->side};
+    int slot = 0;
+    for (size_t i0 = 0; i0 < nb; i0 += per, slot ^= 1) {
+        const size_t n = std::min(per, nb - i0);
+        cudaStream_t st = streams[slot];
+        // dense per-item layout on the device
+        const size_t dq = ex.q, dk = ex.k, dv = ex.v, dout = ex.out;
+        zwg_batch db{n, dq, dk, dv, dout};
+        Plan pl = plan_for(sh, n, c->sm_count);
+        if (!c->q[slot].ensure(n * dq * 4 + 16) || !c->k[slot].ensure(n * dk * 4 + 16) ||
+            !c->v[slot].ensure(n * dv * 4 + 16) || !c->out[slot].ensure(n * dout * 4 + 16) ||
+            !c->ws[slot].ensure(pl.ws_bytes + 16))
+            return fail("device staging allocation failed");
+        cudaError_t e = cudaSuccess;
+        for (size_t j = 0; j < n && e == cudaSuccess; j++) {
+            const size_t it = i0 + j;
+            if (dq) e = cudaMemcpyAsync((float*)c->q[slot].ptr + j * dq, q + it * qbs, dq * 4, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess && dk) e = cudaMemcpyAsync((float*)c->k[slot].ptr + j * dk, k + it * kbs, dk * 4, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess && dv) e = cudaMemcpyAsync((float*)c->v[slot].ptr + j * dv, v + it * vbs, dv * 4, cudaMemcpyHostToDevice, st);
+        }
+        if (e != cudaSuccess) return cuda_fail("host to device copy", e);
+        int rc = run_dev(c, &s, &db, (float*)c->q[slot].ptr, (float*)c->k[slot].ptr, (float*)c->v[slot].ptr,
+                         (float*)c->out[slot].ptr, c->ws[slot].ptr, c->ws[slot].cap, st);
+        if (rc) return rc;
+        // only the head columns of each output row are written, as in the reference
+        for (size_t j = 0; j < n && e == cudaSuccess; j++)
+            e = cudaMemcpy2DAsync(out + (i0 + j) * obs, s.out_stride * 4, (float*)c->out[slot].ptr + j * dout,
+                                  s.out_stride * 4, s.n_head * s.d * 4, s.n_q, cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) return cuda_fail("device to host copy", e);
+    }
+    int rc = sync_and_check(c, c->side);
+    int rc2 = sync_and_check(c, c->stream);
+    return rc ? rc : rc2;
+}
+
+int zwg_attention(const zwg_attn_shape* sh, const float* q, const float* k, const float* v, float* out) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    int rc = check_shape(sh);
+    if (rc) return rc;
+    if (sh->n_q && (!q || !out)) return fail("null q/out");
+    if (sh->n_kv && (!k || !v)) return fail("null k/v");
+    return host_call(c, sh, nullptr, q, k, v, out);
+}
+
+int zwg_attention_mha(const float* q, const float* k, const float* v, size_t n_q, size_t n_kv, size_t n_state,
+                      size_t n_head, int32_t causal, float* out) {
+    if (n_head == 0 || n_state % n_head) return fail("n_state %zu not divisible by n_head %zu", n_state, n_head);
+    zwg_attn_shape sh{n_q, n_kv, n_head, n_head, n_state / n_head, n_state, n_state, n_state, causal, 0};
+    return zwg_attention(&sh, q, k, v, out);
+}
+
+int zwg_attention_batch_host(const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
+                             const float* v, float* out) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    int rc = check_shape(sh);
+    if (rc) return rc;
+    if (!b) return fail("null batch");
+    return host_call(c, sh, b, q, k, v, out);
+}
+
+int zwg_f32_to_bf16(const float* x, uint16_t* y, size_t n, void* stream) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
+    if (zwg::f32_to_bf16_launch(x, y, n, st)) return fail("f32_to_bf16: unaligned buffers or launch failure");
+    return ZWG_OK;
+}
+
+int zwg_enc_attn_bf16(size_t n_batch, size_t n_ctx, size_t n_head, const uint16_t* q, const uint16_t* k,
+                      const uint16_t* v, float* out, void* stream) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    if (n_batch == 0 || n_ctx == 0) return ZWG_OK;
+    if (n_head == 0 || n_head > 64 || n_ctx > (1u << 20) || n_batch > 65535) return fail("enc_attn: bad sizes");
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15) return fail("enc_attn: q/k/v must be 16-byte aligned");
+    if (((uintptr_t)out) & 15) return fail("enc_attn: out must be 16-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
+    zwg::EncTcParams p{q, k, v, out, (int)n_batch, (int)n_ctx, (int)n_head, c->err};
+    if (zwg::enc_tc_launch(p, st)) return cuda_fail("enc_attn launch", cudaGetLastError());
+    return ZWG_OK;
+}
+
+int zwg_rope_kt_append(size_t n_batch, size_t n, size_t n_past, size_t n_head, size_t n_head_kv, size_t d,
+                       size_t n_ctx, float* q, const float* k, const float* v, float* cache_kt, float* cache_v,
+                       const float* cos_tab, const float* sin_tab, size_t q_bstride, size_t kv_bstride,
+                       size_t cache_bstride, void* stream) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    if (d == 0 || d % 2) return fail("rope: d must be even");
+    if (n_past + n > n_ctx) return fail("rope: context full (%zu + %zu > %zu)", n_past, n, n_ctx);
+    if (n_head_kv == 0 || n_head % n_head_kv) return fail("rope: bad head counts");
+    cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
+    zwg::RopeParams p{q, k, v, cache_kt, cache_v, cos_tab, sin_tab, n, n_past, n_head, n_head_kv, d, n_ctx,
+                      q_bstride, kv_bstride, cache_bstride};
+    if (zwg::rope_kt_append_launch(p, n_batch, st)) return cuda_fail("rope launch", cudaGetLastError());
+    return ZWG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+// Internal kernel parameter blocks and launchers shared by the C-ABI layer (api.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace zwg {
+
+// Batched attentionEx arguments (the AttnShape fields of src/ops.zig:477-492 plus
+// per-item strides). Strides are in elements.
+struct FlashParams {
+    const float* q;
+    const float* k;
+    const float* v;
+    float* out;
+    size_t n_q, n_kv, n_head, n_head_kv, d;
+    size_t q_stride, kv_stride, out_stride;
+    size_t kt_stride;  // 0: keys are rows
+    int causal;
+    size_t q_bs, k_bs, v_bs, out_bs;
+};
+
+struct DecodeParams {
+    const float* q;
+    const float* k;
+    const float* v;
+    float* out;
+    float* ws;  // split partials [n_batch][n_head_kv][n_splits][rows][d + 2]
+    size_t n_q, n_kv, n_head, n_head_kv, d;
+    size_t q_stride, kv_stride, out_stride;
+    size_t kt_stride;
+    int causal;
+    int n_splits;
+    int chunk;  // keys per split
+    size_t q_bs, k_bs, v_bs, out_bs;
+};
+
+int flash_f32_launch(const FlashParams& p, size_t n_batch, cudaStream_t st);
+
+bool decode_supported(size_t d, size_t rows, size_t kt_stride);
+void decode_plan(size_t n_batch, size_t n_head_kv, size_t n_kv, bool kt, int sm_count,
+                 int* n_splits, int* chunk);
+size_t decode_workspace_floats(size_t n_batch, size_t n_head_kv, size_t rows, int n_splits, size_t d);
+int decode_f32_launch(const DecodeParams& p, size_t n_batch, cudaStream_t st);
+
+// Encoder tensor-core attention (attn_tc.cu).
+struct EncTcParams {
+    const uint16_t* q;
+    const uint16_t* k;
+    const uint16_t* v;
+    float* out;
+    int n_batch, n_ctx, n_head;
+    int* err;  // device error word
+};
+int enc_tc_launch(const EncTcParams& p, cudaStream_t st);
+
+// Elementwise helpers (misc.cu).
+int f32_to_bf16_launch(const float* x, uint16_t* y, size_t n, cudaStream_t st);
+
+struct RopeParams {
+    float* q;
+    const float* k;
+    const float* v;
+    float* cache_kt;
+    float* cache_v;
+    const float* cos_tab;
+    const float* sin_tab;
+    size_t n, n_past, n_head, n_head_kv, d, n_ctx;
+    size_t q_bs, kv_bs, cache_bs;
+};
+int rope_kt_append_launch(const RopeParams& p, size_t n_batch, cudaStream_t st);
+
+}  // namespace zwg

@@ -1,0 +1,254 @@
+"""Host-side mirror of the reference's attention operator interface (src/ops.zig:464-605),
+running on the B200 through libzwgpu.
+
+Same names, argument meaning and error behaviour as the reference:
+  - `AttnShape` mirrors ops.AttnShape (src/ops.zig:477-492);
+  - `attention_ex(q, k, v, sh, scratch, out)` mirrors ops.attentionEx (src/ops.zig:562) on
+    host float32 arrays, synchronously (the pool argument has no counterpart);
+  - `attention(...)` mirrors ops.attention (src/ops.zig:593);
+  - `attention_scratch_ex / _kt / attention_scratch` mirror the sizers
+    (src/ops.zig:545-560) and return the device workspace in floats.
+Shape violations the reference asserts on (src/ops.zig:564-568) raise ValueError here.
+
+Device entry points (torch tensors on a CUDA device, stream ordered on the current torch
+stream): `attention_dev`, `enc_attn_bf16`, `rope_kt_append`, `f32_to_bf16`.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+
+Q_BLOCK = 64  # src/ops.zig:473, kept for callers that size buffers by it
+
+
+@dataclass
+class AttnShape:
+    """ops.AttnShape (src/ops.zig:477-492). Strides in floats. kt_stride=None: keys are rows."""
+
+    n_q: int
+    n_kv: int
+    n_head: int
+    n_head_kv: int
+    d: int
+    q_stride: int
+    kv_stride: int
+    out_stride: int
+    causal: bool
+    kt_stride: Optional[int] = None
+
+    def to_c(self) -> _lib.AttnShapeC:
+        return _lib.AttnShapeC(self.n_q, self.n_kv, self.n_head, self.n_head_kv, self.d, self.q_stride,
+                               self.kv_stride, self.out_stride, 1 if self.causal else 0, self.kt_stride or 0)
+
+    def extents(self):
+        """Elements of q, k, v, out that the call reads or writes."""
+        def span(rows, stride, width):
+            return (rows - 1) * stride + width if rows else 0
+        q = span(self.n_q, self.q_stride, self.n_head * self.d)
+        if self.kt_stride:
+            k = self.n_head_kv * self.d * self.kt_stride
+        else:
+            k = span(self.n_kv, self.kv_stride, self.n_head_kv * self.d)
+        v = span(self.n_kv, self.kv_stride, self.n_head_kv * self.d)
+        out = span(self.n_q, self.out_stride, self.n_head * self.d)
+        return q, k, v, out
+
+
+def mha_shape(n_q: int, n_kv: int, n_state: int, n_head: int, causal: bool) -> AttnShape:
+    """The shape ops.attention builds (src/ops.zig:593-605)."""
+    if n_head <= 0 or n_state % n_head:
+        raise ValueError(f"n_state {n_state} is not a multiple of n_head {n_head}")
+    return AttnShape(n_q, n_kv, n_head, n_head, n_state // n_head, n_state, n_state, n_state, causal)
+
+
+def _validate(sh: AttnShape) -> None:
+    if sh.n_head_kv <= 0 or sh.n_head % sh.n_head_kv:
+        raise ValueError("n_head must be a positive multiple of n_head_kv")
+    if sh.causal and sh.n_kv < sh.n_q:
+        raise ValueError("causal attention needs n_kv >= n_q")
+
+
+def _host_f32(a, n: int, name: str) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    if a.size < n:
+        raise ValueError(f"{name} holds {a.size} floats, the shape needs {n}")
+    return a
+
+
+def attention_ex(q, k, v, sh: AttnShape, scratch=None, out=None, device: int = 0) -> np.ndarray:
+    """ops.attentionEx (src/ops.zig:562) on the GPU: host float32 in, host float32 out."""
+    _validate(sh)
+    nq, nk, nv, no = sh.extents()
+    q = _host_f32(q, nq, "q")
+    k = _host_f32(k, nk, "k")
+    v = _host_f32(v, nv, "v")
+    if out is None:
+        out = np.zeros(max(no, 1), np.float32)
+    elif not (isinstance(out, np.ndarray) and out.dtype == np.float32 and out.flags.c_contiguous):
+        raise ValueError("out must be a contiguous float32 numpy array")
+    if out.size < no:
+        raise ValueError(f"out holds {out.size} floats, the shape needs {no}")
+    _lib.ensure_init(device)
+    lib = _lib.load()
+    c = sh.to_c()
+    _lib.check(lib.zwg_attention(ctypes.byref(c), q.ctypes.data, k.ctypes.data, v.ctypes.data, out.ctypes.data))
+    return out
+
+
+def attention(q, k, v, n_q: int, n_kv: int, n_state: int, n_head: int, causal: bool, scratch=None, out=None,
+              device: int = 0) -> np.ndarray:
+    """ops.attention (src/ops.zig:593)."""
+    return attention_ex(q, k, v, mha_shape(n_q, n_kv, n_state, n_head, causal), scratch, out, device)
+
+
+def attention_batch_host(q, k, v, sh: AttnShape, n_batch: int, out=None, device: int = 0) -> np.ndarray:
+    """attentionEx over n_batch independent host items laid out back to back, with copies
+    pipelined against compute (zwg_attention_batch_host)."""
+    _validate(sh)
+    nq, nk, nv, no = sh.extents()
+    q = _host_f32(q, nq * n_batch, "q")
+    k = _host_f32(k, nk * n_batch, "k")
+    v = _host_f32(v, nv * n_batch, "v")
+    if out is None:
+        out = np.zeros(max(no * n_batch, 1), np.float32)
+    _lib.ensure_init(device)
+    lib = _lib.load()
+    c = sh.to_c()
+    b = _lib.BatchC(n_batch, nq, nk, nv, no)
+    _lib.check(lib.zwg_attention_batch_host(ctypes.byref(c), ctypes.byref(b), q.ctypes.data, k.ctypes.data,
+                                            v.ctypes.data, out.ctypes.data))
+    return out
+
+
+# ---- scratch sizers (src/ops.zig:545-560): device workspace in floats ----------------------
+
+def attention_workspace_bytes(sh: AttnShape, n_batch: int = 1) -> int:
+    lib = _lib.load()
+    c = sh.to_c()
+    b = _lib.BatchC(n_batch, 0, 0, 0, 0)
+    return int(lib.zwg_attention_workspace(ctypes.byref(c), ctypes.byref(b)))
+
+
+def attention_scratch_ex(n_q, n_kv, n_head, n_head_kv, d) -> int:
+    sh = AttnShape(n_q, n_kv, n_head, n_head_kv, d, n_head * d, n_head_kv * d, n_head * d, False)
+    return attention_workspace_bytes(sh) // 4
+
+
+def attention_scratch_kt(n_q, kt_stride, n_head, n_head_kv=None, d=64) -> int:
+    n_head_kv = n_head_kv or n_head
+    sh = AttnShape(n_q, kt_stride, n_head, n_head_kv, d, n_head * d, n_head_kv * d, n_head * d, True, kt_stride)
+    return attention_workspace_bytes(sh) // 4
+
+
+def attention_scratch(n_q, n_kv, n_head, n_state) -> int:
+    return attention_scratch_ex(n_q, n_kv, n_head, n_head, n_state // n_head)
+
+
+# ---- device (torch) entry points -----------------------------------------------------------
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dev_ptr(t, dtype, name):
+    torch = _torch()
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t.data_ptr()
+
+
+def _stream_of(t):
+    torch = _torch()
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def attention_dev(q, k, v, sh: AttnShape, out, n_batch: int = 1, batch_strides=None, workspace=None):
+    """attentionEx on device f32 tensors over n_batch items (zwg_attention_dev).
+
+    batch_strides: (q, k, v, out) element strides between items; default = each tensor's
+    numel / n_batch. workspace: a CUDA uint8 tensor of at least attention_workspace_bytes."""
+    torch = _torch()
+    _validate(sh)
+    _lib.ensure_init(q.device.index or 0)
+    if batch_strides is None:
+        batch_strides = tuple(t.numel() // n_batch for t in (q, k, v, out))
+    c = sh.to_c()
+    b = _lib.BatchC(n_batch, *batch_strides)
+    need = attention_workspace_bytes(sh, n_batch)
+    if workspace is None and need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if workspace is not None else 0
+    ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    lib = _lib.load()
+    _lib.check(lib.zwg_attention_dev(ctypes.byref(c), ctypes.byref(b), _dev_ptr(q, torch.float32, "q"),
+                                     _dev_ptr(k, torch.float32, "k"), _dev_ptr(v, torch.float32, "v"),
+                                     _dev_ptr(out, torch.float32, "out"), ws_ptr, ws_len, _stream_of(q)))
+    return out
+
+
+def enc_attn_bf16(q, k, v, n_head: int, out=None):
+    """Encoder self-attention on tcgen05 tensor cores: bf16 q, k, v [B][n_ctx][n_head*64],
+    f32 out of the same shape (zwg_enc_attn_bf16)."""
+    torch = _torch()
+    if q.dim() != 3 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must share one [B][n_ctx][n_state] shape")
+    B, n_ctx, ns = q.shape
+    if ns != n_head * 64:
+        raise ValueError("head dim must be 64")
+    if out is None:
+        out = torch.empty(B, n_ctx, ns, dtype=torch.float32, device=q.device)
+    _lib.ensure_init(q.device.index or 0)
+    lib = _lib.load()
+    _lib.check(lib.zwg_enc_attn_bf16(B, n_ctx, n_head, _dev_ptr(q, torch.bfloat16, "q"),
+                                     _dev_ptr(k, torch.bfloat16, "k"), _dev_ptr(v, torch.bfloat16, "v"),
+                                     _dev_ptr(out, torch.float32, "out"), _stream_of(q)))
+    return out
+
+
+def f32_to_bf16(x, out=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    _lib.ensure_init(x.device.index or 0)
+    _lib.check(_lib.load().zwg_f32_to_bf16(_dev_ptr(x, torch.float32, "x"), _dev_ptr(out, torch.bfloat16, "out"),
+                                           x.numel(), _stream_of(x)))
+    return out
+
+
+def rope_tables(n_ctx: int, d: int, base: float):
+    """cos/sin [n_ctx][d/2] f32: inverse frequencies base^(-2i/d) and angles in f64, cast to
+    f32 (src/llm.zig:128-137)."""
+    half = d // 2
+    i = np.arange(half, dtype=np.float64)
+    inv = 1.0 / np.power(np.float64(base), 2.0 * i / np.float64(d))
+    ang = np.arange(n_ctx, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def rope_kt_append(q, k, v, cache_kt, cache_v, cos_t, sin_t, n_past: int, n_head: int, n_head_kv: int, d: int,
+                   n_ctx: int, n_batch: int = 1):
+    """Qwen2 RoPE on q (in place) and k, then append k into the transposed cache and v into
+    the value cache at positions n_past.. (src/llm.zig:182-190, 221-238)."""
+    torch = _torch()
+    n = q.numel() // n_batch // (n_head * d)
+    _lib.ensure_init(q.device.index or 0)
+    _lib.check(_lib.load().zwg_rope_kt_append(
+        n_batch, n, n_past, n_head, n_head_kv, d, n_ctx, _dev_ptr(q, torch.float32, "q"),
+        _dev_ptr(k, torch.float32, "k"), _dev_ptr(v, torch.float32, "v"), _dev_ptr(cache_kt, torch.float32, "cache_kt"),
+        _dev_ptr(cache_v, torch.float32, "cache_v"), _dev_ptr(cos_t, torch.float32, "cos"),
+        _dev_ptr(sin_t, torch.float32, "sin"), q.numel() // n_batch, k.numel() // n_batch,
+        cache_kt.numel() // n_batch, _stream_of(q)))
+
+
+def sync() -> None:
+    _lib.check(_lib.load().zwg_sync())
