@@ -1,0 +1,464 @@
+#!/usr/bin/env python
+"""Headline benchmark of the zwhisper attention engine on B200.
+
+Headline workload: Whisper small.en encoder self-attention,
+64 consecutive 30 s windows x 12 layers x 12 heads of d=64 over n_ctx=1500, bf16
+tensor-core compute with f32 softmax and accumulation. One step = all 12 layers' attention
+over the job's 64 windows (distinct Q/K/V per layer, inputs far larger than L2). Windows
+are sharded in contiguous blocks over the ranks (64 / N each, no collective on the data
+path): total work is fixed, so scaling is "strong".
+
+Reported (one JSON line from rank 0):
+  value      windows/s with inputs resident in HBM (CUDA events, max over ranks);
+  e2e        windows/s through the C-ABI drop-in (zwg_attention_batch_host, math mode
+             bf16) from pinned host f32 buffers, host<->device copies timed;
+  roofline   the tcgen05 encoder kernel: algorithmic FLOPs per launch / average launch
+             time, against the measured bf16 peak;
+  cpu_baseline  the C restatement of the reference attention (oracle/attn_ref.c) on the
+             host cores, rank 0 at N=1;
+  secondary  decode-attention workloads (configs 1, 3, 4) at N=1: tok/s and HBM roofline.
+
+`--impl reference` times the reference's CPU attention (the C restatement; the Zig source
+cannot be built here) on the same workload and prints the same line with "impl".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_CTX, N_STATE, N_HEAD, N_LAYER, WINDOWS = 1500, 768, 12, 12, 64
+METRIC = "whisper_small_en_encoder_attention_windows_per_s"
+UNIT = "windows/s"
+FLOP_PER_WINDOW_LAYER = 4 * N_CTX * N_CTX * N_STATE          # QK^T and PV, 2 flops per MAC
+SIGMA = (N_STATE ** 0.5) * 0.02                               # LN output x N(0, 0.02^2) weights
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch from the committed ncu summary, when one exists."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks during the timed region
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="zwg_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sms.append(float(parts[1]))
+                    maxes.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------------------------
+# distributed plumbing (one process per GPU; no collective on the data path)
+
+def dist_setup():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def shard(n: int, rank: int, world: int):
+    return n * rank // world, n * (rank + 1) // world
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline: the C restatement of the reference attention
+
+class CpuSample:
+    """One window through all 12 layers' attention (12 calls of the small.en shape) in the
+    C restatement of the reference attention, on `threads` host cores."""
+
+    def __init__(self, threads: int = 0):
+        import numpy as np
+
+        from oracle import attention as OA
+        from oracle import cref
+        self.threads = threads or os.cpu_count() or 1
+        self.isa = cref.isa()
+        rng = np.random.default_rng(0)
+        self.run = cref.Runner(OA.mha_shape(N_CTX, N_CTX, N_STATE, N_HEAD, False), self.threads)
+        self.q, self.k, self.v = ((rng.standard_normal(N_CTX * N_STATE, dtype=np.float32) * SIGMA) for _ in range(3))
+        self.out = np.zeros(N_CTX * N_STATE, np.float32)
+
+    def window(self):
+        for _ in range(N_LAYER):
+            self.run(self.q, self.k, self.v, self.out)
+
+
+def cpu_windows_per_s(min_seconds: float = 10.0, max_reps: int = 40, threads: int = 0):
+    """Windows/s of the CPU restatement, repeated until min_seconds of work."""
+    s = CpuSample(threads)
+    s.run(s.q, s.k, s.v, s.out)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        s.window()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or reps >= max_reps:
+            break
+    return {"value": reps / el, "unit": UNIT, "cores": s.threads, "kind": "port",
+            "sample": f"{reps} window(s) x {N_LAYER} layers of {N_HEAD}-head 1500x1500 d64 f32 attention, "
+                      f"oracle/attn_ref.c ({s.isa}), {el:.1f} s", "isa": s.isa}
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU attention on the host cores: each step is one window through all
+    12 layers (a bounded sample of the 64-window workload)."""
+    if rank != 0:
+        return
+    s = CpuSample()
+    for _ in range(args.warmup):
+        s.window()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s.window()
+    el = time.perf_counter() - t0
+    value = args.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "whisper small.en encoder attention (configs[2]), "
+                                                     "1 window x 12 layers per step (bounded sample)",
+                                        "n_ctx": N_CTX, "n_state": N_STATE, "n_head": N_HEAD, "n_layer": N_LAYER},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": s.threads, "kind": "port",
+                         "sample": f"1 window x {N_LAYER} layers per step, oracle/attn_ref.c ({s.isa}); "
+                                   "the reference's Zig source cannot be built here (no Zig toolchain)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+
+def time_cuda(fn, steps, stream=None):
+    import torch
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1e-3
+
+
+def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
+    """Decode-attention workloads (configs 1, 3, 4) at one GPU: one step = one new token
+    for every item through all layers' attention (f32 K/V, the reference's precision)."""
+    import torch
+
+    from zwhisper_b200 import ops
+    res = []
+
+    def run_case(name, metric, B, layers, calls):
+        # calls: list of (shape, q, k, v, out, ws, batch_strides, bytes_per_layer_call)
+        def step():
+            for _ in range(layers):
+                for sh, q, k, v, o, ws, bs, _ in calls:
+                    ops.attention_dev(q, k, v, sh, o, n_batch=B, batch_strides=bs, workspace=ws)
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        t = time_cuda(step, steps)
+        per_step = t / steps
+        byts = layers * sum(c[7] for c in calls)
+        res.append({"workload": name, "metric": metric, "value": B / per_step, "unit": "tok/s",
+                    "ms_per_step": per_step * 1e3,
+                    "roofline": {"bound": "hbm", "achieved": byts / per_step / 1e9, "peak": hbm_peak,
+                                 "unit": "GB/s", "frac": byts / per_step / 1e9 / hbm_peak, "traffic": None}})
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32)
+
+    # config 1: whisper base.en decoder step, 32 windows, 6 layers; self over 224 of 448, cross over 1500
+    B, H, d, ns = 32, 8, 64, 512
+    ck, cv = randn(B, 448, ns), randn(B, 448, ns)
+    xk, xv = randn(B, 1500, ns), randn(B, 1500, ns)
+    q, o = randn(B, 1, ns), torch.empty(B, 1, ns, device=dev)
+    sh_s = ops.mha_shape(1, 224, ns, H, True)
+    sh_c = ops.mha_shape(1, 1500, ns, H, False)
+    ws_s = torch.empty(max(1, ops.attention_workspace_bytes(sh_s, B)), dtype=torch.uint8, device=dev)
+    ws_c = torch.empty(max(1, ops.attention_workspace_bytes(sh_c, B)), dtype=torch.uint8, device=dev)
+    run_case("whisper base.en decoder self+cross attention step (configs[1]): 32 windows, 6 layers",
+             "whisper_base_en_decoder_attention_tok_per_s", B, 6,
+             [(sh_s, q, ck, cv, o, ws_s, (ns, 448 * ns, 448 * ns, ns), B * 224 * ns * 4 * 2),
+              (sh_c, q, xk, xv, o, ws_c, (ns, 1500 * ns, 1500 * ns, ns), B * 1500 * ns * 4 * 2)])
+    del ck, cv, xk, xv
+    # configs 3 and 4: Qwen2 decode over the transposed key cache at the mean cache length
+    for cfg, B, layers, H, Hkv, d, n_kv in (("configs[3] Qwen2.5-0.5B", 16, 24, 14, 2, 64, 2128),
+                                           ("configs[4] Qwen2.5-1.5B", 64, 28, 12, 2, 128, 2256)):
+        n_ctx = 2560
+        kvw = Hkv * d
+        kts = [randn(B, Hkv, d, n_ctx) for _ in range(layers)]
+        vs = [randn(B, n_ctx, kvw) for _ in range(layers)]
+        q, o = randn(B, H * d), torch.empty(B, H * d, device=dev)
+        sh = ops.AttnShape(1, n_kv, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
+        ws = torch.empty(max(1, ops.attention_workspace_bytes(sh, B)), dtype=torch.uint8, device=dev)
+        bs = (H * d, Hkv * d * n_ctx, n_ctx * kvw, H * d)
+        byts = B * n_kv * kvw * 4 * 2
+
+        def step(kts=kts, vs=vs, q=q, o=o, sh=sh, ws=ws, bs=bs, B=B):
+            for layer in range(len(kts)):
+                ops.attention_dev(q, kts[layer], vs[layer], sh, o, n_batch=B, batch_strides=bs, workspace=ws)
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        t = time_cuda(step, steps) / steps
+        achieved = layers * byts / t / 1e9
+        res.append({"workload": f"{cfg} decode attention, {B} sequences x {layers} layers, n_kv={n_kv} "
+                                f"(mean of the decode), K^T cache n_ctx={n_ctx}",
+                    "metric": "qwen_decode_attention_tok_per_s", "value": B / t, "unit": "tok/s",
+                    "ms_per_step": t * 1e3,
+                    "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                                 "frac": achieved / hbm_peak, "traffic": None}})
+        del kts, vs
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+
+    from zwhisper_b200 import _lib, ops
+    hbm_peak, tc_peak, peak_kind = load_peaks()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w0, w1 = shard(WINDOWS, rank, world)
+    nw = w1 - w0
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+
+    def rand_bf16():
+        return (torch.randn(nw, N_CTX, N_STATE, generator=g, device=dev, dtype=torch.float32) * SIGMA).to(torch.bfloat16)
+
+    layers = [(rand_bf16(), rand_bf16(), rand_bf16()) for _ in range(N_LAYER)]
+    out = torch.empty(nw, N_CTX, N_STATE, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for q, k, v in layers:
+            ops.enc_attn_bf16(q, k, v, N_HEAD, out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _lib.check(_lib.load().zwg_sync())
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t = time_cuda(step, args.steps, stream)
+    clk = clocks.stop()
+    _lib.check(_lib.load().zwg_sync())
+    barrier(world)
+    t_max = max_over_ranks(t, world)
+    value = WINDOWS * args.steps / t_max
+    launches = args.steps * N_LAYER
+    per_launch = t / launches
+    flops_launch = FLOP_PER_WINDOW_LAYER * nw
+    achieved = flops_launch / per_launch / 1e12
+
+    # ---- end to end through the C-ABI drop-in with pinned host buffers
+    e2e_steps = max(1, args.e2e_steps)
+    nel = nw * N_CTX * N_STATE
+    hq = torch.empty(nel, dtype=torch.float32, pin_memory=True)
+    hk = torch.empty(nel, dtype=torch.float32, pin_memory=True)
+    hv = torch.empty(nel, dtype=torch.float32, pin_memory=True)
+    ho = torch.empty(nel, dtype=torch.float32, pin_memory=True)
+    hq.copy_(layers[0][0].float().reshape(-1).cpu())
+    hk.copy_(layers[0][1].float().reshape(-1).cpu())
+    hv.copy_(layers[0][2].float().reshape(-1).cpu())
+    del layers
+    torch.cuda.empty_cache()
+    _lib.ensure_init(local)
+    ops.set_math("bf16", local)
+    sh = ops.mha_shape(N_CTX, N_CTX, N_STATE, N_HEAD, False)
+    c_sh = sh.to_c()
+    c_b = _lib.BatchC(nw, N_CTX * N_STATE, N_CTX * N_STATE, N_CTX * N_STATE, N_CTX * N_STATE)
+    import ctypes
+    lib = _lib.load()
+
+    def e2e_step():
+        for _ in range(N_LAYER):
+            _lib.check(lib.zwg_attention_batch_host(ctypes.byref(c_sh), ctypes.byref(c_b), hq.data_ptr(),
+                                                    hk.data_ptr(), hv.data_ptr(), ho.data_ptr()))
+    e2e_step()  # warm-up (allocates the context's staging)
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    t_e2e = time.perf_counter() - t0
+    barrier(world)
+    t_e2e = max_over_ranks(t_e2e, world)
+    ops.set_math("f32", local)
+    e2e_value = WINDOWS * e2e_steps / t_e2e
+    h2d = N_LAYER * 3 * WINDOWS * N_CTX * N_STATE * 4
+    d2h = N_LAYER * WINDOWS * N_CTX * N_STATE * 4
+    del hq, hk, hv, ho
+
+    secondary = None
+    cpu = None
+    if world == 1 and not args.no_secondary:
+        secondary = secondary_decode(dev, hbm_peak)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_windows_per_s(min_seconds=args.cpu_seconds)
+
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_max / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "whisper small.en encoder self-attention (configs[2]): 64 windows x 12 layers x "
+                               "12 heads, n_ctx 1500, d 64, bf16 operands, f32 softmax/accumulation, f32 out",
+                   "windows": WINDOWS, "n_ctx": N_CTX, "n_state": N_STATE, "n_head": N_HEAD, "n_layer": N_LAYER,
+                   "parallelism": f"windows sharded {WINDOWS // world if WINDOWS % world == 0 else 'uneven'} "
+                                  f"per GPU over {world}, no collective",
+                   "l2": "inputs larger than L2: distinct Q/K/V per layer, 5.3 GB per step"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "zwg_attention_batch_host (ops.attentionEx drop-in), math mode bf16, pinned f32 host "
+                        "buffers, conversion + tcgen05 kernel + copies on two streams",
+                "steps": e2e_steps},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tc_peak, "peak_source": f"{peak_kind} bf16 (burst)",
+                     "kernel": "enc_attn_tc_kernel", "flops_per_launch": flops_launch,
+                     "avg_launch_ms": per_launch * 1e3,
+                     "traffic": profiled_traffic("enc_attn_tc_small_en.txt")},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if secondary is not None:
+        line["secondary"] = secondary
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_setup()
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -83,6 +83,16 @@ ZWG_API size_t zwg_last_error(char* buf, size_t len);
 /* Number of CUDA devices visible (0 when none). */
 ZWG_API int zwg_device_count(void);
 
+/* Math mode of the calling thread's context for the host-pointer entry points below.
+ * ZWG_MATH_F32 (default): f32 operands and accumulation on every shape, the reference's
+ * arithmetic. ZWG_MATH_BF16: encoder-shaped calls (self-attention, n_q == n_kv, d == 64,
+ * MHA, rows of exactly n_head*64, keys as rows, not causal) convert Q/K/V to bf16 on the
+ * device and run the tcgen05 tensor-core kernel with f32 softmax and accumulation; other
+ * shapes stay f32. No reference counterpart (the reference computes in f32 only). */
+#define ZWG_MATH_F32 0
+#define ZWG_MATH_BF16 1
+ZWG_API int zwg_set_math(int mode);
+
 /* ---- drop-in, host pointers, synchronous (parity path) ------------------------------ */
 
 /* ops.attentionEx (src/ops.zig:562): q[n_q][q_stride], k, v[n_kv][kv_stride],

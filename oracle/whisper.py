@@ -342,20 +342,28 @@ def encode(W: Dict[str, np.ndarray], hp: Hparams, mel: np.ndarray, offset: int =
 
 @dataclass
 class Decoder:
-    """src/decoder.zig: Q8 weights, f32 KV cache, cross K/V per window."""
+    """src/decoder.zig: f32 KV cache, cross K/V per window. `weights="q8"` quantizes the
+    decoder matrices as the current source does (src/decoder.zig:220-229); `"f16"` widens
+    the file's f16 matrices instead, which is what the shipped reference binary (an older
+    build) computes: its logits agree with this variant to about 1e-6."""
 
     W: Dict[str, np.ndarray]
     hp: Hparams
     attention: AttnFn = _oracle_attention
+    weights: str = "q8"
     q8: Dict[str, np.ndarray] = field(default_factory=dict)
     n_past: int = 0
 
     def __post_init__(self):
         hp = self.hp
+        assert self.weights in ("q8", "f16")
         for name, w in self.W.items():
             if name.startswith("decoder.") and w.ndim == 2 and name.endswith("weight") and "positional" not in name:
-                q, s = q8_quantize(w)
-                self.q8[name] = q8_dequant(q, s)
+                if self.weights == "q8":
+                    q, s = q8_quantize(w)
+                    self.q8[name] = q8_dequant(q, s)
+                else:
+                    self.q8[name] = w.astype(np.float32)
         nt = hp.n_text_state
         self.cache_k = np.zeros((hp.n_text_layer, hp.n_text_ctx, nt), np.float32)
         self.cache_v = np.zeros_like(self.cache_k)

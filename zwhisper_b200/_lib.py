@@ -15,6 +15,8 @@ LIB_PATH = os.path.join(HERE, "libzwgpu.so")
 ZWG_OK = 0
 ZWG_ERROR = 2
 ZWG_TIMEOUT = 4
+ZWG_MATH_F32 = 0
+ZWG_MATH_BF16 = 1
 
 c_size = ctypes.c_size_t
 c_ptr = ctypes.c_void_p
@@ -58,6 +60,7 @@ SIGNATURES = {
     "zwg_rope_kt_append": (ctypes.c_int, [c_size, c_size, c_size, c_size, c_size, c_size, c_size, c_ptr, c_ptr,
                                           c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_size, c_size, c_ptr]),
     "zwg_sync": (ctypes.c_int, []),
+    "zwg_set_math": (ctypes.c_int, [ctypes.c_int]),
 }
 
 _lib = None

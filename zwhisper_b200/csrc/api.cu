@@ -42,7 +42,9 @@ struct Ctx {
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;  // second stream for pipelined host batches
     int* err = nullptr;           // device error word
+    int math = ZWG_MATH_F32;
     DevBuf q[2], k[2], v[2], out[2], ws[2];
+    DevBuf qh[2], kh[2], vh[2];   // bf16 copies for the tensor-core path
 };
 
 std::mutex g_mu;
@@ -179,6 +181,14 @@ extern "C" {
 
 int zwg_version(void) { return 1; }
 
+int zwg_set_math(int mode) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    if (mode != ZWG_MATH_F32 && mode != ZWG_MATH_BF16) return fail("unknown math mode %d", mode);
+    c->math = mode;
+    return ZWG_OK;
+}
+
 int zwg_device_count(void) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
@@ -217,6 +227,7 @@ int zwg_shutdown(void) {
     cudaStreamSynchronize(c->side);
     for (int i = 0; i < 2; i++) {
         c->q[i].release(); c->k[i].release(); c->v[i].release(); c->out[i].release(); c->ws[i].release();
+        c->qh[i].release(); c->kh[i].release(); c->vh[i].release();
     }
     cudaFree(c->err);
     cudaStreamDestroy(c->stream);
@@ -263,6 +274,14 @@ int zwg_attention_dev(const zwg_attn_shape* sh, const zwg_batch* b, const float*
     return run_dev(c, sh, b, q, k, v, out, workspace, workspace_bytes, st);
 }
 
+// An encoder-shaped call the tcgen05 kernel computes exactly as specified.
+static bool tc_eligible(const zwg_attn_shape* sh) {
+    const size_t ns = sh->n_head * 64;
+    return sh->d == 64 && !sh->causal && sh->n_head == sh->n_head_kv && sh->kt_stride == 0 &&
+           sh->n_q == sh->n_kv && sh->n_q > 0 && sh->q_stride == ns && sh->kv_stride == ns &&
+           sh->out_stride == ns && sh->n_head <= 64 && sh->n_q <= (1u << 20);
+}
+
 // Host-pointer path: stage inputs, run, copy the written head columns back.
 static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
                      const float* v, float* out) {
@@ -298,8 +317,22 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
             if (e == cudaSuccess && dv) e = cudaMemcpyAsync((float*)c->v[slot].ptr + j * dv, v + it * vbs, dv * 4, cudaMemcpyHostToDevice, st);
         }
         if (e != cudaSuccess) return cuda_fail("host to device copy", e);
-        int rc = run_dev(c, &s, &db, (float*)c->q[slot].ptr, (float*)c->k[slot].ptr, (float*)c->v[slot].ptr,
+        int rc;
+        if (c->math == ZWG_MATH_BF16 && tc_eligible(sh)) {
+            const size_t ne = n * dq;  // q, k, v have the same extent here
+            if (!c->qh[slot].ensure(ne * 2 + 16) || !c->kh[slot].ensure(ne * 2 + 16) || !c->vh[slot].ensure(ne * 2 + 16))
+                return fail("device staging allocation failed");
+            if (zwg::f32_to_bf16_launch((float*)c->q[slot].ptr, (uint16_t*)c->qh[slot].ptr, ne, st) ||
+                zwg::f32_to_bf16_launch((float*)c->k[slot].ptr, (uint16_t*)c->kh[slot].ptr, ne, st) ||
+                zwg::f32_to_bf16_launch((float*)c->v[slot].ptr, (uint16_t*)c->vh[slot].ptr, ne, st))
+                return cuda_fail("bf16 conversion", cudaGetLastError());
+            zwg::EncTcParams tp{(uint16_t*)c->qh[slot].ptr, (uint16_t*)c->kh[slot].ptr, (uint16_t*)c->vh[slot].ptr,
+                                (float*)c->out[slot].ptr, (int)n, (int)s.n_q, (int)s.n_head, c->err};
+            rc = zwg::enc_tc_launch(tp, st) ? cuda_fail("enc_attn launch", cudaGetLastError()) : ZWG_OK;
+        } else {
+            rc = run_dev(c, &s, &db, (float*)c->q[slot].ptr, (float*)c->k[slot].ptr, (float*)c->v[slot].ptr,
                          (float*)c->out[slot].ptr, c->ws[slot].ptr, c->ws[slot].cap, st);
+        }
         if (rc) return rc;
         // only the head columns of each output row are written, as in the reference
         for (size_t j = 0; j < n && e == cudaSuccess; j++)

@@ -125,6 +125,14 @@ def attention_batch_host(q, k, v, sh: AttnShape, n_batch: int, out=None, device:
     return out
 
 
+def set_math(mode: str, device: int = 0) -> None:
+    """"f32" (default, the reference's arithmetic) or "bf16" (encoder-shaped host calls on
+    the tcgen05 kernel) for the calling thread's context (zwg_set_math)."""
+    _lib.ensure_init(device)
+    code = {"f32": _lib.ZWG_MATH_F32, "bf16": _lib.ZWG_MATH_BF16}[mode]
+    _lib.check(_lib.load().zwg_set_math(code))
+
+
 # ---- scratch sizers (src/ops.zig:545-560): device workspace in floats ----------------------
 
 def attention_workspace_bytes(sh: AttnShape, n_batch: int = 1) -> int:
