@@ -123,6 +123,21 @@ ZWG_API int zwg_attention_dev(const zwg_attn_shape* sh, const zwg_batch* b, cons
                       const float* k, const float* v, float* out, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference. The decode-shaped zwg_attention_dev (split-K kernel)
+ * for callers that cannot allocate device memory: the split partials live in a 4 MiB
+ * array inside the library instead of caller workspace, and the call allocates nothing.
+ * Some hosts cannot call cudaMalloc: an embedding that reaches the engine only through
+ * this C ABI from a runtime without CUDA allocator bindings, or a streaming decode thread
+ * that must not stall, since cudaMalloc/cudaFree can synchronize the device. Limits and
+ * rules: decode shapes only (d in {32, 64, 128}, n_q * n_head / n_head_kv <= 8); a call
+ * whose partials exceed 4 MiB returns ZWG_ERROR with a message and launches nothing;
+ * every device that loads the library holds the 4 MiB until exit; the first call on a
+ * device looks up the array's device address (make it before any stream capture); all
+ * calls share the array, so calls that overlap on the GPU race: keep one device's calls
+ * on one stream or ordered. Needs no zwg_init. */
+ZWG_API int zwg_attention_dev_noalloc(const zwg_attn_shape* sh, const zwg_batch* b, const float* q,
+                                      const float* k, const float* v, float* out, void* stream);
+
 /* Encoder self-attention on tcgen05 tensor cores (src/encoder.zig:167): bf16 q, k, v
  * [n_batch][n_ctx][n_head*64], non-causal, d = 64, f32 softmax and accumulation,
  * f32 out [n_batch][n_ctx][n_head*64]. Rows of 16-byte aligned buffers are required

@@ -55,6 +55,8 @@ SIGNATURES = {
     "zwg_attention_workspace": (c_size, [ctypes.POINTER(AttnShapeC), ctypes.POINTER(BatchC)]),
     "zwg_attention_dev": (ctypes.c_int, [ctypes.POINTER(AttnShapeC), ctypes.POINTER(BatchC), c_ptr, c_ptr, c_ptr,
                                          c_ptr, c_ptr, c_size, c_ptr]),
+    "zwg_attention_dev_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnShapeC), ctypes.POINTER(BatchC), c_ptr, c_ptr,
+                                                 c_ptr, c_ptr, c_ptr]),
     "zwg_enc_attn_bf16": (ctypes.c_int, [c_size, c_size, c_size, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "zwg_f32_to_bf16": (ctypes.c_int, [c_ptr, c_ptr, c_size, c_ptr]),
     "zwg_rope_kt_append": (ctypes.c_int, [c_size, c_size, c_size, c_size, c_size, c_size, c_size, c_ptr, c_ptr,

@@ -177,6 +177,11 @@ int sync_and_check(Ctx* c, cudaStream_t st) {
 
 }  // namespace
 
+namespace zwg {
+int set_last_error(const char* msg) { return fail("%s", msg); }
+int set_last_error_cuda(const char* what, cudaError_t e) { return cuda_fail(what, e); }
+}  // namespace zwg
+
 extern "C" {
 
 int zwg_version(void) { return 1; }

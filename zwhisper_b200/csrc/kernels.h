@@ -37,6 +37,10 @@ struct DecodeParams {
 
 int flash_f32_launch(const FlashParams& p, size_t n_batch, cudaStream_t st);
 
+// Record the calling thread's last error message (read by zwg_last_error); return ZWG_ERROR.
+int set_last_error(const char* msg);
+int set_last_error_cuda(const char* what, cudaError_t e);
+
 bool decode_supported(size_t d, size_t rows, size_t kt_stride);
 void decode_plan(size_t n_batch, size_t n_head_kv, size_t n_kv, bool kt, int sm_count,
                  int* n_splits, int* chunk);
