@@ -433,6 +433,57 @@ def run_ours(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_case(args):
+    """One kernel on a small case, for ncu captures: `enc_tc` = the tcgen05 encoder kernel
+    on 16 small.en windows (one layer, 184 MB of inputs and output, above L2); `decode_qwen`
+    = the split-K decode kernel on 16 Qwen2.5-1.5B sequences (n_kv 2256, K^T cache 2560);
+    `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention."""
+    import torch
+
+    from zwhisper_b200 import ops
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    if args.kernel_case == "enc_tc":
+        B = 16
+        q, k, v = ((torch.randn(B, N_CTX, N_STATE, generator=g, device=dev) * SIGMA).to(torch.bfloat16) for _ in range(3))
+        out = torch.empty(B, N_CTX, N_STATE, device=dev)
+
+        def fn():
+            ops.enc_attn_bf16(q, k, v, N_HEAD, out)
+        work = f"{FLOP_PER_WINDOW_LAYER * B / 1e9:.1f} GFLOP per launch"
+    elif args.kernel_case == "decode_qwen":
+        B, H, Hkv, d, n_ctx, n_kv = 16, 12, 2, 128, 2560, 2256
+        q = torch.randn(B, H * d, generator=g, device=dev)
+        kt = torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev)
+        v = torch.randn(B, n_ctx, Hkv * d, generator=g, device=dev)
+        out = torch.empty_like(q)
+        sh = ops.AttnShape(1, n_kv, H, Hkv, d, H * d, Hkv * d, H * d, True, n_ctx)
+        ws = torch.empty(max(1, ops.attention_workspace_bytes(sh, B)), dtype=torch.uint8, device=dev)
+
+        def fn():
+            ops.attention_dev(q, kt, v, sh, out, n_batch=B, workspace=ws)
+        work = f"{B * n_kv * Hkv * d * 8 / 1e6:.1f} MB of K/V per launch"
+    else:
+        B, ns = 32, 512
+        q = torch.randn(B, 1, ns, generator=g, device=dev)
+        k = torch.randn(B, 1500, ns, generator=g, device=dev)
+        v = torch.randn(B, 1500, ns, generator=g, device=dev)
+        out = torch.empty_like(q)
+        sh = ops.mha_shape(1, 1500, ns, 8, False)
+        ws = torch.empty(max(1, ops.attention_workspace_bytes(sh, B)), dtype=torch.uint8, device=dev)
+
+        def fn():
+            ops.attention_dev(q, k, v, sh, out, n_batch=B, workspace=ws)
+        work = f"{B * 1500 * ns * 8 / 1e6:.1f} MB of K/V per launch"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    t = time_cuda(fn, args.steps)
+    ops.sync()
+    print(json.dumps({"kernel_case": args.kernel_case, "ms_per_launch": t / args.steps * 1e3, "work": work}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -443,7 +494,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_whisper"], default=None)
     args = ap.parse_args()
+    if args.kernel_case:
+        run_kernel_case(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -4,28 +4,38 @@
 // ops.attention, src/ops.zig:593-605 -> attentionEx, src/ops.zig:562-590): per window
 // and head, O = softmax(Q K^T / sqrt(64)) V over n_ctx = 1500 frames, non-causal.
 //
-// One CTA computes a 128-row query tile of one (window, head):
-//   warp 0      TMA producer: Q once, then K and V tiles of 128 keys into a 3-stage ring
-//               (128-byte swizzle, no multicast);
-//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma:
-//                 S_j = Q K_j^T  (M=128, N=128, K=64; A and B K-major)  -> TMEM S[j % 2]
-//                 O  += P_j V_j  (M=128, N=64,  K=128; P K-major, V MN-major) -> TMEM O
-//               in the order S_0, S_1, O_0, S_2, O_1, ... so the next scores are computed
-//               while the softmax warps work on the current ones;
-//   warps 4-7   softmax, one thread per query row (TMEM lane = row): read the row of S,
-//               online max in base 2, P = exp2(S * log2e/8 - m) written as bf16 into a
-//               swizzled shared-memory tile (the A operand of the second MMA), row sums in
-//               f32, O rescaled in TMEM only when the running max grows by more than 2^8
-//               (otherwise the stale max is kept; numerator and denominator share it);
-//               finally O / l is written to global memory as f32.
-// Keys past n_ctx come from the TMA's zero fill and are masked to -inf before the max;
-// query rows past n_ctx are computed on zeros and not stored.
+// Persistent kernel, one CTA per SM. A work item is a pair of 128-row query tiles of one
+// (window, head); items are dealt round-robin to the CTAs, pairs of one head first so CTAs
+// running together read the same K/V through L2.
+//   warp 0      TMA producer: both Q tiles of an item (double-buffered across items), then
+//               K and V tiles of 128 keys into a 3-stage ring (128-byte swizzle, no
+//               multicast).
+//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma (kind::f16, bf16):
+//                 S_t = Q_t K_j^T  (M=128, N=128, K=64; A, B K-major from shared memory)
+//                 O_t += P_t V_j   (M=128, N=64, K=128; P from TMEM, V MN-major in smem)
+//               for the two query tiles t = 0, 1, ordered per tile as PV_t(j), S_t(j+1), so
+//               one tile's scores are computed while the other tile's softmax runs. The
+//               tensor pipe runs a thread's MMAs in issue order, which makes it safe for
+//               S_t(j+1) to overwrite the TMEM columns P_t(j) occupied.
+//   warps 2-3   idle (they complete the control warpgroup for the register split);
+//   warps 4-11  two softmax warpgroups, one per query tile, one thread per query row (TMEM
+//               lane = row): read the row of S, online max in base 2, P = exp2(S * c - m)
+//               packed to bf16 and stored back into the first 64 columns of the same TMEM
+//               region (the A operand of the PV MMA), f32 row sums, O rescaled in TMEM only
+//               when the running max grows by more than 2^8 (otherwise the stale max is
+//               kept: numerator and denominator share it); after the last tile, O / l is
+//               written to global memory as f32.
+// TMEM columns: S/P of tile 0 at 0, O_0 at 128, S/P of tile 1 at 256, O_1 at 384.
+// Keys past n_ctx come from the TMA's zero fill and are masked to -inf before the max; query
+// rows past n_ctx are computed on zeros and not stored.
 //
 // Every mbarrier wait is bounded (sm100::mbar_wait): a wait that runs out records
-// kErrTimeout in the context's error word and the kernel skips to its teardown.
+// kErrTimeout in the context's error word, the CTA skips to its teardown, and CTAs that
+// start later see the error word and exit at once.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -38,68 +48,76 @@ using namespace sm100;
 
 namespace enc_tc {
 
-constexpr int BM = 128;        // query rows per CTA
+constexpr int BM = 128;        // query rows per tile
 constexpr int BN = 128;        // keys per tile
 constexpr int D = 64;          // head dim
 constexpr int NS = 3;          // K/V pipeline stages
-constexpr int THREADS = 256;
+constexpr int THREADS = 384;   // 12 warps: control warpgroup + two softmax warpgroups
+// Register split (setmaxnreg): launched at 168 per thread (65536 / 384, rounded down to a
+// multiple of 8) = 64512 in all; the control warpgroup gives back to 56 and the two softmax
+// warpgroups take 224: 128 * 56 + 256 * 224 = 64512, the launch total exactly.
+constexpr uint32_t REGS_CONTROL = 56;
+constexpr uint32_t REGS_SOFTMAX = 224;
+static_assert(128 * REGS_CONTROL + 256 * REGS_SOFTMAX <= 384 * 168, "register split exceeds the launch");
 constexpr uint32_t TILE_BYTES = BM * D * 2;  // 16 KB: one [128][64] bf16 tile
-constexpr uint32_t P_BYTES = BM * BN * 2;    // 32 KB: [128][128] bf16 = two K-major halves
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_O = 256;
+__host__ __device__ constexpr uint32_t s_col(int t) { return t ? 256u : 0u; }
+__host__ __device__ constexpr uint32_t o_col(int t) { return t ? 384u : 128u; }
 
 struct Smem {
-    // 1024-byte aligned tiles (128-byte swizzle atoms)
-    uint8_t q[TILE_BYTES];
+    uint8_t q[2][2][TILE_BYTES];  // [buffer][query tile], 1024-byte aligned tiles
     uint8_t k[NS][TILE_BYTES];
     uint8_t v[NS][TILE_BYTES];
-    uint8_t p[2][P_BYTES];
-    uint64_t q_full;
-    uint64_t k_full[NS];
-    uint64_t v_full[NS];
-    uint64_t kv_empty[NS];
-    uint64_t s_full[2];
-    uint64_t p_full[2];
-    uint64_t o_done;
+    uint64_t q_full[2], q_empty[2];
+    uint64_t k_full[NS], v_full[NS], kv_empty[NS];
+    uint64_t s_full[2], p_full[2], o_final[2];
     uint32_t tmem_base;
+    int abort_flag;
 };
 
 constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;  // + alignment slack
 
+struct Work {
+    int n_items, n_pairs, n_tiles;
+};
+
+__device__ __forceinline__ void decode_item(int item, int n_pairs, int n_head, int& win, int& head, int& pair) {
+    pair = item % n_pairs;
+    head = (item / n_pairs) % n_head;
+    win = item / (n_pairs * n_head);
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, float* __restrict__ out, int n_ctx, int n_head,
-                       int* err) {
+                       int n_items, int* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int q_tile = blockIdx.x;
-    const int head = blockIdx.y;
-    const int item = blockIdx.z;
-    const int q0 = q_tile * BM;
-    const int n_tiles = (n_ctx + BN - 1) / BN;
+    const int n_tiles = (n_ctx + BN - 1) / BN;          // key tiles (= query tiles)
+    const int n_pairs = (n_tiles + 1) / 2;
 
     // after a recorded failure the remaining CTAs do nothing (uniform exit, before any
     // barrier or TMEM allocation)
-    __shared__ int abort_flag;
-    if (threadIdx.x == 0) abort_flag = err ? *(volatile int*)err : 0;
+    if (threadIdx.x == 0) sm.abort_flag = err ? *(volatile int*)err : 0;
     __syncthreads();
-    if (abort_flag) return;
+    if (sm.abort_flag) return;
 
     if (threadIdx.x == 0) {
-        mbar_init(&sm.q_full, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&sm.q_full[b], 1);
+            mbar_init(&sm.q_empty[b], 1);
+            mbar_init(&sm.s_full[b], 1);
+            mbar_init(&sm.p_full[b], 128);
+            mbar_init(&sm.o_final[b], 1);
+        }
         for (int s = 0; s < NS; s++) {
             mbar_init(&sm.k_full[s], 1);
             mbar_init(&sm.v_full[s], 1);
             mbar_init(&sm.kv_empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
-            mbar_init(&sm.s_full[b], 1);
-            mbar_init(&sm.p_full[b], 128);
-        }
-        mbar_init(&sm.o_done, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -111,157 +129,189 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
-    if (warp == 0) {
+    if (warp < 4) {
+      regs_dec<REGS_CONTROL>();
+      if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             prefetch_tmap(&tm_q);
             prefetch_tmap(&tm_k);
             prefetch_tmap(&tm_v);
-            const int c0 = head * D;
-            mbar_arrive_expect_tx(&sm.q_full, TILE_BYTES);
-            tma_load_3d(&tm_q, &sm.q_full, sm.q, c0, q0, item);
-            for (int j = 0; j < n_tiles; j++) {
-                const int s = j % NS;
-                if (j >= NS && !mbar_wait(&sm.kv_empty[s], ((j / NS) - 1) & 1, err)) break;
-                mbar_arrive_expect_tx(&sm.k_full[s], TILE_BYTES);
-                tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s], c0, j * BN, item);
-                mbar_arrive_expect_tx(&sm.v_full[s], TILE_BYTES);
-                tma_load_3d(&tm_v, &sm.v_full[s], sm.v[s], c0, j * BN, item);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, it++) {
+                int win, head, pair;
+                decode_item(item, n_pairs, n_head, win, head, pair);
+                const int c0 = head * D;
+                const int qb = it & 1;
+                if (it >= 2 && !(ok = mbar_wait(&sm.q_empty[qb], ((it >> 1) - 1) & 1, err))) break;
+                mbar_arrive_expect_tx(&sm.q_full[qb], 2 * TILE_BYTES);
+                tma_load_3d(&tm_q, &sm.q_full[qb], sm.q[qb][0], c0, pair * 2 * BM, win);
+                tma_load_3d(&tm_q, &sm.q_full[qb], sm.q[qb][1], c0, pair * 2 * BM + BM, win);
+                for (int j = 0; j < n_tiles; j++, g++) {
+                    const int s = g % NS;
+                    if (g >= NS && !(ok = mbar_wait(&sm.kv_empty[s], ((g / NS) - 1) & 1, err))) break;
+                    mbar_arrive_expect_tx(&sm.k_full[s], TILE_BYTES);
+                    tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s], c0, j * BN, win);
+                    mbar_arrive_expect_tx(&sm.v_full[s], TILE_BYTES);
+                    tma_load_3d(&tm_v, &sm.v_full[s], sm.v[s], c0, j * BN, win);
+                }
             }
         }
-    } else if (warp == 1) {
+      } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_f16(BM, BN, true, false, false);
             constexpr uint32_t idesc_o = idesc_f16(BM, D, true, false, true);
-            const uint32_t q_addr = smem_u32(sm.q);
-            bool ok = mbar_wait(&sm.q_full, 0, err);
-            // S_j = Q K_j^T: four K=16 steps along the head dim inside the 128-byte rows
-            auto issue_s = [&](int j) -> bool {
-                const int s = j % NS;
-                if (!mbar_wait(&sm.k_full[s], (j / NS) & 1, err)) return false;
-                tc_fence_after();
-                const uint32_t k_addr = smem_u32(sm.k[s]);
-                const uint32_t d_tmem = tmem + ((j & 1) ? TMEM_S1 : TMEM_S0);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, it++) {
+                const int qb = it & 1;
+                if (!(ok = mbar_wait(&sm.q_full[qb], (it >> 1) & 1, err))) break;
+                const uint32_t q_addr0 = smem_u32(sm.q[qb][0]), q_addr1 = smem_u32(sm.q[qb][1]);
+                auto issue_s = [&](int t, int s) {
+                    const uint32_t k_addr = smem_u32(sm.k[s]);
+                    const uint32_t q_addr = t ? q_addr1 : q_addr0;
 #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) {
-                    const uint64_t a = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-                    const uint64_t b = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-                    mma_f16_ss(d_tmem, a, b, idesc_s, kk > 0);
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint64_t a = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
+                        const uint64_t b = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
+                        mma_f16_ss(tmem + s_col(t), a, b, idesc_s, kk > 0);
+                    }
+                };
+                {
+                    const int s = g % NS;
+                    if (!(ok = mbar_wait(&sm.k_full[s], (g / NS) & 1, err))) break;
+                    tc_fence_after();
+                    issue_s(0, s);
+                    mma_commit(&sm.s_full[0]);
+                    issue_s(1, s);
+                    mma_commit(&sm.s_full[1]);
                 }
-                mma_commit(&sm.s_full[j & 1]);
-                return true;
-            };
-            // O += P_j V_j: eight K=16 steps along the keys; P in two 64-key halves
-            auto issue_o = [&](int j) -> bool {
-                const int s = j % NS;
-                if (!mbar_wait(&sm.p_full[j & 1], (j >> 1) & 1, err)) return false;
-                if (!mbar_wait(&sm.v_full[s], (j / NS) & 1, err)) return false;
-                tc_fence_after();
-                const uint32_t p_addr = smem_u32(sm.p[j & 1]);
-                const uint32_t v_addr = smem_u32(sm.v[s]);
+                for (int j = 0; ok && j < n_tiles; j++) {
+                    const uint32_t gj = g + j;
+                    const int s = gj % NS;
+                    const int s2 = (gj + 1) % NS;
+                    for (int t = 0; t < 2; t++) {
+                        if (!(ok = mbar_wait(&sm.p_full[t], gj & 1, err))) break;
+                        if (t == 0 && !(ok = mbar_wait(&sm.v_full[s], (gj / NS) & 1, err))) break;
+                        tc_fence_after();
+                        const uint32_t v_addr = smem_u32(sm.v[s]);
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++) {
-                    const uint64_t a = smem_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, 8192, 1024);
-                    mma_f16_ss(tmem + TMEM_O, a, b, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < BN / 16; kk++) {
+                            const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, 8192, 1024);
+                            mma_f16_ts(tmem + o_col(t), tmem + s_col(t) + kk * 8, b, idesc_o,
+                                       (j > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        if (j + 1 < n_tiles) {
+                            if (t == 0 && !(ok = mbar_wait(&sm.k_full[s2], ((gj + 1) / NS) & 1, err))) break;
+                            tc_fence_after();
+                            issue_s(t, s2);
+                            mma_commit(&sm.s_full[t]);
+                        } else {
+                            mma_commit(&sm.o_final[t]);
+                        }
+                    }
+                    if (ok) mma_commit(&sm.kv_empty[s]);
                 }
-                mma_commit(&sm.kv_empty[s]);
-                mma_commit(&sm.o_done);
-                return true;
-            };
-            if (ok) ok = issue_s(0);
-            for (int j = 1; ok && j <= n_tiles; j++) {
-                if (j < n_tiles) ok = issue_s(j);
-                if (ok) ok = issue_o(j - 1);
+                if (ok) mma_commit(&sm.q_empty[qb]);
+                g += n_tiles;
             }
         }
-    } else if (warp >= 4) {
-        // ------------------------------------------------------------ softmax warps
-        const int row = (warp - 4) * 32 + lane;                 // TMEM lane = query row
-        const uint32_t lane_addr = (uint32_t)((warp - 4) * 32) << 16;
-        const float c = 1.4426950408889634f * 0.125f;           // log2(e) / sqrt(64)
-        float m = -INFINITY;                                    // running max, base-2 units
-        float l = 0.f;
+      }
+    } else {
+        regs_inc<REGS_SOFTMAX>();
+        // ------------------------------------------------------------ softmax warpgroups
+        const int t = (warp - 4) >> 2;                  // query tile of this warpgroup
+        const int quarter = warp & 3;                   // TMEM lanes this warp may access
+        const int row = quarter * 32 + lane;            // TMEM lane = query row in the tile
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        const uint32_t s_addr = tmem + lane_addr + s_col(t);
+        const uint32_t o_addr = tmem + lane_addr + o_col(t);
+        const float c = 1.4426950408889634f * 0.125f;  // log2(e) / sqrt(64)
+        uint32_t g = 0;
+        int it = 0;
         bool ok = true;
-        for (int j = 0; j < n_tiles && ok; j++) {
-            const int b = j & 1;
-            if (!mbar_wait(&sm.s_full[b], (j >> 1) & 1, err)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t sr[BN];
-#pragma unroll
-            for (int cc = 0; cc < BN / 32; cc++) {
-                uint32_t tmp[32];
-                tmem_ld32(tmem + lane_addr + (b ? TMEM_S1 : TMEM_S0) + cc * 32, tmp);
-#pragma unroll
-                for (int i = 0; i < 32; i++) sr[cc * 32 + i] = tmp[i];
-            }
-            tmem_ld_wait();
-            const int valid = n_ctx - j * BN;                   // keys present in this tile
-            float mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < BN; i++) {
-                float x = __uint_as_float(sr[i]);
-                if (i >= valid) x = -INFINITY;
-                sr[i] = __float_as_uint(x);
-                mx = fmaxf(mx, x);
-            }
-            const float m_tile = mx * c;
-            // P buffer b and the O accumulator are free once O_{j-1} has completed
-            if (j > 0) {
-                if (!mbar_wait(&sm.o_done, (j - 1) & 1, err)) { ok = false; break; }
+        for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, it++) {
+            int win, head, pair;
+            decode_item(item, n_pairs, n_head, win, head, pair);
+            float m = -INFINITY;                        // running max, base-2 units
+            float l = 0.f;
+            for (int j = 0; j < n_tiles; j++) {
+                const uint32_t gj = g + j;
+                if (!(ok = mbar_wait(&sm.s_full[t], gj & 1, err))) break;
                 tc_fence_after();
-            }
-            if (j == 0) {
-                m = m_tile;
-            } else if (m_tile > m + 8.0f) {
-                const float corr = exp2_approx(m - m_tile);
-                l *= corr;
+                uint32_t sr[BN];
 #pragma unroll
-                for (int cc = 0; cc < D / 32; cc++) {
-                    uint32_t o[32];
-                    tmem_ld32(tmem + lane_addr + TMEM_O + cc * 32, o);
-                    tmem_ld_wait();
+                for (int cc = 0; cc < BN / 32; cc++) {
+                    uint32_t tmp[32];
+                    tmem_ld32(s_addr + cc * 32, tmp);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-                    tmem_st32(tmem + lane_addr + TMEM_O + cc * 32, o);
+                    for (int i = 0; i < 32; i++) sr[cc * 32 + i] = tmp[i];
+                }
+                tmem_ld_wait();
+                const int valid = n_ctx - j * BN;        // keys present in this tile
+                float mx = -INFINITY;
+                if (valid >= BN) {
+#pragma unroll
+                    for (int i = 0; i < BN; i++) mx = fmaxf(mx, __uint_as_float(sr[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < BN; i++) {
+                        const float x = i < valid ? __uint_as_float(sr[i]) : -INFINITY;
+                        sr[i] = __float_as_uint(x);
+                        mx = fmaxf(mx, x);
+                    }
+                }
+                const float m_tile = mx * c;
+                if (j == 0) {
+                    m = m_tile;
+                } else if (m_tile > m + 8.0f) {
+                    // O_t of the previous tile is complete: this tile's S was committed
+                    // after the previous PV
+                    const float corr = exp2_approx(m - m_tile);
+                    l *= corr;
+#pragma unroll
+                    for (int cc = 0; cc < D / 32; cc++) {
+                        uint32_t o[32];
+                        tmem_ld32(o_addr + cc * 32, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+                        tmem_st32(o_addr + cc * 32, o);
+                    }
+                    m = m_tile;
+                }
+                const float neg_m = -m;
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float p0 = exp2_approx(fmaf(__uint_as_float(sr[cc * 32 + 2 * e]), c, neg_m));
+                        const float p1 = exp2_approx(fmaf(__uint_as_float(sr[cc * 32 + 2 * e + 1]), c, neg_m));
+                        l += p0 + p1;
+                        __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+                        pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+                    }
+                    tmem_st16(s_addr + cc * 16, pk);
                 }
                 tmem_st_wait();
-                m = m_tile;
+                tc_fence_before();
+                mbar_arrive(&sm.p_full[t]);
             }
-            // probabilities -> bf16, 128-byte swizzled K-major rows: 16-byte chunk c of
-            // row r in 64-key half h lands at chunk (c ^ (r & 7)) of that row
-            uint8_t* pbase = sm.p[b];
-            const float neg_m = -m;
-#pragma unroll
-            for (int ch = 0; ch < BN / 8; ch++) {
-                uint32_t packed[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float p0 = exp2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e]), c, neg_m));
-                    const float p1 = exp2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e + 1]), c, neg_m));
-                    l += p0 + p1;
-                    __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-                    packed[e] = *reinterpret_cast<uint32_t*>(&h2);
-                }
-                const int half = ch >> 3, cir = ch & 7;
-                uint8_t* dst = pbase + half * (BM * 128) + row * 128 + ((cir ^ (row & 7)) << 4);
-                *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(&sm.p_full[b]);
-        }
-        // ---- epilogue: O / l -> out[item][q0 + row][head * 64 ..]
-        if (ok && mbar_wait(&sm.o_done, (n_tiles - 1) & 1, err)) {
+            // ---- epilogue: O / l -> out[win][q0 + row][head * 64 ..]
+            if (!ok || !(ok = mbar_wait(&sm.o_final[t], it & 1, err))) break;
             tc_fence_after();
             const float inv = l > 0.f ? 1.0f / l : 0.f;
-            const int grow = q0 + row;
-            float* orow = out + ((size_t)item * n_ctx + grow) * (size_t)(n_head * D) + head * D;
+            const int grow = pair * 2 * BM + t * BM + row;
+            float* orow = out + ((size_t)win * n_ctx + grow) * (size_t)(n_head * D) + head * D;
 #pragma unroll
             for (int cc = 0; cc < D / 32; cc++) {
                 uint32_t o[32];
-                tmem_ld32(tmem + lane_addr + TMEM_O + cc * 32, o);
+                tmem_ld32(o_addr + cc * 32, o);
                 tmem_ld_wait();
                 if (grow < n_ctx) {
 #pragma unroll
@@ -272,6 +322,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
+            tc_fence_before();
+            g += n_tiles;
         }
     }
 
@@ -339,8 +391,14 @@ int enc_tc_launch(const EncTcParams& p, cudaStream_t st) {
             attr_set[dev] = true;
         }
     }
-    dim3 grid((unsigned)((p.n_ctx + BM - 1) / BM), (unsigned)p.n_head, (unsigned)p.n_batch);
-    enc_attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mk, mv, p.out, p.n_ctx, p.n_head, p.err);
+    static int sm_count[64] = {};
+    if (!sm_count[dev]) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int n_tiles = (p.n_ctx + BN - 1) / BN;
+    const long long n_items = (long long)p.n_batch * p.n_head * ((n_tiles + 1) / 2);
+    if (n_items > (1ll << 30)) return -1;
+    const int grid = (int)std::min<long long>(n_items, sm_count[dev] > 0 ? sm_count[dev] : 148);
+    enc_attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mk, mv, p.out, p.n_ctx, p.n_head, (int)n_items,
+                                                          p.err);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
