@@ -99,8 +99,6 @@ def test_rejects_calls_beyond_the_scratch_limit(env):
     lib = _lib.load()
     c = sh.to_c()
     b = _lib.BatchC(B, H * d, Hkv * d * n_ctx, n_ctx * Hkv * d, H * d)
-    need = ops.attention_workspace_bytes(sh, B)
-    assert need > (4 << 20)
     rc = lib.zwg_attention_dev_noalloc(ctypes.byref(c), ctypes.byref(b), q.data_ptr(), k.data_ptr(), k.data_ptr(),
                                        out.data_ptr(), None)
     assert rc == _lib.ZWG_ERROR

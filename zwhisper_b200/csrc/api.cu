@@ -117,7 +117,9 @@ Plan plan_for(const zwg_attn_shape* sh, size_t n_batch, int sm_count) {
     Plan pl{};
     pl.decode = use_decode(sh);
     if (pl.decode) {
-        zwg::decode_plan(n_batch, sh->n_head_kv, sh->n_kv, sh->kt_stride != 0, sm_count, &pl.n_splits, &pl.chunk);
+        int ch_tiles = 1;
+        zwg::decode_tma_plan(n_batch, sh->n_head_kv, sh->n_kv, sm_count, &pl.n_splits, &ch_tiles);
+        pl.chunk = ch_tiles * 32;
         const size_t rows = sh->n_q * (sh->n_head / sh->n_head_kv);
         pl.ws_bytes = zwg::decode_workspace_floats(n_batch, sh->n_head_kv, rows, pl.n_splits, sh->d) * sizeof(float);
     }
@@ -143,7 +145,8 @@ int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q
         p.n_splits = pl.n_splits; p.chunk = pl.chunk;
         if (b) { p.q_bs = b->q_batch_stride; p.k_bs = b->k_batch_stride; p.v_bs = b->v_batch_stride; p.out_bs = b->out_batch_stride; }
         if (p.k_bs % 4 || p.v_bs % 4 || p.q_bs % 4) return fail("decode kernel needs batch strides that are multiples of 4");
-        rc = zwg::decode_f32_launch(p, nb, st);
+        if (!zwg::decode_tma_supported(p)) return fail("decode shape not supported by the TMA decode kernel");
+        rc = zwg::decode_tma_launch(p, nb, c->sm_count, c->err, st);
     } else {
         zwg::FlashParams p{};
         p.q = q; p.k = k; p.v = v; p.out = out;

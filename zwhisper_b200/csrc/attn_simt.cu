@@ -428,6 +428,8 @@ int decode_rmax(size_t rows) {
     return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8;
 }
 
+int decode_combine_launch(const DecodeParams& p, size_t n_batch, cudaStream_t st);
+
 template <int D, bool KT>
 static int decode_launch_d(const DecodeParams& p, size_t n_batch, int rmax, cudaStream_t st) {
     dim3 grid((unsigned)p.n_splits, (unsigned)p.n_head_kv, (unsigned)n_batch);
@@ -438,12 +440,20 @@ static int decode_launch_d(const DecodeParams& p, size_t n_batch, int rmax, cuda
         default: decode_f32_kernel<D, KT, 8><<<grid, 128, 0, st>>>(p); break;
     }
     if (cudaPeekAtLastError() != cudaSuccess) return -1;
-    if (p.n_splits > 1) {
-        const size_t rows = p.n_q * (p.n_head / p.n_head_kv);
-        decode_combine_kernel<D><<<(unsigned)(n_batch * p.n_head_kv * rows), D, 0, st>>>(p);
-        if (cudaPeekAtLastError() != cudaSuccess) return -1;
-    }
+    if (p.n_splits > 1) return decode_combine_launch(p, n_batch, st);
     return 0;
+}
+
+int decode_combine_launch(const DecodeParams& p, size_t n_batch, cudaStream_t st) {
+    const size_t rows = p.n_q * (p.n_head / p.n_head_kv);
+    const unsigned blocks = (unsigned)(n_batch * p.n_head_kv * rows);
+    switch (p.d) {
+        case 32: decode_combine_kernel<32><<<blocks, 32, 0, st>>>(p); break;
+        case 64: decode_combine_kernel<64><<<blocks, 64, 0, st>>>(p); break;
+        case 128: decode_combine_kernel<128><<<blocks, 128, 0, st>>>(p); break;
+        default: return -1;
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
 int decode_f32_launch(const DecodeParams& p, size_t n_batch, cudaStream_t st) {

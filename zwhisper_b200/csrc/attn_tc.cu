@@ -10,22 +10,25 @@
 //   warp 0      TMA producer: both Q tiles of an item (double-buffered across items), then
 //               K and V tiles of 128 keys into a 3-stage ring (128-byte swizzle, no
 //               multicast).
-//   warp 1      allocates 512 TMEM columns; lane 0 issues tcgen05.mma (kind::f16, bf16):
+//   warps 1-2   warp 1 allocates 512 TMEM columns; lane 0 of warp 1 + t issues the
+//               tcgen05.mma (kind::f16, bf16) of query tile t:
 //                 S_t = Q_t K_j^T  (M=128, N=128, K=64; A, B K-major from shared memory)
 //                 O_t += P_t V_j   (M=128, N=64, K=128; P from TMEM, V MN-major in smem)
-//               for the two query tiles t = 0, 1, ordered per tile as PV_t(j), S_t(j+1), so
-//               one tile's scores are computed while the other tile's softmax runs. The
-//               tensor pipe runs a thread's MMAs in issue order, which makes it safe for
-//               S_t(j+1) to overwrite the TMEM columns P_t(j) occupied.
-//   warps 2-3   idle (they complete the control warpgroup for the register split);
+//               for the two query tiles t = 0, 1. The next scores S_t(j+1) are issued as soon
+//               as the softmax has copied S_t(j) into registers (P has its own columns), so
+//               the tensor core computes them while the exponentials of tile j run; the PV
+//               of tile j follows when P_t(j) is written.
+//   warp 3      idle (it completes the control warpgroup for the register split);
 //   warps 4-11  two softmax warpgroups, one per query tile, one thread per query row (TMEM
-//               lane = row): read the row of S, online max in base 2, P = exp2(S * c - m)
-//               packed to bf16 and stored back into the first 64 columns of the same TMEM
-//               region (the A operand of the PV MMA), f32 row sums, O rescaled in TMEM only
-//               when the running max grows by more than 2^8 (otherwise the stale max is
-//               kept: numerator and denominator share it); after the last tile, O / l is
-//               written to global memory as f32.
-// TMEM columns: S/P of tile 0 at 0, O_0 at 128, S/P of tile 1 at 256, O_1 at 384.
+//               lane = row): read the 128 scores of the row (then release the score columns
+//               to the next S), online max in base 2, P = exp2(S * c - m) packed to bf16 and
+//               stored into the tile's P columns (the A operand of the PV MMA) once the
+//               previous PV has read them, f32 row sums, O rescaled in TMEM only when the
+//               running max grows by more than 2^8 (otherwise the stale max is kept:
+//               numerator and denominator share it); after the last tile, O / l is written
+//               to global memory as f32.
+// TMEM columns per query tile t: S at 256t (128), P at 256t + 128 (64 columns of bf16
+// pairs), O at 256t + 192 (64); the two tiles fill all 512.
 // Keys past n_ctx come from the TMA's zero fill and are masked to -inf before the max; query
 // rows past n_ctx are computed on zeros and not stored.
 //
@@ -58,11 +61,42 @@ constexpr int THREADS = 384;   // 12 warps: control warpgroup + two softmax warp
 // warpgroups take 224: 128 * 56 + 256 * 224 = 64512, the launch total exactly.
 constexpr uint32_t REGS_CONTROL = 56;
 constexpr uint32_t REGS_SOFTMAX = 224;
-static_assert(128 * REGS_CONTROL + 256 * REGS_SOFTMAX <= 384 * 168, "register split exceeds the launch");
+static_assert(128 * REGS_CONTROL + 256 * REGS_SOFTMAX <= THREADS * 168, "register split exceeds the launch");
 constexpr uint32_t TILE_BYTES = BM * D * 2;  // 16 KB: one [128][64] bf16 tile
 constexpr uint32_t TMEM_COLS = 512;
+// per query tile t: scores at 256t, probabilities (bf16 pairs) at 256t + 128, O at 256t + 192
 __host__ __device__ constexpr uint32_t s_col(int t) { return t ? 256u : 0u; }
-__host__ __device__ constexpr uint32_t o_col(int t) { return t ? 384u : 128u; }
+__host__ __device__ constexpr uint32_t p_col(int t) { return t ? 384u : 128u; }
+__host__ __device__ constexpr uint32_t o_col(int t) { return t ? 448u : 192u; }
+
+// Pairs of exponentials per 16 (per 32 columns) evaluated by exp2_poly2 on the FMA pipe;
+// the others use the MUFU ex2. MUFU is the limit of a d=64 attention (16 exponentials per
+// clock per SM against 128 FMA lanes), so part of the work moves to the FMA pipe.
+#ifndef ZWG_POLY_PAIRS
+#define ZWG_POLY_PAIRS 0
+#endif
+constexpr int POLY_PAIRS = ZWG_POLY_PAIRS;
+
+// 2^x from a Cody-Waite split x = j + f (j = round(x), |f| <= 0.5) and a degree-3 minimax
+// polynomial for 2^f fitted here (max relative error 1.0e-4, well below bf16 rounding of
+// P); 2^j is added into the exponent field. Inputs are clamped at -120 (so -inf gives
+// ~7.5e-37 rather than a wrapped exponent). Packed f32x2 arithmetic, two values at once.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+    x.x = fmaxf(x.x, -120.f);
+    x.y = fmaxf(x.y, -120.f);
+    const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+    const float2 r = __fadd2_rn(t, make_float2(-kRound, -kRound));
+    const float2 f = __ffma2_rn(r, make_float2(-1.f, -1.f), x);
+    float2 p = __ffma2_rn(make_float2(0.05500858277f, 0.05500858277f), f,
+                          make_float2(0.24221037328f, 0.24221037328f));
+    p = __ffma2_rn(p, f, make_float2(0.69328290224f, 0.69328290224f));
+    p = __ffma2_rn(p, f, make_float2(1.f, 1.f));
+    // the low bits of t hold j; shifting them into the exponent field scales by 2^j
+    p.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+    p.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+    return p;
+}
 
 struct Smem {
     uint8_t q[2][2][TILE_BYTES];  // [buffer][query tile], 1024-byte aligned tiles
@@ -70,12 +104,16 @@ struct Smem {
     uint8_t v[NS][TILE_BYTES];
     uint64_t q_full[2], q_empty[2];
     uint64_t k_full[NS], v_full[NS], kv_empty[NS];
-    uint64_t s_full[2], p_full[2], o_final[2];
+    uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
     uint32_t tmem_base;
     int abort_flag;
 };
 
 constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;  // + alignment slack
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 struct Work {
     int n_items, n_pairs, n_tiles;
@@ -108,15 +146,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; b++) {
             mbar_init(&sm.q_full[b], 1);
-            mbar_init(&sm.q_empty[b], 1);
+            mbar_init(&sm.q_empty[b], 2);  // one commit from each MMA issuer
             mbar_init(&sm.s_full[b], 1);
+            mbar_init(&sm.s_free[b], 128);
             mbar_init(&sm.p_full[b], 128);
-            mbar_init(&sm.o_final[b], 1);
+            mbar_init(&sm.pv_done[b], 1);
         }
         for (int s = 0; s < NS; s++) {
             mbar_init(&sm.k_full[s], 1);
             mbar_init(&sm.v_full[s], 1);
-            mbar_init(&sm.kv_empty[s], 1);
+            mbar_init(&sm.kv_empty[s], 2);  // one commit from each MMA issuer
         }
         fence_mbar_init();
     }
@@ -159,62 +198,57 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
         }
-      } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+      } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------------------ MMA issuers
+        // warp 1 issues the MMAs of query tile 0, warp 2 those of tile 1: a thread's MMAs
+        // run in issue order, and with one issuer per tile neither tile's instructions
+        // wait behind the other tile's barriers.
         if (lane == 0) {
+            const int t = warp - 1;
             constexpr uint32_t idesc_s = idesc_f16(BM, BN, true, false, false);
             constexpr uint32_t idesc_o = idesc_f16(BM, D, true, false, true);
-            uint32_t g = 0;
+            uint32_t g = 0;      // global key-tile counter (phases of the per-tile barriers)
             int it = 0;
             bool ok = true;
             for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, it++) {
                 const int qb = it & 1;
                 if (!(ok = mbar_wait(&sm.q_full[qb], (it >> 1) & 1, err))) break;
-                const uint32_t q_addr0 = smem_u32(sm.q[qb][0]), q_addr1 = smem_u32(sm.q[qb][1]);
-                auto issue_s = [&](int t, int s) {
-                    const uint32_t k_addr = smem_u32(sm.k[s]);
-                    const uint32_t q_addr = t ? q_addr1 : q_addr0;
+                const uint32_t q_addr = smem_u32(sm.q[qb][t]);
+                // S_t(tile gj) = Q_t K^T into the score columns, once the softmax has read the
+                // previous scores out of them (s_free of tile gj - 1)
+                auto issue_s = [&](uint32_t gj) -> bool {
+                    if (!mbar_wait(&sm.k_full[gj % NS], (gj / NS) & 1, err)) return false;
+                    if (gj > 0 && !mbar_wait(&sm.s_free[t], (gj - 1) & 1, err)) return false;
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(sm.k[gj % NS]);
 #pragma unroll
                     for (int kk = 0; kk < D / 16; kk++) {
                         const uint64_t a = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
                         const uint64_t b = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
                         mma_f16_ss(tmem + s_col(t), a, b, idesc_s, kk > 0);
                     }
+                    mma_commit(&sm.s_full[t]);
+                    return true;
                 };
-                {
-                    const int s = g % NS;
-                    if (!(ok = mbar_wait(&sm.k_full[s], (g / NS) & 1, err))) break;
-                    tc_fence_after();
-                    issue_s(0, s);
-                    mma_commit(&sm.s_full[0]);
-                    issue_s(1, s);
-                    mma_commit(&sm.s_full[1]);
-                }
+                ok = issue_s(g);
                 for (int j = 0; ok && j < n_tiles; j++) {
                     const uint32_t gj = g + j;
                     const int s = gj % NS;
-                    const int s2 = (gj + 1) % NS;
-                    for (int t = 0; t < 2; t++) {
-                        if (!(ok = mbar_wait(&sm.p_full[t], gj & 1, err))) break;
-                        if (t == 0 && !(ok = mbar_wait(&sm.v_full[s], (gj / NS) & 1, err))) break;
-                        tc_fence_after();
-                        const uint32_t v_addr = smem_u32(sm.v[s]);
+                    // next scores first: they need only K(j+1) and free score columns
+                    if (j + 1 < n_tiles && !(ok = issue_s(gj + 1))) break;
+                    // O_t += P_t(j) V(j) once the softmax has written P_t(j)
+                    if (!(ok = mbar_wait(&sm.p_full[t], gj & 1, err))) break;
+                    if (!(ok = mbar_wait(&sm.v_full[s], (gj / NS) & 1, err))) break;
+                    tc_fence_after();
+                    const uint32_t v_addr = smem_u32(sm.v[s]);
 #pragma unroll
-                        for (int kk = 0; kk < BN / 16; kk++) {
-                            const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, 8192, 1024);
-                            mma_f16_ts(tmem + o_col(t), tmem + s_col(t) + kk * 8, b, idesc_o,
-                                       (j > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        if (j + 1 < n_tiles) {
-                            if (t == 0 && !(ok = mbar_wait(&sm.k_full[s2], ((gj + 1) / NS) & 1, err))) break;
-                            tc_fence_after();
-                            issue_s(t, s2);
-                            mma_commit(&sm.s_full[t]);
-                        } else {
-                            mma_commit(&sm.o_final[t]);
-                        }
+                    for (int kk = 0; kk < BN / 16; kk++) {
+                        const uint64_t b = smem_desc_sw128(v_addr + kk * 16 * 128, 8192, 1024);
+                        mma_f16_ts(tmem + o_col(t), tmem + p_col(t) + kk * 8, b, idesc_o,
+                                   (j > 0 || kk > 0) ? 1u : 0u);
                     }
-                    if (ok) mma_commit(&sm.kv_empty[s]);
+                    mma_commit(&sm.pv_done[t]);
+                    mma_commit(&sm.kv_empty[s]);
                 }
                 if (ok) mma_commit(&sm.q_empty[qb]);
                 g += n_tiles;
@@ -229,6 +263,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int row = quarter * 32 + lane;            // TMEM lane = query row in the tile
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         const uint32_t s_addr = tmem + lane_addr + s_col(t);
+        const uint32_t p_addr = tmem + lane_addr + p_col(t);
         const uint32_t o_addr = tmem + lane_addr + o_col(t);
         const float c = 1.4426950408889634f * 0.125f;  // log2(e) / sqrt(64)
         uint32_t g = 0;
@@ -252,27 +287,58 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int i = 0; i < 32; i++) sr[cc * 32 + i] = tmp[i];
                 }
                 tmem_ld_wait();
+                // the scores are in registers: the next S may be written over them
+                tc_fence_before();
+                mbar_arrive(&sm.s_free[t]);
                 const int valid = n_ctx - j * BN;        // keys present in this tile
-                float mx = -INFINITY;
-                if (valid >= BN) {
+                if (valid < BN) {
 #pragma unroll
-                    for (int i = 0; i < BN; i++) mx = fmaxf(mx, __uint_as_float(sr[i]));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < BN; i++) {
-                        const float x = i < valid ? __uint_as_float(sr[i]) : -INFINITY;
-                        sr[i] = __float_as_uint(x);
-                        mx = fmaxf(mx, x);
-                    }
+                    for (int i = 0; i < BN; i++)
+                        if (i >= valid) sr[i] = __float_as_uint(-INFINITY);
                 }
-                const float m_tile = mx * c;
-                if (j == 0) {
-                    m = m_tile;
-                } else if (m_tile > m + 8.0f) {
-                    // O_t of the previous tile is complete: this tile's S was committed
-                    // after the previous PV
-                    const float corr = exp2_approx(m - m_tile);
-                    l *= corr;
+                // row max over 8 independent partial maxima
+                float mxp[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) mxp[k] = __uint_as_float(sr[k]);
+#pragma unroll
+                for (int i = 8; i < BN; i++) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sr[i]));
+#pragma unroll
+                for (int k = 0; k < 4; k++) mxp[k] = fmaxf(mxp[k], mxp[k + 4]);
+                const float m_tile = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])) * c;
+                // the running max is kept stale unless it grows by more than 2^8
+                const bool rescale = j > 0 && m_tile > m + 8.0f;
+                const float m_old = m;
+                if (j == 0 || rescale) m = m_tile;
+                const float2 c2 = make_float2(c, c);
+                const float2 nm2 = make_float2(-m, -m);
+                float2 lp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                make_float2(0.f, 0.f)};
+                uint32_t pk[BN / 2];
+#pragma unroll
+                for (int e = 0; e < BN / 2; e++) {
+                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1])),
+                                                c2, nm2);
+                    // a share of the exponentials can run on the FMA pipe, the rest on MUFU
+                    const float2 pr = ((e & 15) < POLY_PAIRS) ? exp2_poly2(x)
+                                                             : make_float2(exp2_approx(x.x), exp2_approx(x.y));
+                    lp[e & 3] = __fadd2_rn(lp[e & 3], pr);
+                    __nv_bfloat162 h2 = __floats2bfloat162_rn(pr.x, pr.y);
+                    pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+                {
+                    const float2 a = __fadd2_rn(lp[0], lp[1]), b = __fadd2_rn(lp[2], lp[3]);
+                    const float2 s2 = __fadd2_rn(a, b);
+                    const float corr = rescale ? exp2_approx(m_old - m) : 1.f;
+                    l = l * corr + (s2.x + s2.y);
+                }
+                // the previous PV must be done before O is rescaled or P overwritten; the
+                // exponentials above ran while it was in flight
+                if (j > 0) {
+                    if (!(ok = mbar_wait(&sm.pv_done[t], (gj - 1) & 1, err))) break;
+                    tc_fence_after();
+                }
+                if (rescale) {
+                    const float corr = exp2_approx(m_old - m);
 #pragma unroll
                     for (int cc = 0; cc < D / 32; cc++) {
                         uint32_t o[32];
@@ -282,28 +348,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
                         tmem_st32(o_addr + cc * 32, o);
                     }
-                    m = m_tile;
                 }
-                const float neg_m = -m;
 #pragma unroll
-                for (int cc = 0; cc < 4; cc++) {
-                    uint32_t pk[16];
+                for (int cc = 0; cc < BN / 32; cc++) {
+                    uint32_t q16[16];
 #pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const float p0 = exp2_approx(fmaf(__uint_as_float(sr[cc * 32 + 2 * e]), c, neg_m));
-                        const float p1 = exp2_approx(fmaf(__uint_as_float(sr[cc * 32 + 2 * e + 1]), c, neg_m));
-                        l += p0 + p1;
-                        __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-                        pk[e] = *reinterpret_cast<uint32_t*>(&h2);
-                    }
-                    tmem_st16(s_addr + cc * 16, pk);
+                    for (int i = 0; i < 16; i++) q16[i] = pk[cc * 16 + i];
+                    tmem_st16(p_addr + cc * 16, q16);
                 }
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&sm.p_full[t]);
             }
             // ---- epilogue: O / l -> out[win][q0 + row][head * 64 ..]
-            if (!ok || !(ok = mbar_wait(&sm.o_final[t], it & 1, err))) break;
+            if (!ok || !(ok = mbar_wait(&sm.pv_done[t], (g + n_tiles - 1) & 1, err))) break;
             tc_fence_after();
             const float inv = l > 0.f ? 1.0f / l : 0.f;
             const int grow = pair * 2 * BM + t * BM + row;
