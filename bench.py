@@ -16,7 +16,8 @@ Reported (one JSON line from rank 0):
              time, against the measured bf16 peak;
   cpu_baseline  the C restatement of the reference attention (oracle/attn_ref.c) on the
              host cores, rank 0 at N=1;
-  secondary  decode-attention workloads (configs 1, 3, 4) at N=1: tok/s and HBM roofline.
+  secondary  decode-attention workloads (configs 1, 3, 4) at N=1: tok/s and HBM roofline,
+             each decode step (all layers) replayed from a CUDA graph.
 
 `--impl reference` times the reference's CPU attention (the C restatement; the Zig source
 cannot be built here) on the same workload and prints the same line with "impl".
@@ -226,6 +227,25 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------------------------------------
 # our arm
 
+def time_graph(fn, steps, warmup=3):
+    """Capture one call of fn (a whole decode step: every layer's attention) in a CUDA
+    graph and time `steps` replays with CUDA events. Decode steps are launch-bound at these
+    sizes; a serving loop replays a captured step the same way."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    t = time_cuda(graph.replay, steps)
+    del graph
+    return t
+
+
 def time_cuda(fn, steps, stream=None):
     import torch
     s = torch.cuda.Event(enable_timing=True)
@@ -240,7 +260,8 @@ def time_cuda(fn, steps, stream=None):
 
 def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
     """Decode-attention workloads (configs 1, 3, 4) at one GPU: one step = one new token
-    for every item through all layers' attention (f32 K/V, the reference's precision)."""
+    for every item through all layers' attention (f32 K/V, the reference's precision),
+    captured once in a CUDA graph and replayed."""
     import torch
 
     from zwhisper_b200 import ops
@@ -252,10 +273,7 @@ def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
             for _ in range(layers):
                 for sh, q, k, v, o, ws, bs, _ in calls:
                     ops.attention_dev(q, k, v, sh, o, n_batch=B, batch_strides=bs, workspace=ws)
-        for _ in range(warmup):
-            step()
-        torch.cuda.synchronize()
-        t = time_cuda(step, steps)
+        t = time_graph(step, steps, warmup)
         per_step = t / steps
         byts = layers * sum(c[7] for c in calls)
         res.append({"workload": name, "metric": metric, "value": B / per_step, "unit": "tok/s",
@@ -299,10 +317,7 @@ def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
         def step(kts=kts, vs=vs, q=q, o=o, sh=sh, ws=ws, bs=bs, B=B):
             for layer in range(len(kts)):
                 ops.attention_dev(q, kts[layer], vs[layer], sh, o, n_batch=B, batch_strides=bs, workspace=ws)
-        for _ in range(warmup):
-            step()
-        torch.cuda.synchronize()
-        t = time_cuda(step, steps) / steps
+        t = time_graph(step, steps, warmup) / steps
         achieved = layers * byts / t / 1e9
         res.append({"workload": f"{cfg} decode attention, {B} sequences x {layers} layers, n_kv={n_kv} "
                                 f"(mean of the decode), K^T cache n_ctx={n_ctx}",
@@ -437,6 +452,7 @@ def run_kernel_case(args):
     """One kernel on a small case, for ncu captures: `enc_tc` = the tcgen05 encoder kernel
     on 16 small.en windows (one layer, 184 MB of inputs and output, above L2); `decode_qwen`
     = the split-K decode kernel on 16 Qwen2.5-1.5B sequences (n_kv 2256, K^T cache 2560);
+    `decode_qwen05` = the same on 16 Qwen2.5-0.5B sequences (d 64, n_kv 2128);
     `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention."""
     import torch
 
@@ -452,8 +468,9 @@ def run_kernel_case(args):
         def fn():
             ops.enc_attn_bf16(q, k, v, N_HEAD, out)
         work = f"{FLOP_PER_WINDOW_LAYER * B / 1e9:.1f} GFLOP per launch"
-    elif args.kernel_case == "decode_qwen":
-        B, H, Hkv, d, n_ctx, n_kv = 16, 12, 2, 128, 2560, 2256
+    elif args.kernel_case in ("decode_qwen", "decode_qwen05"):
+        B, H, Hkv, d, n_ctx, n_kv = (16, 12, 2, 128, 2560, 2256) if args.kernel_case == "decode_qwen" else \
+            (16, 14, 2, 64, 2560, 2128)
         q = torch.randn(B, H * d, generator=g, device=dev)
         kt = torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev)
         v = torch.randn(B, n_ctx, Hkv * d, generator=g, device=dev)
@@ -494,7 +511,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_whisper"], default=None)
+    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_whisper"], default=None)
     args = ap.parse_args()
     if args.kernel_case:
         run_kernel_case(args)

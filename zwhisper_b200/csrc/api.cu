@@ -102,9 +102,11 @@ Extents extents(const zwg_attn_shape* sh) {
     return e;
 }
 
+// Decode-shaped calls (few query rows per kv head) take the TMA decode kernel; an empty
+// key range (its rows are all zeros) takes the tiled kernel, which writes them.
 bool use_decode(const zwg_attn_shape* sh) {
     const size_t rows = sh->n_q * (sh->n_head / sh->n_head_kv);
-    return zwg::decode_supported(sh->d, rows, sh->kt_stride);
+    return sh->n_kv > 0 && zwg::decode_supported(sh->d, rows, sh->kt_stride);
 }
 
 struct Plan {
@@ -117,11 +119,10 @@ Plan plan_for(const zwg_attn_shape* sh, size_t n_batch, int sm_count) {
     Plan pl{};
     pl.decode = use_decode(sh);
     if (pl.decode) {
-        int ch_tiles = 1;
-        zwg::decode_tma_plan(n_batch, sh->n_head_kv, sh->n_kv, sm_count, &pl.n_splits, &ch_tiles);
-        pl.chunk = ch_tiles * 32;
+        int grid = 1, p_max = 1;
+        zwg::decode_tma_plan(n_batch, sh->n_head_kv, sh->n_kv, sm_count, &grid, &p_max);
         const size_t rows = sh->n_q * (sh->n_head / sh->n_head_kv);
-        pl.ws_bytes = zwg::decode_workspace_floats(n_batch, sh->n_head_kv, rows, pl.n_splits, sh->d) * sizeof(float);
+        pl.ws_bytes = zwg::decode_tma_workspace_bytes(n_batch, sh->n_head_kv, rows, sh->d, p_max);
     }
     return pl;
 }

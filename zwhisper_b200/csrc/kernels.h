@@ -48,10 +48,10 @@ size_t decode_workspace_floats(size_t n_batch, size_t n_head_kv, size_t rows, in
 int decode_f32_launch(const DecodeParams& p, size_t n_batch, cudaStream_t st);
 int decode_combine_launch(const DecodeParams& p, size_t n_batch, cudaStream_t st);
 
-// TMA-fed split-K decode kernel (attn_decode_tma.cu). n_splits = chunks of keys, chunk =
-// keys per chunk (a multiple of 32).
+// TMA-fed, stream-K scheduled decode kernel (attn_decode_tma.cu).
 bool decode_tma_supported(const DecodeParams& p);
-void decode_tma_plan(size_t n_batch, size_t n_head_kv, size_t n_kv, int sm_count, int* n_chunks, int* ch_tiles);
+void decode_tma_plan(size_t n_batch, size_t n_head_kv, size_t n_kv, int sm_count, int* grid, int* p_max);
+size_t decode_tma_workspace_bytes(size_t n_batch, size_t n_head_kv, size_t rows, size_t d, int p_max);
 int decode_tma_launch(const DecodeParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st);
 
 // Encoder tensor-core attention (attn_tc.cu).
