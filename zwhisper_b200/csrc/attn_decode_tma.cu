@@ -6,7 +6,8 @@
 // All R = n_q * group query rows that read a kv head are processed together, so each K/V
 // byte is read once per GQA group. The segments' tiles are laid end to end and every CTA of
 // a persistent grid takes an equal contiguous range of them (stream-K): no wave
-// quantization, whatever the batch. A range can start or end inside a segment; each CTA
+// quantization, whatever the batch (with at least as many segments as CTAs, ranges hold
+// whole segments instead). A range can start or end inside a segment; each CTA
 // merges what it computed for a segment into one partial (max, sum, accumulator), and the
 // last CTA to finish a segment (atomic ticket) merges that segment's pieces and writes the
 // output; a segment held by one CTA is written directly.
@@ -95,6 +96,7 @@ struct Geo {
     int n_t;          // tiles per segment
     int n_segs;
     int p_max;        // pieces per segment the workspace holds
+    int aligned;      // ranges follow segment boundaries (at least as many segments as CTAs)
 };
 
 __device__ __forceinline__ void named_barrier(int id, int threads) {
@@ -108,14 +110,18 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
-// First tile of CTA c and the CTA that owns global tile x, for G CTAs over T tiles.
-__host__ __device__ __forceinline__ long long range_begin(long long c, long long T, long long G) {
-    return c * T / G;
+// First tile of CTA c, for G CTAs over the T tiles of `geo`: equal ranges, or, with at least
+// as many segments as CTAs, equal numbers of whole segments (no segment is then shared, and
+// no CTA pays the merge of a shared segment).
+__host__ __device__ __forceinline__ long long range_begin(long long c, const Geo& geo, long long G) {
+    if (geo.aligned) return (c * geo.n_segs / G) * geo.n_t;
+    return c * geo.total / G;
 }
-__host__ __device__ __forceinline__ int owner_of(long long x, long long T, int G) {
-    long long c = x * G / T;
-    while (c + 1 < G && range_begin(c + 1, T, G) <= x) c++;
-    while (c > 0 && range_begin(c, T, G) > x) c--;
+// The CTA whose range holds tile x.
+__host__ __device__ __forceinline__ int owner_of(long long x, const Geo& geo, int G) {
+    long long c = x * G / geo.total;
+    while (c + 1 < G && range_begin(c + 1, geo, G) <= x) c++;
+    while (c > 0 && range_begin(c, geo, G) > x) c--;
     return (int)c;
 }
 
@@ -131,8 +137,8 @@ __global__ void __launch_bounds__(Cfg<D, RMAX>::THREADS, 1)
     const int G = (int)(p.n_head / p.n_head_kv);
     const int R = (int)p.n_q * G;
     const int n_kv = (int)p.n_kv;
-    const long long t_begin = range_begin(blockIdx.x, geo.total, gridDim.x);
-    const long long t_end = range_begin(blockIdx.x + 1, geo.total, gridDim.x);
+    const long long t_begin = range_begin(blockIdx.x, geo, gridDim.x);
+    const long long t_end = range_begin(blockIdx.x + 1, geo, gridDim.x);
 
     if (threadIdx.x == 0) sm.abort_flag = err ? *(volatile int*)err : 0;
     __syncthreads();
@@ -450,8 +456,8 @@ __global__ void __launch_bounds__(Cfg<D, RMAX>::THREADS, 1)
         }
         named_barrier(1, C::NW * 32);
         if (threadIdx.x == 0) mbar_arrive(&sm.q_empty[qb]);  // q buffer free for the producer
-        const int c_first = owner_of(seg_first, geo.total, gridDim.x);
-        const int c_last = owner_of(seg_first + geo.n_t - 1, geo.total, gridDim.x);
+        const int c_first = owner_of(seg_first, geo, gridDim.x);
+        const int c_last = owner_of(seg_first + geo.n_t - 1, geo, gridDim.x);
         const int n_pieces = c_last - c_first + 1;
         const int piece = blockIdx.x - c_first;
         float* part_seg = p.ws + (size_t)seg * geo.p_max * R * (D + 2);
@@ -621,6 +627,7 @@ static int launch_d(const DecodeParams& p, size_t n_batch, int rmax, int grid, i
     geo.n_segs = (int)(n_batch * p.n_head_kv);
     geo.total = (long long)geo.n_t * geo.n_segs;
     geo.p_max = p_max;
+    geo.aligned = geo.n_segs >= grid ? 1 : 0;
     auto go = [&](auto kern, size_t smem, int threads) -> int {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return -1;
