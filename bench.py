@@ -53,17 +53,24 @@ def load_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def profiled_traffic(name: str):
-    """DRAM bytes per launch from the committed ncu summary, when one exists."""
+def profiled_traffic(name: str, units: float):
+    """DRAM bytes (read + write) of one launch over `units` windows or sequences, from the
+    committed ncu summary of a smaller case of the same kernel, scaled by the units
+    processed (the traffic of these kernels grows in proportion); None without a summary."""
     path = os.path.join(ROOT, "profiles", name)
+    bytes_, per = None, None
     try:
         with open(path) as f:
             for line in f:
                 if line.startswith("dram_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].split()[0])
+                    bytes_ = float(line.split(":", 1)[1].split()[0])
+                elif line.startswith("units_per_launch:"):
+                    per = float(line.split(":", 1)[1].split()[0])
     except OSError:
-        pass
-    return None
+        return None
+    if bytes_ is None or not per:
+        return None
+    return bytes_ * units / per
 
 
 # ---------------------------------------------------------------------------------------------
@@ -319,12 +326,14 @@ def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
                 ops.attention_dev(q, kts[layer], vs[layer], sh, o, n_batch=B, batch_strides=bs, workspace=ws)
         t = time_graph(step, steps, warmup) / steps
         achieved = layers * byts / t / 1e9
+        traffic = profiled_traffic("decode_tma_qwen15_b16.txt", B) if d == 128 else None
         res.append({"workload": f"{cfg} decode attention, {B} sequences x {layers} layers, n_kv={n_kv} "
                                 f"(mean of the decode), K^T cache n_ctx={n_ctx}",
                     "metric": "qwen_decode_attention_tok_per_s", "value": B / t, "unit": "tok/s",
                     "ms_per_step": t * 1e3,
                     "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                                 "frac": achieved / hbm_peak, "traffic": None}})
+                                 "frac": achieved / hbm_peak, "traffic": traffic,
+                                 "bytes_per_launch": byts}})
         del kts, vs
     torch.cuda.empty_cache()
     return res
@@ -437,7 +446,8 @@ def run_ours(args, rank, world, local):
                      "frac": achieved / tc_peak, "peak_source": f"{peak_kind} bf16 (burst)",
                      "kernel": "enc_attn_tc_kernel", "flops_per_launch": flops_launch,
                      "avg_launch_ms": per_launch * 1e3,
-                     "traffic": profiled_traffic("enc_attn_tc_small_en.txt")},
+                     "traffic": profiled_traffic("enc_attn_tc_small_en.txt", nw),
+                     "traffic_note": "ncu DRAM read+write of a 16-window launch scaled to this launch's windows"},
         "gpu_launches": launches,
         "clocks": clk,
     }
