@@ -137,6 +137,8 @@ def dist_setup():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # keep stdout to the one JSON line: no NCCL banner
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
