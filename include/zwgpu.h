@@ -83,14 +83,21 @@ ZWG_API size_t zwg_last_error(char* buf, size_t len);
 /* Number of CUDA devices visible (0 when none). */
 ZWG_API int zwg_device_count(void);
 
-/* Math mode of the calling thread's context for the host-pointer entry points below.
- * ZWG_MATH_F32 (default): f32 operands and accumulation on every shape, the reference's
- * arithmetic. ZWG_MATH_BF16: encoder-shaped calls (self-attention, n_q == n_kv, d == 64,
- * MHA, rows of exactly n_head*64, keys as rows, not causal) convert Q/K/V to bf16 on the
- * device and run the tcgen05 tensor-core kernel with f32 softmax and accumulation; other
- * shapes stay f32. No reference counterpart (the reference computes in f32 only). */
+/* Math mode of the calling thread's context: ZWG_MATH_F32 (0, the default) or an OR of the
+ * tensor-core flags below. No reference counterpart (the reference computes in f32 only).
+ * ZWG_MATH_F32: f32 operands and accumulation on every shape, the reference's arithmetic.
+ * ZWG_MATH_BF16 (host-pointer entry points): encoder-shaped calls (self-attention,
+ *   n_q == n_kv, d == 64, MHA, rows of exactly n_head*64, keys as rows, not causal)
+ *   convert Q/K/V to bf16 on the device and run the tcgen05 kernel with f32 softmax and
+ *   accumulation.
+ * ZWG_MATH_TF32 (host- and device-pointer entry points): prefill-shaped calls over a
+ *   transposed key cache (kt_stride > 0, more than 8 query rows per kv head, d 64 or 128,
+ *   16-byte aligned buffers and strides that are multiples of 4) run the tcgen05 kernel
+ *   with kind::tf32 operands read straight from the f32 caches (10-bit mantissa) and f32
+ *   softmax and accumulation. Other shapes stay f32. */
 #define ZWG_MATH_F32 0
 #define ZWG_MATH_BF16 1
+#define ZWG_MATH_TF32 2
 ZWG_API int zwg_set_math(int mode);
 
 /* ---- drop-in, host pointers, synchronous (parity path) ------------------------------ */
@@ -115,10 +122,10 @@ ZWG_API int zwg_attention_batch_host(const zwg_attn_shape* sh, const zwg_batch* 
  * src/ops.zig:545-556, sizes the reference's scratch the same way: per shape). */
 ZWG_API size_t zwg_attention_workspace(const zwg_attn_shape* sh, const zwg_batch* b);
 
-/* ops.attentionEx over a batch, f32 operands and accumulation, device pointers. Decode-like
- * shapes (n_q * n_head / n_head_kv <= 8 rows per kv head) run the split-K kernel;
- * others run the tiled kernel. `stream` is a cudaStream_t; NULL means the legacy default
- * stream, as in the CUDA runtime. The device entry points below take `stream` the same way. */
+/* ops.attentionEx over a batch, device pointers. Decode-like shapes (n_q * n_head /
+ * n_head_kv <= 8 rows per kv head) run the split-K kernel; others run the tiled f32
+ * kernel, or the tf32 tensor-core kernel for the prefill shapes ZWG_MATH_TF32 covers.
+ * `stream` is a cudaStream_t; NULL means the legacy default stream, as in the CUDA runtime. The device entry points below take `stream` the same way. */
 ZWG_API int zwg_attention_dev(const zwg_attn_shape* sh, const zwg_batch* b, const float* q,
                       const float* k, const float* v, float* out, void* workspace,
                       size_t workspace_bytes, void* stream);

@@ -270,3 +270,25 @@ def test_encoder_tc_vs_f32_oracle(ops, gpu):
     err = np.abs(got - want)
     np.testing.assert_allclose(got, want, atol=BF16_ATOL, rtol=BF16_RTOL)
     assert err.max() < BF16_ATOL
+
+
+def test_encoder_tc_rescale_path(ops, gpu):
+    """Scores that grow key tile by key tile (keys scaled up with their position) make the
+    running max rise by more than 2^8 several times per row, so the kernel's O-rescale
+    branch runs, in some rows of a warp and not in others (rows get different slopes)."""
+    import torch
+    rng = np.random.default_rng(31)
+    B, n_ctx, H = 1, 1500, 2
+    ns = H * 64
+    pos = np.arange(n_ctx, dtype=np.float32)[:, None]
+    slope = (0.5 + rng.random((n_ctx, 1), dtype=np.float32))           # per query row
+    q = (slope + 0.1 * rng.standard_normal((n_ctx, ns), dtype=np.float32)).astype(np.float32)
+    k = (0.25 * pos / 128 + 0.1 * rng.standard_normal((n_ctx, ns), dtype=np.float32)).astype(np.float32)
+    v = rng.standard_normal((n_ctx, ns), dtype=np.float32)
+    tq, tk, tv = (torch.from_numpy(x).to(gpu).to(torch.bfloat16).view(B, n_ctx, ns) for x in (q, k, v))
+    out = ops.enc_attn_bf16(tq, tk, tv, H)
+    ops.sync()
+    got = out.cpu().numpy().reshape(n_ctx, ns)
+    qb, kb, vb = (t.float().cpu().numpy().reshape(1, n_ctx, H, 64).transpose(0, 2, 1, 3) for t in (tq, tk, tv))
+    want = A.attention_batched(qb, kb, vb, causal=False).transpose(0, 2, 1, 3).reshape(n_ctx, ns)
+    np.testing.assert_allclose(got, want, atol=BF16_ATOL, rtol=BF16_RTOL)

@@ -17,6 +17,7 @@ ZWG_ERROR = 2
 ZWG_TIMEOUT = 4
 ZWG_MATH_F32 = 0
 ZWG_MATH_BF16 = 1
+ZWG_MATH_TF32 = 2
 
 c_size = ctypes.c_size_t
 c_ptr = ctypes.c_void_p

@@ -156,7 +156,10 @@ int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q
         p.kt_stride = sh->kt_stride; p.causal = sh->causal ? 1 : 0;
         if (b) { p.q_bs = b->q_batch_stride; p.k_bs = b->k_batch_stride; p.v_bs = b->v_batch_stride; p.out_bs = b->out_batch_stride; }
         if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 3) return fail("f32 buffers must be 4-byte aligned");
-        rc = zwg::flash_f32_launch(p, nb, st);
+        if ((c->math & ZWG_MATH_TF32) && zwg::prefill_tc_supported(p, nb))
+            rc = zwg::prefill_tc_launch(p, nb, c->sm_count, c->err, st);
+        else
+            rc = zwg::flash_f32_launch(p, nb, st);
     }
     if (rc) return cuda_fail("kernel launch", cudaGetLastError());
     return ZWG_OK;
@@ -193,7 +196,7 @@ int zwg_version(void) { return 1; }
 int zwg_set_math(int mode) {
     Ctx* c = cur();
     if (!c) return ZWG_ERROR;
-    if (mode != ZWG_MATH_F32 && mode != ZWG_MATH_BF16) return fail("unknown math mode %d", mode);
+    if (mode & ~(ZWG_MATH_BF16 | ZWG_MATH_TF32)) return fail("unknown math mode %d", mode);
     c->math = mode;
     return ZWG_OK;
 }
@@ -327,7 +330,7 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
         }
         if (e != cudaSuccess) return cuda_fail("host to device copy", e);
         int rc;
-        if (c->math == ZWG_MATH_BF16 && tc_eligible(sh)) {
+        if ((c->math & ZWG_MATH_BF16) && tc_eligible(sh)) {
             const size_t ne = n * dq;  // q, k, v have the same extent here
             if (!c->qh[slot].ensure(ne * 2 + 16) || !c->kh[slot].ensure(ne * 2 + 16) || !c->vh[slot].ensure(ne * 2 + 16))
                 return fail("device staging allocation failed");

@@ -36,6 +36,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace zwg {
 
@@ -549,27 +550,10 @@ __global__ void __launch_bounds__(Cfg<D, RMAX>::THREADS, 1)
 
 // ---- host side -------------------------------------------------------------------------------
 
-typedef CUresult (*EncodeTiledFn2)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn2 encode_fn() {
-    static EncodeTiledFn2 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn2)ptr;
-    });
-    return fn;
-}
-
 // f32 3-d map: dims (inner, rows, batch) with the given row and batch strides in elements.
 static bool map3(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t batch,
                  uint64_t row_stride, uint64_t batch_stride, uint32_t box_inner, uint32_t box_rows) {
-    EncodeTiledFn2 fn = encode_fn();
+    EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return false;
     if (batch < 1) batch = 1;
     if (batch_stride == 0) batch_stride = row_stride * rows;  // a single item: any valid stride

@@ -1,0 +1,510 @@
+// Qwen2 prefill attention on tcgen05 tensor cores: causal grouped-query attention of a
+// chunk of queries over the transposed f32 key cache, kind::tf32 with f32 accumulation.
+//
+// Reference: the Qwen2 attention call src/llm.zig:191-202, which runs ops.attentionEx
+// (src/ops.zig:517-541, 562-590) with kt_stride = n_ctx over cache_kt[n_head_kv][d][n_ctx]
+// and cache_v[n_ctx][n_head_kv*d] (src/llm.zig:27-28, 184-190); query head h reads kv head
+// h / (n_head / n_head_kv) (src/ops.zig:521); query i sees keys j <= n_kv - n_q + i. Prefill
+// runs the prompt in chunks of up to 256 queries (src/llm.zig:257-266).
+//
+// Design. The caches stay in the reference's f32 layout; the tensor cores read them as
+// tf32 (10-bit mantissa, the low 13 bits of each f32 ignored), so no conversion pass or
+// second copy of the cache exists.
+//   - A tile is 128 rows = qn consecutive queries x the `group` query heads of one kv head
+//     (row = query * group + head-in-group), so one K/V tile feeds every head of the group
+//     and the rows of a tile share nearly the same causal limit. Q comes in by one 4-d TMA
+//     box per 32-column chunk ([qn][group][32 floats], 128-byte swizzle): exactly the
+//     K-major A operand.
+//   - K^T tiles are 64 keys x d, loaded as two [d][32 keys] boxes: the MN-major B operand
+//     of S = Q K^T, read straight from the transposed cache. V tiles are 64 keys x d, loaded
+//     as [64 keys][32 columns] boxes: the MN-major B operand of O += P V. An MN-major tf32
+//     operand must be in the 128-byte swizzle with 32-byte atoms (descriptor layout 1, TMA
+//     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B); the 16-byte-atom swizzle that serves K-major
+//     operands gives an MMA that writes zeros.
+//   - TMEM: two 64-column score buffers (S of tile j in buffer j % 2; the softmax writes the
+//     probabilities P back over the scores as tf32, and P is the TMEM A operand of the PV
+//     MMA) and a d-column O accumulator: 256 columns.
+//   - Warp 0: TMA producer (lane 0: Q and K^T, lane 1: V, each with its own 2-stage ring,
+//     so a K^T load never waits behind a V slot). Warp 1: TMEM allocation and the single
+//     MMA-issuing thread, order S0 S1 | PV0 S2 | PV1 S3 ...: the next scores are computed
+//     while the softmax works on the current ones, and S(j+2) overwrites buffer j % 2 only
+//     after PV(j) in issue order (tcgen05.mma from one thread executes in order). Warps
+//     2-5: softmax, one thread per row (TMEM lane), online max in base 2 kept stale unless
+//     it grows by more than 2^8, exp2 on the MUFU, P rounded to tf32 (round to nearest).
+//   - Persistent grid over (sequence, kv head, query tile) items, longest causal range first.
+// Every wait is bounded; a wait that runs out records kErrTimeout, the CTA drains its own
+// copies and MMAs with bounded waits, frees TMEM and returns.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+#include "tmap.cuh"
+
+namespace zwg {
+namespace prefill_tc {
+
+using namespace sm100;
+
+constexpr int BM = 128;                // rows per tile = TMEM lanes
+constexpr int BN = 64;                 // keys per tile
+constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr uint32_t TMEM_COLS = 256;    // S/P buffers 2 x 64 columns, O up to 128 columns
+constexpr uint32_t O_COL = 2 * BN;
+
+template <int D>
+struct Cfg {
+    static constexpr uint32_t Q_CHUNK = BM * 128;           // [128 rows][32 floats]
+    static constexpr uint32_t Q_BYTES = (D / 32) * Q_CHUNK;
+    static constexpr uint32_t K_CHUNK = D * 128;            // [D rows][32 keys]
+    static constexpr uint32_t K_BYTES = 2 * K_CHUNK;
+    static constexpr uint32_t V_CHUNK = BN * 128;           // [64 keys][32 floats]
+    static constexpr uint32_t V_BYTES = (D / 32) * V_CHUNK;
+    // d = 64: 96 KB of tiles, two CTAs per SM; d = 128: 192 KB, one
+    static constexpr int CTAS_PER_SM = D == 64 ? 2 : 1;
+};
+
+template <int D>
+struct Smem {
+    alignas(1024) uint8_t q[Cfg<D>::Q_BYTES];
+    alignas(1024) uint8_t k[2][Cfg<D>::K_BYTES];
+    alignas(1024) uint8_t v[2][Cfg<D>::V_BYTES];
+    uint64_t q_full, q_empty;
+    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t s_full[2], p_full[2], pv_done, drain;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+template <int D>
+constexpr size_t smem_bytes() {
+    return sizeof(Smem<D>) + 1024;  // + alignment slack
+}
+
+struct Args {
+    float* out;
+    size_t out_stride, out_bs;
+    int n_q, n_kv, n_head_kv, group, qn, rows, n_mt, n_items, causal;
+    int* err;
+};
+
+// Items are ordered longest first: query tile n_mt - 1 of every (sequence, kv head), then
+// tile n_mt - 2, ...; with a static stride over a persistent grid this deals the long
+// causal ranges out first.
+__device__ __forceinline__ void item_of(const Args& a, int idx, int& b, int& kh, int& mt) {
+    const int n_bh = a.n_items / a.n_mt;
+    mt = a.n_mt - 1 - idx / n_bh;
+    const int bh = idx % n_bh;
+    b = bh / a.n_head_kv;
+    kh = bh % a.n_head_kv;
+}
+
+// Key tiles a query tile needs: up to the causal limit of its last query.
+__device__ __forceinline__ int item_tiles(const Args& a, int mt) {
+    int keys = a.n_kv;
+    if (a.causal) {
+        const int last_q = min((mt + 1) * a.qn, a.n_q) - 1;
+        keys = min(a.n_kv - a.n_q + last_q + 1, a.n_kv);
+    }
+    return (keys + BN - 1) / BN;
+}
+
+template <int D>
+__global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const Args a) {
+    using C = Cfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    int* err = a.err;
+
+    // after a recorded failure the remaining CTAs do nothing
+    if (threadIdx.x == 0) sm.abort_flag = err ? *(volatile int*)err : 0;
+    __syncthreads();
+    if (sm.abort_flag) return;
+
+    // Rows of the Q tile the loads never write (qn * group < 128 when 128 is not a multiple
+    // of the group) are zeroed once, so their scores stay finite.
+    if (a.rows < BM) {
+        const int n16 = (BM - a.rows) * 8;  // 16-byte words per chunk
+        for (int c = 0; c < D / 32; c++) {
+            uint4* p = reinterpret_cast<uint4*>(sm.q + c * C::Q_CHUNK + a.rows * 128);
+            for (int i = threadIdx.x; i < n16; i += THREADS) p[i] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+    }
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.q_full, 1);
+        mbar_init(&sm.q_empty, 1);
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&sm.k_full[s], 1);
+            mbar_init(&sm.k_empty[s], 1);
+            mbar_init(&sm.v_full[s], 1);
+            mbar_init(&sm.v_empty[s], 1);
+            mbar_init(&sm.s_full[s], 1);
+            mbar_init(&sm.p_full[s], 128);
+        }
+        mbar_init(&sm.pv_done, 1);
+        mbar_init(&sm.drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&sm.tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producers
+        // Each lane counts the loads it issued per barrier, and at exit (normal or not) waits
+        // for the last of them, so no copy is in flight when the CTA releases its memory.
+        if (lane == 0) {
+            prefetch_tmap(&tm_q);
+            prefetch_tmap(&tm_k);
+            uint32_t g = 0, n_q_loads = 0, n_k_loads = 0;  // K^T tile n goes to stage n % 2
+            bool ok = true;
+            for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
+                int b, kh, mt;
+                item_of(a, idx, b, kh, mt);
+                const int n_t = item_tiles(a, mt);
+                if (n_q_loads > 0 && !(ok = mbar_wait(&sm.q_empty, (n_q_loads - 1) & 1, err))) break;
+                mbar_arrive_expect_tx(&sm.q_full, (D / 32) * a.rows * 128);
+                for (int c = 0; c < D / 32; c++)
+                    tma_load_4d(&tm_q, &sm.q_full, sm.q + c * C::Q_CHUNK, c * 32, kh * a.group, mt * a.qn, b);
+                n_q_loads++;
+                for (int j = 0; j < n_t; j++) {
+                    const uint32_t gj = g + j, s = gj & 1;
+                    if (gj >= 2 && !(ok = mbar_wait(&sm.k_empty[s], ((gj >> 1) - 1) & 1, err))) break;
+                    mbar_arrive_expect_tx(&sm.k_full[s], C::K_BYTES);
+                    tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s], j * BN, kh * D, b);
+                    tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s] + C::K_CHUNK, j * BN + 32, kh * D, b);
+                    n_k_loads++;
+                }
+                g += n_t;
+            }
+            if (n_q_loads > 0) mbar_wait_drain(&sm.q_full, (n_q_loads - 1) & 1);
+            if (n_k_loads > 0) mbar_wait_drain(&sm.k_full[0], (((n_k_loads + 1) >> 1) - 1) & 1);
+            if (n_k_loads > 1) mbar_wait_drain(&sm.k_full[1], ((n_k_loads >> 1) - 1) & 1);
+        } else if (lane == 1) {
+            prefetch_tmap(&tm_v);
+            uint32_t g = 0, n_v_loads = 0;
+            bool ok = true;
+            for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
+                int b, kh, mt;
+                item_of(a, idx, b, kh, mt);
+                const int n_t = item_tiles(a, mt);
+                for (int j = 0; j < n_t; j++) {
+                    const uint32_t gj = g + j, s = gj & 1;
+                    if (gj >= 2 && !(ok = mbar_wait(&sm.v_empty[s], ((gj >> 1) - 1) & 1, err))) break;
+                    mbar_arrive_expect_tx(&sm.v_full[s], C::V_BYTES);
+                    for (int c = 0; c < D / 32; c++)
+                        tma_load_3d(&tm_v, &sm.v_full[s], sm.v[s] + c * C::V_CHUNK, kh * D + c * 32, j * BN, b);
+                    n_v_loads++;
+                }
+                g += n_t;
+            }
+            if (n_v_loads > 0) mbar_wait_drain(&sm.v_full[0], (((n_v_loads + 1) >> 1) - 1) & 1);
+            if (n_v_loads > 1) mbar_wait_drain(&sm.v_full[1], ((n_v_loads >> 1) - 1) & 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = idesc_tf32(BM, BN, false, true);
+            constexpr uint32_t idesc_o = idesc_tf32(BM, D, false, true);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x, it++) {
+                int b, kh, mt;
+                item_of(a, idx, b, kh, mt);
+                const int n_t = item_tiles(a, mt);
+                if (!(ok = mbar_wait(&sm.q_full, it & 1, err))) break;
+                const uint32_t q_addr = smem_u32(sm.q);
+                // S(j) = Q K^T(j) into score buffer (g + j) % 2
+                auto issue_s = [&](int j) -> bool {
+                    const uint32_t gj = g + j, s = gj & 1;
+                    if (!mbar_wait(&sm.k_full[s], (gj >> 1) & 1, err)) return false;
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(sm.k[s]);
+#pragma unroll
+                    for (int kk = 0; kk < D / 8; kk++) {
+                        const uint64_t ad = smem_desc_sw128(q_addr + (kk >> 2) * C::Q_CHUNK + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128_32b(k_addr + kk * 1024, C::K_CHUNK, 512);
+                        mma_tf32_ss(tmem + s * BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(&sm.k_empty[s]);
+                    mma_commit(&sm.s_full[s]);
+                    if (j == n_t - 1) mma_commit(&sm.q_empty);  // the next item's Q may load
+                    return true;
+                };
+                ok = issue_s(0);
+                if (ok && n_t > 1) ok = issue_s(1);
+                for (int j = 0; ok && j < n_t; j++) {
+                    const uint32_t gj = g + j, s = gj & 1;
+                    if (!(ok = mbar_wait(&sm.p_full[s], (gj >> 1) & 1, err))) break;
+                    if (!(ok = mbar_wait(&sm.v_full[s], (gj >> 1) & 1, err))) break;
+                    tc_fence_after();
+                    const uint32_t v_addr = smem_u32(sm.v[s]);
+#pragma unroll
+                    for (int kk = 0; kk < BN / 8; kk++) {
+                        const uint64_t bd = smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512);
+                        mma_tf32_ts(tmem + O_COL, tmem + s * BN + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&sm.pv_done);
+                    mma_commit(&sm.v_empty[s]);
+                    if (j + 2 < n_t && !(ok = issue_s(j + 2))) break;
+                }
+                g += n_t;
+            }
+            // every MMA issued so far completes before TMEM is released
+            mma_commit(&sm.drain);
+            mbar_wait_drain(&sm.drain, 0);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax warps 2-5
+        const int quarter = warp & 3;                  // TMEM lanes this warp may access
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        const float c = 1.4426950408889634f * (D == 64 ? 0.125f : 0.08838834764831845f);  // log2(e)/sqrt(d)
+        const int il = row / a.group, hg = row - il * a.group;
+        uint32_t g = 0;
+        bool ok = true;
+        for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
+            int b, kh, mt;
+            item_of(a, idx, b, kh, mt);
+            const int n_t = item_tiles(a, mt);
+            const int i = mt * a.qn + il;
+            const bool valid = row < a.rows && i < a.n_q;
+            const int lim = a.causal ? min(a.n_kv - a.n_q + min(i, a.n_q - 1) + 1, a.n_kv) : a.n_kv;
+            float m = 0.f, l = 0.f;
+            for (int j = 0; j < n_t; j++) {
+                const uint32_t gj = g + j, s = gj & 1;
+                if (!(ok = mbar_wait_warp(&sm.s_full[s], (gj >> 1) & 1, err))) break;
+                tc_fence_after();
+                const uint32_t s_addr = tmem + lane_addr + s * BN;
+                uint32_t sr[64];
+                {
+                    uint32_t x[32], y[32];
+                    tmem_ld32(s_addr, x);
+                    tmem_ld32(s_addr + 32, y);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        sr[e] = x[e];
+                        sr[32 + e] = y[e];
+                    }
+                }
+                const int valid_keys = lim - j * BN;
+                if (valid_keys < BN) {
+#pragma unroll
+                    for (int e = 0; e < 64; e++)
+                        if (e >= valid_keys) sr[e] = __float_as_uint(-INFINITY);
+                }
+                float mx[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) mx[e] = __uint_as_float(sr[e]);
+#pragma unroll
+                for (int e = 8; e < 64; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sr[e]));
+#pragma unroll
+                for (int e = 0; e < 4; e++) mx[e] = fmaxf(mx[e], mx[e + 4]);
+                const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;
+                // tile 0 always holds key 0, which every row sees: m_tile is finite there
+                float corr = 1.f;
+                bool rescale = false;
+                if (j == 0) {
+                    m = m_tile;
+                } else if (m_tile > m + 8.f) {
+                    corr = exp2_approx(m - m_tile);
+                    m = m_tile;
+                    rescale = true;
+                }
+                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int e = 0; e < 64; e++) {
+                    const uint32_t p = to_tf32(exp2_approx(fmaf(__uint_as_float(sr[e]), c, -m)));
+                    ls[e & 3] += __uint_as_float(p);
+                    sr[e] = p;
+                }
+                l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+                // the previous PV must be done before O is rescaled
+                if (j > 0) {
+                    if (!(ok = mbar_wait_warp(&sm.pv_done, (gj - 1) & 1, err))) break;
+                    tc_fence_after();
+                }
+                // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows
+                // must (corr is 1 in the others)
+                if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+                    for (int cc = 0; cc < D / 32; cc++) {
+                        uint32_t o[32];
+                        tmem_ld32(tmem + lane_addr + O_COL + cc * 32, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                        tmem_st32(tmem + lane_addr + O_COL + cc * 32, o);
+                    }
+                }
+                {
+                    uint32_t x[32], y[32];
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        x[e] = sr[e];
+                        y[e] = sr[32 + e];
+                    }
+                    tmem_st32(s_addr, x);
+                    tmem_st32(s_addr + 32, y);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&sm.p_full[s]);
+            }
+            if (!ok) break;
+            // ---- epilogue: O / l -> out[b][i][(kh * group + hg) * D ..]
+            if (!(ok = mbar_wait_warp(&sm.pv_done, (g + n_t - 1) & 1, err))) break;
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            float* orow = a.out + (size_t)b * a.out_bs + (size_t)(valid ? i : 0) * a.out_stride +
+                          (size_t)(kh * a.group + hg) * D;
+#pragma unroll
+            for (int cc = 0; cc < D / 32; cc++) {
+                uint32_t o[32];
+                tmem_ld32(tmem + lane_addr + O_COL + cc * 32, o);
+                tmem_ld_wait();
+                if (valid) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4) {
+                        const float4 v4 = make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                                                      __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+                        *reinterpret_cast<float4*>(orow + cc * 32 + e) = v4;
+                    }
+                }
+            }
+            tc_fence_before();
+            g += n_t;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+}  // namespace prefill_tc
+
+// ---- host side -------------------------------------------------------------------------------
+
+namespace {
+
+bool encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+            const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return false;
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    return fn(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D>
+int launch_d(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st) {
+    using namespace prefill_tc;
+    const int group = (int)(p.n_head / p.n_head_kv);
+    const int qn = BM / group;
+    Args a{};
+    a.out = p.out;
+    a.out_stride = p.out_stride;
+    a.out_bs = p.out_bs;
+    a.n_q = (int)p.n_q;
+    a.n_kv = (int)p.n_kv;
+    a.n_head_kv = (int)p.n_head_kv;
+    a.group = group;
+    a.qn = qn;
+    a.rows = qn * group;
+    a.n_mt = (int)((p.n_q + qn - 1) / qn);
+    a.causal = p.causal;
+    a.err = err;
+    const long long n_items = (long long)n_batch * (long long)p.n_head_kv * a.n_mt;
+    if (n_items <= 0 || n_items >= (1ll << 31)) return -1;
+    a.n_items = (int)n_items;
+
+    // a single item: any valid batch stride
+    const size_t q_bs = n_batch > 1 ? p.q_bs : p.n_q * p.q_stride;
+    const size_t k_bs = n_batch > 1 ? p.k_bs : p.n_head_kv * p.d * p.kt_stride;
+    const size_t v_bs = n_batch > 1 ? p.v_bs : p.n_kv * p.kv_stride;
+    CUtensorMap mq, mk, mv;
+    {
+        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)p.n_head, (cuuint64_t)p.n_q, (cuuint64_t)n_batch};
+        cuuint64_t strides[3] = {(cuuint64_t)D * 4, (cuuint64_t)p.q_stride * 4, (cuuint64_t)q_bs * 4};
+        cuuint32_t box[4] = {32, (cuuint32_t)group, (cuuint32_t)qn, 1};
+        if (!encode(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return -1;
+    }
+    {
+        cuuint64_t dims[3] = {(cuuint64_t)p.n_kv, (cuuint64_t)(p.n_head_kv * D), (cuuint64_t)n_batch};
+        cuuint64_t strides[2] = {(cuuint64_t)p.kt_stride * 4, (cuuint64_t)k_bs * 4};
+        cuuint32_t box[3] = {32, (cuuint32_t)D, 1};
+        if (!encode(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.k, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+            return -1;
+    }
+    {
+        cuuint64_t dims[3] = {(cuuint64_t)(p.n_head_kv * D), (cuuint64_t)p.n_kv, (cuuint64_t)n_batch};
+        cuuint64_t strides[2] = {(cuuint64_t)p.kv_stride * 4, (cuuint64_t)v_bs * 4};
+        cuuint32_t box[3] = {32, (cuuint32_t)BN, 1};
+        if (!encode(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.v, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+            return -1;
+    }
+
+    static std::mutex mu;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[dev]) {
+            if (cudaFuncSetAttribute(prefill_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_bytes<D>()) != cudaSuccess)
+                return -1;
+            attr_set[dev] = true;
+        }
+    }
+    const int slots = (sm_count > 0 ? sm_count : 148) * Cfg<D>::CTAS_PER_SM;
+    const int grid = (int)std::min<long long>(n_items, slots);
+    prefill_tc_kernel<D><<<grid, THREADS, smem_bytes<D>(), st>>>(mq, mk, mv, a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace
+
+bool prefill_tc_supported(const FlashParams& p, size_t n_batch) {
+    if (!(p.d == 64 || p.d == 128)) return false;
+    if (p.kt_stride == 0 || p.n_head_kv == 0 || p.n_head % p.n_head_kv) return false;
+    const size_t group = p.n_head / p.n_head_kv;
+    if (group == 0 || group > (size_t)prefill_tc::BM) return false;
+    if (p.n_q == 0 || p.n_kv == 0 || (p.causal && p.n_kv < p.n_q)) return false;
+    if (p.n_q >= (1u << 30) || p.n_kv >= (1u << 30) || n_batch == 0 || n_batch >= (1u << 30)) return false;
+    // TMA: 16-byte aligned bases and strides; float4 output stores
+    if (((uintptr_t)p.q | (uintptr_t)p.k | (uintptr_t)p.v | (uintptr_t)p.out) & 15) return false;
+    if (p.q_stride % 4 || p.kv_stride % 4 || p.kt_stride % 4 || p.out_stride % 4) return false;
+    if (n_batch > 1 && (p.q_bs % 4 || p.k_bs % 4 || p.v_bs % 4 || p.out_bs % 4)) return false;
+    return true;
+}
+
+int prefill_tc_launch(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st) {
+    if (!prefill_tc_supported(p, n_batch)) return -1;
+    return p.d == 64 ? launch_d<64>(p, n_batch, sm_count, err, st) : launch_d<128>(p, n_batch, sm_count, err, st);
+}
+
+}  // namespace zwg

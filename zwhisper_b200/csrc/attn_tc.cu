@@ -44,6 +44,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace zwg {
 
@@ -276,7 +277,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             float l = 0.f;
             for (int j = 0; j < n_tiles; j++) {
                 const uint32_t gj = g + j;
-                if (!(ok = mbar_wait(&sm.s_full[t], gj & 1, err))) break;
+                if (!(ok = mbar_wait_warp(&sm.s_full[t], gj & 1, err))) break;
                 tc_fence_after();
                 uint32_t sr[BN];
 #pragma unroll
@@ -334,11 +335,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // the previous PV must be done before O is rescaled or P overwritten; the
                 // exponentials above ran while it was in flight
                 if (j > 0) {
-                    if (!(ok = mbar_wait(&sm.pv_done[t], (gj - 1) & 1, err))) break;
+                    if (!(ok = mbar_wait_warp(&sm.pv_done[t], (gj - 1) & 1, err))) break;
                     tc_fence_after();
                 }
-                if (rescale) {
-                    const float corr = exp2_approx(m_old - m);
+                // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows
+                // must (corr is 1 in the others)
+                if (__any_sync(0xffffffffu, rescale)) {
+                    const float corr = rescale ? exp2_approx(m_old - m) : 1.f;
 #pragma unroll
                     for (int cc = 0; cc < D / 32; cc++) {
                         uint32_t o[32];
@@ -361,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mbar_arrive(&sm.p_full[t]);
             }
             // ---- epilogue: O / l -> out[win][q0 + row][head * 64 ..]
-            if (!ok || !(ok = mbar_wait(&sm.pv_done[t], (g + n_tiles - 1) & 1, err))) break;
+            if (!ok || !(ok = mbar_wait_warp(&sm.pv_done[t], (g + n_tiles - 1) & 1, err))) break;
             tc_fence_after();
             const float inv = l > 0.f ? 1.0f / l : 0.f;
             const int grow = pair * 2 * BM + t * BM + row;
@@ -397,26 +400,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---- host side -----------------------------------------------------------------------------
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn get_encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    });
-    return fn;
-}
-
 // 3-d map over a bf16 [n_batch][n_ctx][n_head*64] tensor with [1][128][64] boxes.
 static bool make_map(CUtensorMap* map, const void* base, int n_batch, int n_ctx, int n_head) {
-    EncodeTiledFn fn = get_encode_fn();
+    EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return false;
     const cuuint64_t row = (cuuint64_t)n_head * 64;
     cuuint64_t dims[3] = {row, (cuuint64_t)n_ctx, (cuuint64_t)n_batch};

@@ -65,6 +65,11 @@ struct EncTcParams {
 };
 int enc_tc_launch(const EncTcParams& p, cudaStream_t st);
 
+// Prefill over a transposed key cache on tcgen05 tensor cores, kind::tf32
+// (attn_prefill_tc.cu): d 64 or 128, group <= 128, TMA-aligned buffers and strides.
+bool prefill_tc_supported(const FlashParams& p, size_t n_batch);
+int prefill_tc_launch(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st);
+
 // Elementwise helpers (misc.cu).
 int f32_to_bf16_launch(const float* x, uint16_t* y, size_t n, cudaStream_t st);
 

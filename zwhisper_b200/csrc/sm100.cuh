@@ -58,6 +58,24 @@ ZWG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
     return false;
 }
 
+// mbar_wait for code that all 32 lanes of a warp run together (around .sync.aligned
+// tcgen05 loads and stores): the lanes agree on the outcome, so a wait that gives up in
+// one lane sends the whole warp to the teardown.
+ZWG_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, err));
+}
+
+// Bounded wait used only while tearing a CTA down after an error: it waits for copies and
+// MMAs this CTA issued itself (which complete on their own), ignores the error word, and
+// gives up after about a second.
+ZWG_DEV bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 20); i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(1000);
+    }
+    return false;
+}
+
 // ---- TMA ---------------------------------------------------------------------------------
 
 ZWG_DEV void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2) {
@@ -65,6 +83,14 @@ ZWG_DEV void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int c
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
         "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+ZWG_DEV void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
 
@@ -108,6 +134,34 @@ ZWG_DEV void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint3
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
         : "memory");
+}
+
+// D(tmem) (+)= A(smem desc) . B(smem desc), kind::tf32 (32-bit containers, f32 accumulate)
+ZWG_DEV void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// D(tmem) (+)= A(tmem) . B(smem desc), kind::tf32: row m of A in lane m, one element per
+// 32-bit column.
+ZWG_DEV void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// f32 -> tf32 (round to nearest, ties away from zero), kept in a 32-bit container.
+ZWG_DEV uint32_t to_tf32(float x) {
+    uint32_t y;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(y) : "f"(x));
+    return y;
 }
 
 // Arrive once on `bar` when all tcgen05 operations issued so far by this thread complete.
@@ -181,6 +235,22 @@ ZWG_DEV uint64_t smem_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_
     return d;
 }
 
+// Shared-memory descriptor for an MN-major operand of 32-bit elements (kind::tf32) in the
+// 128-byte swizzle with 32-byte atoms (layout 1; what a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes): each K row is 128 bytes of 32 MN-consecutive
+// elements whose 32-byte chunk c sits at c ^ (row % 4). SBO = distance between 4-row groups
+// along K (512 B for dense rows), LBO = distance between 32-element blocks along M/N. The
+// ordinary 128-byte swizzle (layout 2) with an MN-major tf32 operand yields zeros.
+ZWG_DEV uint64_t smem_desc_sw128_32b(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)1 << 61;
+    return d;
+}
+
 // Instruction descriptor for kind::f16 with f32 accumulation.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 = f16, 1 = bf16),
 //   bit 15 A major, bit 16 B major (0 = K-major, 1 = MN-major), bits 17-22 N >> 3,
@@ -188,6 +258,13 @@ ZWG_DEV uint64_t smem_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a_mn, bool b_mn) {
     return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
            ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor for kind::tf32 (A and B format 2) with f32 accumulation; same
+// fields as idesc_f16.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace sm100

@@ -126,10 +126,14 @@ def attention_batch_host(q, k, v, sh: AttnShape, n_batch: int, out=None, device:
 
 
 def set_math(mode: str, device: int = 0) -> None:
-    """"f32" (default, the reference's arithmetic) or "bf16" (encoder-shaped host calls on
-    the tcgen05 kernel) for the calling thread's context (zwg_set_math)."""
+    """Math mode of the calling thread's context (zwg_set_math): "f32" (default, the
+    reference's arithmetic), "bf16" (encoder-shaped host calls on the bf16 tcgen05 kernel),
+    "tf32" (prefill calls over a transposed key cache on the tf32 tcgen05 kernel), or
+    "bf16+tf32" for both."""
     _lib.ensure_init(device)
-    code = {"f32": _lib.ZWG_MATH_F32, "bf16": _lib.ZWG_MATH_BF16}[mode]
+    code = 0
+    for part in mode.split("+"):
+        code |= {"f32": _lib.ZWG_MATH_F32, "bf16": _lib.ZWG_MATH_BF16, "tf32": _lib.ZWG_MATH_TF32}[part]
     _lib.check(_lib.load().zwg_set_math(code))
 
 
