@@ -341,6 +341,59 @@ def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
     return res
 
 
+def secondary_prefill(dev, tc_peak, peak_kind, steps=2, warmup=1):
+    """Qwen2 prefill attention (configs 3 and 4) at one GPU: one step = the whole 2000-token
+    prompt in 256-token causal chunks (src/llm.zig:257-266) through every layer, for every
+    sequence, on the tf32 tensor-core kernel over f32 K^T/V caches (distinct per layer)."""
+    import torch
+
+    from zwhisper_b200 import ops
+    res = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    ops.set_math("tf32", dev.index or 0)
+    try:
+        for cfg, B, layers, H, Hkv, d in (("configs[3] Qwen2.5-0.5B", 16, 24, 14, 2, 64),
+                                          ("configs[4] Qwen2.5-1.5B", 64, 28, 12, 2, 128)):
+            n_prompt, chunk, n_ctx = 2000, 256, 2048
+            kvw = Hkv * d
+            kts = [torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev) for _ in range(layers)]
+            vs = [torch.randn(B, n_ctx, kvw, generator=g, device=dev) for _ in range(layers)]
+            chunks = []
+            for p0 in range(0, n_prompt, chunk):
+                n_q = min(chunk, n_prompt - p0)
+                q = torch.randn(B, n_q, H * d, generator=g, device=dev)
+                sh = ops.AttnShape(n_q, p0 + n_q, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
+                chunks.append((sh, q, torch.empty_like(q), (n_q * H * d, Hkv * d * n_ctx, n_ctx * kvw, n_q * H * d)))
+
+            def step(kts=kts, vs=vs, chunks=chunks, B=B):
+                for layer in range(len(kts)):
+                    for sh, q, o, bs in chunks:
+                        ops.attention_dev(q, kts[layer], vs[layer], sh, o, n_batch=B, batch_strides=bs)
+            for _ in range(warmup):
+                step()
+            torch.cuda.synchronize()
+            t = time_cuda(step, steps) / steps
+            ops.sync()
+            pairs = n_prompt * (n_prompt + 1) // 2
+            flops = 4 * d * H * layers * pairs * B
+            peak = tc_peak / 2
+            res.append({"workload": f"{cfg} prefill attention: {n_prompt}-token prompt in {chunk}-token causal "
+                                    f"chunks, {B} sequences x {layers} layers, tf32 tensor cores over f32 caches",
+                        "metric": "qwen_prefill_attention_tok_per_s", "value": B * n_prompt / t, "unit": "tok/s",
+                        "ms_per_step": t * 1e3,
+                        "roofline": {"bound": "tensor", "achieved": flops / t / 1e12, "peak": peak,
+                                     "unit": "TFLOP/s", "frac": flops / t / 1e12 / peak,
+                                     "peak_source": f"{peak_kind} bf16 (burst) / 2: dense tf32 runs at half the "
+                                                    "bf16 rate", "traffic": None,
+                                     "flops_per_step": flops}})
+            del kts, vs, chunks
+            torch.cuda.empty_cache()
+    finally:
+        ops.set_math("f32", dev.index or 0)
+    return res
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -424,7 +477,7 @@ def run_ours(args, rank, world, local):
     secondary = None
     cpu = None
     if world == 1 and not args.no_secondary:
-        secondary = secondary_decode(dev, hbm_peak)
+        secondary = secondary_decode(dev, hbm_peak) + secondary_prefill(dev, tc_peak, peak_kind)
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_windows_per_s(min_seconds=args.cpu_seconds)
 
@@ -465,7 +518,9 @@ def run_kernel_case(args):
     on 16 small.en windows (one layer, 184 MB of inputs and output, above L2); `decode_qwen`
     = the split-K decode kernel on 16 Qwen2.5-1.5B sequences (n_kv 2256, K^T cache 2560);
     `decode_qwen05` = the same on 16 Qwen2.5-0.5B sequences (d 64, n_kv 2128);
-    `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention."""
+    `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention;
+    `prefill_qwen` = the tf32 prefill kernel on the last 208-query chunk of a 2000-token
+    prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2)."""
     import torch
 
     from zwhisper_b200 import ops
@@ -493,6 +548,19 @@ def run_kernel_case(args):
         def fn():
             ops.attention_dev(q, kt, v, sh, out, n_batch=B, workspace=ws)
         work = f"{B * n_kv * Hkv * d * 8 / 1e6:.1f} MB of K/V per launch"
+    elif args.kernel_case == "prefill_qwen":
+        B, H, Hkv, d, n_ctx, n_past, n_q = 64, 12, 2, 128, 2048, 1792, 208
+        q = torch.randn(B, n_q, H * d, generator=g, device=dev)
+        kt = torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev)
+        v = torch.randn(B, n_ctx, Hkv * d, generator=g, device=dev)
+        out = torch.empty_like(q)
+        sh = ops.AttnShape(n_q, n_past + n_q, H, Hkv, d, H * d, Hkv * d, H * d, True, n_ctx)
+        ops.set_math("tf32")
+
+        def fn():
+            ops.attention_dev(q, kt, v, sh, out, n_batch=B)
+        pairs = sum(n_past + i + 1 for i in range(n_q))
+        work = f"{4 * d * H * pairs * B / 1e9:.1f} GFLOP per launch"
     else:
         B, ns = 32, 512
         q = torch.randn(B, 1, ns, generator=g, device=dev)
@@ -523,7 +591,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_whisper"], default=None)
+    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_whisper", "prefill_qwen"],
+                    default=None)
     args = ap.parse_args()
     if args.kernel_case:
         run_kernel_case(args)

@@ -31,7 +31,7 @@
 //     after PV(j) in issue order (tcgen05.mma from one thread executes in order). Warps
 //     2-5: softmax, one thread per row (TMEM lane), online max in base 2 kept stale unless
 //     it grows by more than 2^8, exp2 on the MUFU, P rounded to tf32 (round to nearest).
-//   - Persistent grid over (sequence, kv head, query tile) items, longest causal range first.
+//   - Persistent grid over (sequence, kv head, query tile) items, a pair's tiles adjacent.
 // Every wait is bounded; a wait that runs out records kErrTimeout, the CTA drains its own
 // copies and MMAs with bounded waits, frees TMEM and returns.
 #include <cuda.h>
@@ -91,15 +91,17 @@ struct Args {
     int* err;
 };
 
-// Items are ordered longest first: query tile n_mt - 1 of every (sequence, kv head), then
-// tile n_mt - 2, ...; with a static stride over a persistent grid this deals the long
-// causal ranges out first.
+// Consecutive items are the query tiles of one (sequence, kv head), longest causal range
+// first: the CTAs running at the same time share that pair's K^T/V tiles through L2, so
+// each K/V byte comes from DRAM about once. (Ordering by query tile first made every tile
+// re-read its pair's 2 MB of K/V from DRAM: 2.3 GB of DRAM reads for 0.35 GB of inputs in
+// a 64-sequence launch.) The static stride over the persistent grid deals each CTA a mix
+// of long and short tiles.
 __device__ __forceinline__ void item_of(const Args& a, int idx, int& b, int& kh, int& mt) {
-    const int n_bh = a.n_items / a.n_mt;
-    mt = a.n_mt - 1 - idx / n_bh;
-    const int bh = idx % n_bh;
+    const int bh = idx / a.n_mt;
+    mt = a.n_mt - 1 - (idx - bh * a.n_mt);
     b = bh / a.n_head_kv;
-    kh = bh % a.n_head_kv;
+    kh = bh - b * a.n_head_kv;
 }
 
 // Key tiles a query tile needs: up to the causal limit of its last query.
