@@ -167,6 +167,57 @@ ZWG_API int zwg_rope_kt_append(size_t n_batch, size_t n, size_t n_past, size_t n
                        const float* sin_tab, size_t q_bstride, size_t kv_bstride,
                        size_t cache_bstride, void* stream);
 
+/* ---- library-owned device state (the device-resident API) ---------------------------
+ * The reference keeps its attention buffers inside the decoder and the LLM
+ * (src/decoder.zig:39-42, 127-130; src/llm.zig:27-28, 124-137). These states hold the
+ * same buffers on the device for n_batch windows or sequences, so a GPU-resident caller
+ * passes only the new rows and the queries. States are created on the calling thread's
+ * device (zwg_init) and used from threads bound to that device; calls are stream ordered
+ * (`stream` as above). q, k_new, v_new, out and the LLM's q/k/v are device pointers;
+ * zwg_cross_kv_set also takes host pointers (pinned for an asynchronous copy). Buffers
+ * are batched: item b of q/out/k_new/v_new starts at b times one item's size. */
+
+/* Whisper decoder: per layer a self K/V cache [n_batch][n_text_ctx][n_state] and cross
+ * K/V [n_batch][n_audio_ctx][n_state]. */
+typedef struct zwg_dec_state zwg_dec_state;
+ZWG_API int zwg_dec_state_create(size_t n_layer, size_t n_batch, size_t n_state, size_t n_head,
+                                 size_t n_text_ctx, size_t n_audio_ctx, zwg_dec_state** out);
+ZWG_API int zwg_dec_state_destroy(zwg_dec_state* st);
+/* Device pointers of one layer's buffers (any output may be NULL). */
+ZWG_API int zwg_dec_state_cache(const zwg_dec_state* st, size_t layer, float** self_k, float** self_v,
+                                float** cross_k, float** cross_v);
+/* setAudio (src/decoder.zig:150-156) for one window and layer: k, v [n_audio_ctx][n_state]. */
+ZWG_API int zwg_cross_kv_set(zwg_dec_state* st, size_t layer, size_t window, const float* k,
+                             const float* v, void* stream);
+/* One decoder step's attention for every window (src/decoder.zig:179-191), q and out
+ * [n_batch][n][n_state]. ZWG_DEC_SELF: k_new, v_new [n_batch][n][n_state] are written at
+ * rows n_past.. of the layer's cache, then causal attention over n_past + n keys.
+ * ZWG_DEC_CROSS: attention over the window's cross K/V (k_new, v_new, n_past unused). */
+#define ZWG_DEC_SELF 0
+#define ZWG_DEC_CROSS 1
+ZWG_API int zwg_dec_step_attn(zwg_dec_state* st, size_t layer, int kind, const float* q, const float* k_new,
+                              const float* v_new, size_t n_past, size_t n, float* out, void* stream);
+
+/* Qwen2 LLM: per layer cache_kt [n_batch][n_head_kv][d][n_ctx] (zeroed) and cache_v
+ * [n_batch][n_ctx][n_head_kv*d]; RoPE tables [n_ctx][d/2] computed in f64 and cast to f32
+ * with base rope_base (src/llm.zig:128-137). */
+typedef struct zwg_llm_state zwg_llm_state;
+ZWG_API int zwg_llm_state_create(size_t n_layer, size_t n_batch, size_t n_head, size_t n_head_kv, size_t d,
+                                 size_t n_ctx, double rope_base, zwg_llm_state** out);
+ZWG_API int zwg_llm_state_destroy(zwg_llm_state* st);
+ZWG_API int zwg_llm_state_cache(const zwg_llm_state* st, size_t layer, float** cache_kt, float** cache_v);
+/* RoPE and cache append (src/llm.zig:180-190): q [n_batch][n][n_head*d] rotated in place;
+ * k, v [n_batch][n][n_head_kv*d] rotated (k) and written at positions n_past.. */
+ZWG_API int zwg_llm_append_rope(zwg_llm_state* st, size_t layer, float* q, const float* k, const float* v,
+                                size_t n_past, size_t n, void* stream);
+/* Causal GQA attention of q [n_batch][n][n_head*d] over the layer's cache, n_kv = n_past + n
+ * (src/llm.zig:191-202); out as q. The context's math mode applies (ZWG_MATH_TF32 runs
+ * prefill chunks on tensor cores). _decode is the n = 1 call. */
+ZWG_API int zwg_llm_attn_prefill(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, size_t n,
+                                 float* out, void* stream);
+ZWG_API int zwg_llm_attn_decode(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, float* out,
+                                void* stream);
+
 /* Synchronize the device and report the context's device-side error word, if set. */
 ZWG_API int zwg_sync(void);
 

@@ -64,7 +64,24 @@ SIGNATURES = {
                                           c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_size, c_size, c_ptr]),
     "zwg_sync": (ctypes.c_int, []),
     "zwg_set_math": (ctypes.c_int, [ctypes.c_int]),
+    "zwg_dec_state_create": (ctypes.c_int, [c_size, c_size, c_size, c_size, c_size, c_size, ctypes.POINTER(c_ptr)]),
+    "zwg_dec_state_destroy": (ctypes.c_int, [c_ptr]),
+    "zwg_dec_state_cache": (ctypes.c_int, [c_ptr, c_size, ctypes.POINTER(c_ptr), ctypes.POINTER(c_ptr),
+                                           ctypes.POINTER(c_ptr), ctypes.POINTER(c_ptr)]),
+    "zwg_cross_kv_set": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr]),
+    "zwg_dec_step_attn": (ctypes.c_int, [c_ptr, c_size, ctypes.c_int, c_ptr, c_ptr, c_ptr, c_size, c_size, c_ptr,
+                                         c_ptr]),
+    "zwg_llm_state_create": (ctypes.c_int, [c_size, c_size, c_size, c_size, c_size, c_size, ctypes.c_double,
+                                            ctypes.POINTER(c_ptr)]),
+    "zwg_llm_state_destroy": (ctypes.c_int, [c_ptr]),
+    "zwg_llm_state_cache": (ctypes.c_int, [c_ptr, c_size, ctypes.POINTER(c_ptr), ctypes.POINTER(c_ptr)]),
+    "zwg_llm_append_rope": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_ptr, c_ptr, c_size, c_size, c_ptr]),
+    "zwg_llm_attn_prefill": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_size, c_size, c_ptr, c_ptr]),
+    "zwg_llm_attn_decode": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_size, c_ptr, c_ptr]),
 }
+
+ZWG_DEC_SELF = 0
+ZWG_DEC_CROSS = 1
 
 _lib = None
 _lock = threading.Lock()

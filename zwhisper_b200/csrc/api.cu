@@ -4,6 +4,7 @@
 #include "../../include/zwgpu.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "api_internal.h"
 
 #include <cuda_runtime.h>
 
@@ -14,38 +15,8 @@
 #include <mutex>
 #include <string>
 
-namespace {
-
-struct DevBuf {
-    void* ptr = nullptr;
-    size_t cap = 0;
-    bool ensure(size_t bytes) {
-        if (bytes <= cap) return true;
-        if (ptr) cudaFree(ptr);
-        ptr = nullptr;
-        cap = 0;
-        size_t want = std::max(bytes, (size_t)256);
-        if (cudaMalloc(&ptr, want) != cudaSuccess) return false;
-        cap = want;
-        return true;
-    }
-    void release() {
-        if (ptr) cudaFree(ptr);
-        ptr = nullptr;
-        cap = 0;
-    }
-};
-
-struct Ctx {
-    int device = -1;
-    int sm_count = 148;
-    cudaStream_t stream = nullptr;
-    cudaStream_t side = nullptr;  // second stream for pipelined host batches
-    int* err = nullptr;           // device error word
-    int math = ZWG_MATH_F32;
-    DevBuf q[2], k[2], v[2], out[2], ws[2];
-    DevBuf qh[2], kh[2], vh[2];   // bf16 copies for the tensor-core path
-};
+namespace zwg {
+namespace capi {
 
 std::mutex g_mu;
 Ctx* g_ctx[64] = {};
@@ -127,6 +98,10 @@ Plan plan_for(const zwg_attn_shape* sh, size_t n_batch, int sm_count) {
     return pl;
 }
 
+size_t workspace_bytes(const zwg_attn_shape* sh, size_t n_batch, int sm_count) {
+    return plan_for(sh, n_batch, sm_count).ws_bytes;
+}
+
 int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
             const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st) {
     const size_t nb = b ? b->n_batch : 1;
@@ -182,7 +157,10 @@ int sync_and_check(Ctx* c, cudaStream_t st) {
     return ZWG_OK;
 }
 
-}  // namespace
+}  // namespace capi
+}  // namespace zwg
+
+using namespace zwg::capi;
 
 namespace zwg {
 int set_last_error(const char* msg) { return fail("%s", msg); }

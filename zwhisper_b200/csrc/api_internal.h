@@ -1,0 +1,59 @@
+// Internals of the C-ABI layer shared by its source files (api.cu: contexts and the
+// attention entry points; state.cu: the library-owned decoder and LLM states).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include <algorithm>
+
+#include "../../include/zwgpu.h"
+
+namespace zwg {
+namespace capi {
+
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    bool ensure(size_t bytes) {
+        if (bytes <= cap) return true;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+        size_t want = std::max(bytes, (size_t)256);
+        if (cudaMalloc(&ptr, want) != cudaSuccess) return false;
+        cap = want;
+        return true;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+};
+
+struct Ctx {
+    int device = -1;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;  // second stream for pipelined host batches
+    int* err = nullptr;           // device error word
+    int math = ZWG_MATH_F32;
+    DevBuf q[2], k[2], v[2], out[2], ws[2];
+    DevBuf qh[2], kh[2], vh[2];   // bf16 copies for the tensor-core path
+};
+
+// The calling thread's context (zwg_init), or nullptr with the last error set.
+Ctx* cur();
+// Record the calling thread's last error (printf format); return ZWG_ERROR.
+int fail(const char* fmt, ...);
+int cuda_fail(const char* what, cudaError_t e);
+// Argument checks of an attention call (the reference's asserts, src/ops.zig:564-568).
+int check_shape(const zwg_attn_shape* sh);
+// Workspace bytes run_dev needs for this shape and batch.
+size_t workspace_bytes(const zwg_attn_shape* sh, size_t n_batch, int sm_count);
+// One batched attention call on device pointers (the body of zwg_attention_dev).
+int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
+            const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st);
+
+}  // namespace capi
+}  // namespace zwg

@@ -264,3 +264,137 @@ def rope_kt_append(q, k, v, cache_kt, cache_v, cos_t, sin_t, n_past: int, n_head
 
 def sync() -> None:
     _lib.check(_lib.load().zwg_sync())
+
+
+# ---- library-owned device state (zwg_dec_state / zwg_llm_state) ----------------------------
+
+def _check_rows(t, n_batch: int, n: int, width: int, name: str):
+    if t.numel() != n_batch * n * width:
+        raise ValueError(f"{name} must hold n_batch * n * {width} floats, got {t.numel()}")
+
+
+class DecoderState:
+    """Whisper decoder attention state on one device (zwg_dec_state): per layer the self
+    K/V cache [n_batch][n_text_ctx][n_state] and the cross K/V [n_batch][n_audio_ctx][n_state]
+    (src/decoder.zig:39-42, 127-130)."""
+
+    def __init__(self, n_layer: int, n_batch: int, n_state: int, n_head: int, n_text_ctx: int = 448,
+                 n_audio_ctx: int = 1500, device: int = 0):
+        _lib.ensure_init(device)
+        self.device, self.n_layer, self.n_batch = device, n_layer, n_batch
+        self.n_state, self.n_head, self.n_text_ctx, self.n_audio_ctx = n_state, n_head, n_text_ctx, n_audio_ctx
+        h = ctypes.c_void_p()
+        _lib.check(_lib.load().zwg_dec_state_create(n_layer, n_batch, n_state, n_head, n_text_ctx, n_audio_ctx,
+                                                    ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            _lib.check(_lib.load().zwg_dec_state_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def cache_ptrs(self, layer: int):
+        """Device addresses (self_k, self_v, cross_k, cross_v) of one layer."""
+        p = [ctypes.c_void_p() for _ in range(4)]
+        _lib.check(_lib.load().zwg_dec_state_cache(self._h, layer, *(ctypes.byref(x) for x in p)))
+        return tuple(x.value for x in p)
+
+    def set_cross(self, layer: int, window: int, k, v) -> None:
+        """setAudio for one window and layer (src/decoder.zig:150-156): k, v [n_audio_ctx][n_state]."""
+        torch = _torch()
+        for t, name in ((k, "k"), (v, "v")):
+            if t.numel() != self.n_audio_ctx * self.n_state or t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError(f"{name} must be contiguous f32 [n_audio_ctx][n_state]")
+        stream = _stream_of(k) if k.is_cuda else None
+        _lib.check(_lib.load().zwg_cross_kv_set(self._h, layer, window, k.data_ptr(), v.data_ptr(), stream))
+
+    def self_attn(self, layer: int, q, k_new, v_new, n_past: int, out=None):
+        """Append k_new/v_new at n_past.. and attend causally (src/decoder.zig:179-184);
+        q, k_new, v_new, out [n_batch][n][n_state] CUDA f32."""
+        torch = _torch()
+        n = q.numel() // (self.n_batch * self.n_state)
+        for t, name in ((q, "q"), (k_new, "k_new"), (v_new, "v_new")):
+            _check_rows(t, self.n_batch, n, self.n_state, name)
+        out = torch.empty_like(q) if out is None else out
+        _lib.check(_lib.load().zwg_dec_step_attn(
+            self._h, layer, _lib.ZWG_DEC_SELF, _dev_ptr(q, torch.float32, "q"), _dev_ptr(k_new, torch.float32, "k_new"),
+            _dev_ptr(v_new, torch.float32, "v_new"), n_past, n, _dev_ptr(out, torch.float32, "out"), _stream_of(q)))
+        return out
+
+    def cross_attn(self, layer: int, q, out=None):
+        """Attention over each window's cross K/V (src/decoder.zig:188-191)."""
+        torch = _torch()
+        n = q.numel() // (self.n_batch * self.n_state)
+        _check_rows(q, self.n_batch, n, self.n_state, "q")
+        out = torch.empty_like(q) if out is None else out
+        _lib.check(_lib.load().zwg_dec_step_attn(
+            self._h, layer, _lib.ZWG_DEC_CROSS, _dev_ptr(q, torch.float32, "q"), None, None, 0, n,
+            _dev_ptr(out, torch.float32, "out"), _stream_of(q)))
+        return out
+
+
+class LlmState:
+    """Qwen2 attention state on one device (zwg_llm_state): per layer cache_kt
+    [n_batch][n_head_kv][d][n_ctx] and cache_v [n_batch][n_ctx][n_head_kv*d], RoPE tables in
+    f64 (src/llm.zig:27-28, 124-137)."""
+
+    def __init__(self, n_layer: int, n_batch: int, n_head: int, n_head_kv: int, d: int, n_ctx: int,
+                 rope_base: float = 1e6, device: int = 0):
+        _lib.ensure_init(device)
+        self.device, self.n_layer, self.n_batch = device, n_layer, n_batch
+        self.n_head, self.n_head_kv, self.d, self.n_ctx = n_head, n_head_kv, d, n_ctx
+        h = ctypes.c_void_p()
+        _lib.check(_lib.load().zwg_llm_state_create(n_layer, n_batch, n_head, n_head_kv, d, n_ctx, float(rope_base),
+                                                    ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            _lib.check(_lib.load().zwg_llm_state_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def cache_ptrs(self, layer: int):
+        """Device addresses (cache_kt, cache_v) of one layer."""
+        kt, v = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(_lib.load().zwg_llm_state_cache(self._h, layer, ctypes.byref(kt), ctypes.byref(v)))
+        return kt.value, v.value
+
+    def append_rope(self, layer: int, q, k, v, n_past: int) -> None:
+        """RoPE on q (in place) and k, cache append at n_past.. (src/llm.zig:180-190)."""
+        torch = _torch()
+        n = q.numel() // (self.n_batch * self.n_head * self.d)
+        _check_rows(q, self.n_batch, n, self.n_head * self.d, "q")
+        _check_rows(k, self.n_batch, n, self.n_head_kv * self.d, "k")
+        _check_rows(v, self.n_batch, n, self.n_head_kv * self.d, "v")
+        _lib.check(_lib.load().zwg_llm_append_rope(
+            self._h, layer, _dev_ptr(q, torch.float32, "q"), _dev_ptr(k, torch.float32, "k"),
+            _dev_ptr(v, torch.float32, "v"), n_past, n, _stream_of(q)))
+
+    def attn(self, layer: int, q, n_past: int, out=None):
+        """Causal GQA attention over the cache, n_kv = n_past + n (src/llm.zig:191-202);
+        n = 1 runs zwg_llm_attn_decode, otherwise zwg_llm_attn_prefill."""
+        torch = _torch()
+        n = q.numel() // (self.n_batch * self.n_head * self.d)
+        _check_rows(q, self.n_batch, n, self.n_head * self.d, "q")
+        out = torch.empty_like(q) if out is None else out
+        lib = _lib.load()
+        if n == 1:
+            rc = lib.zwg_llm_attn_decode(self._h, layer, _dev_ptr(q, torch.float32, "q"), n_past,
+                                         _dev_ptr(out, torch.float32, "out"), _stream_of(q))
+        else:
+            rc = lib.zwg_llm_attn_prefill(self._h, layer, _dev_ptr(q, torch.float32, "q"), n_past, n,
+                                          _dev_ptr(out, torch.float32, "out"), _stream_of(q))
+        _lib.check(rc)
+        return out
