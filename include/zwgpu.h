@@ -167,6 +167,20 @@ ZWG_API int zwg_rope_kt_append(size_t n_batch, size_t n, size_t n_past, size_t n
                        const float* sin_tab, size_t q_bstride, size_t kv_bstride,
                        size_t cache_bstride, void* stream);
 
+/* ---- Q8 weights: the projections around the attention calls ------------------------ */
+
+/* gemm.Q8.quantize (src/gemm.zig:208-230) on the device: w [n][k] f32 (k a multiple of 32)
+ * -> q [n][k] int8 and scales [n][k/32] f32, scale = absmax / 127 per block of 32 and q =
+ * clamp(round(w * 127 / absmax), -127, 127): bit-identical to the reference. */
+ZWG_API int zwg_q8_quantize(const float* w, size_t n, size_t k, int8_t* q, float* scales, void* stream);
+
+/* ops.linear with Q8 weights (src/ops.zig:280-306 -> gemm.ntBlockQ, src/gemm.zig:268-351):
+ * out[m][n] = x[m][k] . W[n][k]^T + bias[n], W = q * scale per block of 32; bias may be NULL.
+ * Device pointers; x [m][k] and out [m][n] f32 row-major, k a multiple of 32, x and q
+ * 16-byte aligned. f32 arithmetic; the weight bytes are streamed once per 8 rows of x. */
+ZWG_API int zwg_linear_q8(const float* x, size_t m, size_t k, const int8_t* q, const float* scales,
+                          const float* bias, size_t n, float* out, void* stream);
+
 /* ---- library-owned device state (the device-resident API) ---------------------------
  * The reference keeps its attention buffers inside the decoder and the LLM
  * (src/decoder.zig:39-42, 127-130; src/llm.zig:27-28, 124-137). These states hold the

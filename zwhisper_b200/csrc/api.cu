@@ -384,6 +384,31 @@ int zwg_enc_attn_bf16(size_t n_batch, size_t n_ctx, size_t n_head, const uint16_
     return ZWG_OK;
 }
 
+int zwg_q8_quantize(const float* w, size_t n, size_t k, int8_t* q, float* scales, void* stream) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    if (k == 0 || k % 32) return fail("q8_quantize: k = %zu must be a positive multiple of 32", k);
+    if (n && (!w || !q || !scales)) return fail("q8_quantize: null buffer");
+    if (n * (k / 32) > (1ull << 40)) return fail("q8_quantize: matrix too large");
+    if (zwg::q8_quantize_launch(w, n, k, q, scales, (cudaStream_t)stream)) return cuda_fail("q8_quantize launch", cudaGetLastError());
+    return ZWG_OK;
+}
+
+int zwg_linear_q8(const float* x, size_t m, size_t k, const int8_t* q, const float* scales, const float* bias,
+                  size_t n, float* out, void* stream) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    if (k == 0 || k % 32) return fail("linear_q8: k = %zu must be a positive multiple of 32", k);
+    if (m == 0 || n == 0) return ZWG_OK;
+    if (!x || !q || !scales || !out) return fail("linear_q8: null buffer");
+    if (((uintptr_t)x | (uintptr_t)q) & 15) return fail("linear_q8: x and q must be 16-byte aligned");
+    if (((uintptr_t)scales | (uintptr_t)out | (uintptr_t)bias) & 3) return fail("linear_q8: f32 buffers must be 4-byte aligned");
+    if (n >= (1u << 30) || k >= (1u << 30)) return fail("linear_q8: matrix too large");
+    if (zwg::q8_linear_launch(x, m, k, q, scales, bias, n, out, (cudaStream_t)stream))
+        return cuda_fail("linear_q8 launch", cudaGetLastError());
+    return ZWG_OK;
+}
+
 int zwg_rope_kt_append(size_t n_batch, size_t n, size_t n_past, size_t n_head, size_t n_head_kv, size_t d,
                        size_t n_ctx, float* q, const float* k, const float* v, float* cache_kt, float* cache_v,
                        const float* cos_tab, const float* sin_tab, size_t q_bstride, size_t kv_bstride,

@@ -70,6 +70,11 @@ int enc_tc_launch(const EncTcParams& p, cudaStream_t st);
 bool prefill_tc_supported(const FlashParams& p, size_t n_batch);
 int prefill_tc_launch(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st);
 
+// Q8 weights (q8.cu): Q8.quantize and ops.linear over int8 blocks of 32.
+int q8_quantize_launch(const float* w, size_t n, size_t k, int8_t* q, float* scales, cudaStream_t st);
+int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
+                     size_t n, float* out, cudaStream_t st);
+
 // Elementwise helpers (misc.cu).
 int f32_to_bf16_launch(const float* x, uint16_t* y, size_t n, cudaStream_t st);
 

@@ -398,3 +398,36 @@ class LlmState:
                                           _dev_ptr(out, torch.float32, "out"), _stream_of(q))
         _lib.check(rc)
         return out
+
+
+# ---- Q8 weights (zwg_q8_quantize / zwg_linear_q8) ------------------------------------------
+
+def quantize_q8(w):
+    """Q8.quantize (src/gemm.zig:208-230) of a CUDA f32 [n][k] tensor: (q int8 [n][k],
+    scales f32 [n][k/32]), bit-identical to the reference."""
+    torch = _torch()
+    n, k = w.shape
+    q = torch.empty(n, k, dtype=torch.int8, device=w.device)
+    s = torch.empty(n, k // 32, dtype=torch.float32, device=w.device)
+    _lib.ensure_init(w.device.index or 0)
+    _lib.check(_lib.load().zwg_q8_quantize(_dev_ptr(w, torch.float32, "w"), n, k, q.data_ptr(), s.data_ptr(),
+                                           _stream_of(w)))
+    return q, s
+
+
+def linear_q8(x, q, scales, bias=None, out=None):
+    """ops.linear with Q8 weights (src/ops.zig:280-306): out[m][n] = x[m][k] . W[n][k]^T + b."""
+    torch = _torch()
+    m, k = x.shape
+    n = q.shape[0]
+    if q.shape[1] != k or q.dtype != torch.int8 or not q.is_contiguous():
+        raise ValueError("q must be contiguous int8 [n][k]")
+    if scales.numel() != n * (k // 32):
+        raise ValueError("scales must hold n * k / 32 floats")
+    out = torch.empty(m, n, dtype=torch.float32, device=x.device) if out is None else out
+    _lib.ensure_init(x.device.index or 0)
+    _lib.check(_lib.load().zwg_linear_q8(
+        _dev_ptr(x, torch.float32, "x"), m, k, q.data_ptr(), _dev_ptr(scales, torch.float32, "scales"),
+        _dev_ptr(bias, torch.float32, "bias") if bias is not None else None, n,
+        _dev_ptr(out, torch.float32, "out"), _stream_of(x)))
+    return out
