@@ -394,6 +394,56 @@ def secondary_prefill(dev, tc_peak, peak_kind, steps=2, warmup=1):
     return res
 
 
+def secondary_q8(dev, hbm_peak, steps=20, warmup=3):
+    """Q8 projections of one decode step at one GPU (the "next" row around the attention):
+    every Qwen2.5-1.5B linear of all 28 layers for one sequence (q, k, v, o, gate, up, down:
+    the reference's batch of one, src/llm.zig:179-216), and the Whisper base.en logits
+    product (51864 x 512, src/decoder.zig:412-413). Weights are int8 blocks of 32 with f32
+    scales (1.125 B per weight), distinct per layer; the bytes are the weight bytes read."""
+    import torch
+
+    from zwhisper_b200 import ops
+    res = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+
+    def q8w(n, k):
+        w = torch.randn(n, k, generator=g, device=dev) * 0.02
+        return ops.quantize_q8(w)
+
+    hidden, inter, kvw, layers = 1536, 8960, 256, 28
+    shapes = [(hidden, hidden), (kvw, hidden), (kvw, hidden), (hidden, hidden), (inter, hidden), (inter, hidden),
+              (hidden, inter)]
+    ws = [[q8w(n, k) for (n, k) in shapes] for _ in range(layers)]
+    xs = {k: torch.randn(1, k, generator=g, device=dev) for k in (hidden, inter)}
+    outs = {n: torch.empty(1, n, device=dev) for n in (hidden, kvw, inter)}
+
+    def step():
+        for lw in ws:
+            for (n, k), (q, sc) in zip(shapes, lw):
+                ops.linear_q8(xs[k], q, sc, out=outs[n])
+    t = time_graph(step, steps, warmup) / steps
+    byts = layers * sum(n * k * 1.125 for n, k in shapes)
+    res.append({"workload": "Qwen2.5-1.5B decode-step projections, 1 sequence x 28 layers x 7 Q8 linears "
+                            "(q/k/v/o/gate/up/down), int8 blocks of 32 + f32 scales",
+                "metric": "q8_projection_weight_GBps", "value": byts / t / 1e9, "unit": "GB/s",
+                "ms_per_step": t * 1e3,
+                "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
+    del ws
+    q, sc = q8w(51864, 512)
+    x1 = torch.randn(1, 512, generator=g, device=dev)
+    o1 = torch.empty(1, 51864, device=dev)
+    t = time_graph(lambda: ops.linear_q8(x1, q, sc, out=o1), steps, warmup) / steps
+    byts = 51864 * 512 * 1.125
+    res.append({"workload": "Whisper base.en logits, 51864 x 512 Q8 weights, 1 token",
+                "metric": "q8_logits_weight_GBps", "value": byts / t / 1e9, "unit": "GB/s", "ms_per_step": t * 1e3,
+                "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -477,7 +527,8 @@ def run_ours(args, rank, world, local):
     secondary = None
     cpu = None
     if world == 1 and not args.no_secondary:
-        secondary = secondary_decode(dev, hbm_peak) + secondary_prefill(dev, tc_peak, peak_kind)
+        secondary = (secondary_decode(dev, hbm_peak) + secondary_prefill(dev, tc_peak, peak_kind) +
+                     secondary_q8(dev, hbm_peak))
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_windows_per_s(min_seconds=args.cpu_seconds)
 

@@ -13,7 +13,7 @@
 //   int8 values and scales are bit-identical to Q8.quantize.
 // q8_linear_kernel<MR>: the decode-shaped product (m <= 8 rows of x per launch; larger m in
 //   chunks of 8). The weight bytes are the traffic (1.125 B per weight with the scales), so
-//   the kernel streams them once: a warp owns 4 weight rows, lane l reads 16 (8 for MR = 8)
+//   the kernel streams them once: a warp owns 1-4 weight rows, lane l reads 16 (8 for MR = 8)
 //   consecutive int8 of each row per step (one 128-bit load, a 512-byte coalesced row
 //   segment per warp), widens them to f32 exactly (byte permute into a 2^23 float, then one
 //   subtraction), takes the dot with the same k range of every x row (rows in pairs per
@@ -32,8 +32,11 @@ namespace q8 {
 
 constexpr int BLOCK = 32;
 constexpr int WARPS = 8;  // per CTA
-constexpr int RW = 4;     // weight rows per warp
-
+// Weight rows per warp (RW) and k steps unrolled per lane (UNR) are chosen so that each lane
+// has about four 16-byte weight loads in flight: with 24-32 resident warps per SM that is
+// 50-64 KB per SM, enough to cover the memory latency. Short rows (k <= 512) take 4 rows
+// per warp, k <= 1536 two, longer rows one row with 4 steps unrolled. With 4-8 x rows a warp
+// takes 4 weight rows, so each x value loaded serves four of them.
 __global__ void __launch_bounds__(256) q8_quantize_kernel(const float* __restrict__ w, int n, int k,
                                                           int8_t* __restrict__ q, float* __restrict__ scales) {
     const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // global warp = block
@@ -57,13 +60,14 @@ __device__ __forceinline__ float i8f(uint32_t ub, int j) {
     return __uint_as_float(__byte_perm(ub, 0x4B000000u, 0x7650u | (uint32_t)j)) - 8388736.0f;  // 2^23 + 128
 }
 
-template <int MR>
-__global__ void __launch_bounds__(256) q8_linear_kernel(const float* __restrict__ x, int m, int k,
+template <int MR, int RW>
+__global__ void __launch_bounds__(256, MR >= 4 ? 1 : 3) q8_linear_kernel(const float* __restrict__ x, int m, int k,
                                                         const int8_t* __restrict__ wq, const float* __restrict__ ws,
                                                         const float* __restrict__ bias, int n,
                                                         float* __restrict__ out) {
     constexpr int KL = MR >= 8 ? 8 : 16;  // k per lane per step
     constexpr int MP = (MR + 1) / 2;      // x row pairs
+    constexpr int UNR = (MR <= 2 && RW == 1) ? 4 : 1;  // k steps unrolled per lane
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = (blockIdx.x * WARPS + warp) * RW;
     if (row0 >= n) return;
@@ -82,6 +86,7 @@ __global__ void __launch_bounds__(256) q8_linear_kernel(const float* __restrict_
 #pragma unroll
         for (int p = 0; p < MP; p++) acc[r][p] = make_float2(0.f, 0.f);
 
+#pragma unroll UNR
     for (int k0 = lane * KL; k0 < k; k0 += 32 * KL) {
         // x rows for this lane's k range
         float xv[MR][KL];
@@ -166,15 +171,27 @@ int q8_quantize_launch(const float* w, size_t n, size_t k, int8_t* q, float* sca
 int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
                      size_t n, float* out, cudaStream_t st) {
     if (m == 0 || n == 0) return 0;
-    const unsigned grid = (unsigned)((n + q8::WARPS * q8::RW - 1) / (q8::WARPS * q8::RW));
+    const int rw = k <= 512 ? 4 : k <= 1536 ? 2 : 1;  // weight rows per warp for 1-2 x rows
     for (size_t m0 = 0; m0 < m; m0 += 8) {
         const int mc = (int)std::min<size_t>(8, m - m0);
         const float* xc = x + m0 * k;
         float* oc = out + m0 * n;
-        if (mc == 1) q8::q8_linear_kernel<1><<<grid, 256, 0, st>>>(xc, mc, (int)k, wq, ws, bias, (int)n, oc);
-        else if (mc == 2) q8::q8_linear_kernel<2><<<grid, 256, 0, st>>>(xc, mc, (int)k, wq, ws, bias, (int)n, oc);
-        else if (mc <= 4) q8::q8_linear_kernel<4><<<grid, 256, 0, st>>>(xc, mc, (int)k, wq, ws, bias, (int)n, oc);
-        else q8::q8_linear_kernel<8><<<grid, 256, 0, st>>>(xc, mc, (int)k, wq, ws, bias, (int)n, oc);
+        const int r = mc <= 2 ? rw : 4;
+        const unsigned grid = (unsigned)((n + q8::WARPS * r - 1) / (q8::WARPS * r));
+        const int ik = (int)k, in = (int)n;
+        if (mc == 1) {
+            if (r == 4) q8::q8_linear_kernel<1, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+            else if (r == 2) q8::q8_linear_kernel<1, 2><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+            else q8::q8_linear_kernel<1, 1><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+        } else if (mc == 2) {
+            if (r == 4) q8::q8_linear_kernel<2, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+            else if (r == 2) q8::q8_linear_kernel<2, 2><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+            else q8::q8_linear_kernel<2, 1><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+        } else if (mc <= 4) {
+            q8::q8_linear_kernel<4, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+        } else {
+            q8::q8_linear_kernel<8, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+        }
         if (cudaPeekAtLastError() != cudaSuccess) return -1;
     }
     return 0;
