@@ -99,7 +99,10 @@ struct Geo {
     int n_t;          // tiles per segment
     int n_segs;
     int p_max;        // pieces per segment the workspace holds
-    int aligned;      // ranges follow segment boundaries (at least as many segments as CTAs)
+    int mode;         // 0: equal ranges over all tiles (stream-K); 1: whole segments per CTA
+                      // (at least as many segments as CTAs); 2: every segment cut into
+                      // `pieces` equal pieces, one per CTA (few segments, many CTAs)
+    int pieces;
 };
 
 __device__ __forceinline__ void named_barrier(int id, int threads) {
@@ -113,11 +116,17 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
-// First tile of CTA c, for G CTAs over the T tiles of `geo`: equal ranges, or, with at least
+// First tile of CTA c, for G CTAs over the T tiles of `geo`: equal ranges; or, with at least
 // as many segments as CTAs, equal numbers of whole segments (no segment is then shared, and
-// no CTA pays the merge of a shared segment).
+// no CTA pays the merge of a shared segment); or, with many more CTAs than segments, one
+// piece of one segment per CTA (no CTA holds two segments, so each pays one merge).
 __host__ __device__ __forceinline__ long long range_begin(long long c, const Geo& geo, long long G) {
-    if (geo.aligned) return (c * geo.n_segs / G) * geo.n_t;
+    if (geo.mode == 1) return (c * geo.n_segs / G) * geo.n_t;
+    if (geo.mode == 2) {
+        if (c >= (long long)geo.n_segs * geo.pieces) return geo.total;
+        const long long seg = c / geo.pieces, pc = c % geo.pieces;
+        return seg * geo.n_t + (pc * geo.n_t) / geo.pieces;
+    }
     return c * geo.total / G;
 }
 // The CTA whose range holds tile x.
@@ -579,15 +588,37 @@ bool decode_tma_supported(const DecodeParams& p) {
     return true;
 }
 
-// Grid and workspace of the stream-K schedule: one CTA per SM (fewer when there are fewer
-// tiles), pieces per segment bounded by ceil(G / segments) + 1.
+// The schedule: one CTA per SM (fewer when there are fewer tiles). With at least as many
+// segments as CTAs each CTA takes whole segments; with at least twice as many SMs as
+// segments every segment is cut into floor(SMs / segments) pieces (at most one per tile),
+// one per CTA; otherwise equal ranges over all tiles. p_max bounds the pieces of a segment.
+static void decode_tma_schedule(size_t n_batch, size_t n_head_kv, size_t n_kv, int sm_count, int* grid, int* p_max,
+                                int* mode, int* pieces) {
+    const long long n_t = std::max<long long>(1, (long long)((n_kv + dec_tma::TK - 1) / dec_tma::TK));
+    const long long segs = std::max<long long>(1, (long long)(n_batch * n_head_kv));
+    const long long total = n_t * segs;
+    const long long sms = std::max(1, sm_count);
+    *pieces = 1;
+    if (segs >= sms) {
+        *grid = (int)sms;
+        *mode = 1;
+        *p_max = 1;
+    } else if (2 * segs <= sms && n_t >= 2) {
+        const long long pc = std::min<long long>(sms / segs, n_t);
+        *grid = (int)(segs * pc);
+        *mode = 2;
+        *pieces = (int)pc;
+        *p_max = (int)pc;
+    } else {
+        *grid = (int)std::max<long long>(1, std::min<long long>(sms, total));
+        *mode = 0;
+        *p_max = (int)((*grid + segs - 1) / segs) + 1;
+    }
+}
+
 void decode_tma_plan(size_t n_batch, size_t n_head_kv, size_t n_kv, int sm_count, int* grid, int* p_max) {
-    const long long n_t = (long long)((n_kv + dec_tma::TK - 1) / dec_tma::TK);
-    const long long segs = (long long)(n_batch * n_head_kv);
-    const long long total = std::max<long long>(1, n_t * segs);
-    const int g = (int)std::max<long long>(1, std::min<long long>(sm_count, total));
-    *grid = g;
-    *p_max = (int)((g + segs - 1) / std::max<long long>(segs, 1)) + 1;
+    int mode = 0, pieces = 1;
+    decode_tma_schedule(n_batch, n_head_kv, n_kv, sm_count, grid, p_max, &mode, &pieces);
 }
 
 size_t decode_tma_workspace_bytes(size_t n_batch, size_t n_head_kv, size_t rows, size_t d, int p_max) {
@@ -597,8 +628,8 @@ size_t decode_tma_workspace_bytes(size_t n_batch, size_t n_head_kv, size_t rows,
 }
 
 template <int D, bool KT>
-static int launch_d(const DecodeParams& p, size_t n_batch, int rmax, int grid, int p_max, int* counters,
-                    int* err, cudaStream_t st) {
+static int launch_d(const DecodeParams& p, size_t n_batch, int rmax, int grid, int p_max, int mode, int pieces,
+                    int* counters, int* err, cudaStream_t st) {
     CUtensorMap mk, mv;
     const uint64_t rows_kv = p.n_kv ? p.n_kv : 1;
     bool okm;
@@ -613,7 +644,8 @@ static int launch_d(const DecodeParams& p, size_t n_batch, int rmax, int grid, i
     geo.n_segs = (int)(n_batch * p.n_head_kv);
     geo.total = (long long)geo.n_t * geo.n_segs;
     geo.p_max = p_max;
-    geo.aligned = geo.n_segs >= grid ? 1 : 0;
+    geo.mode = mode;
+    geo.pieces = pieces;
     auto go = [&](auto kern, size_t smem, int threads) -> int {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return -1;
@@ -632,8 +664,8 @@ int decode_tma_launch(const DecodeParams& p, size_t n_batch, int sm_count, int* 
     if (n_batch == 0 || p.n_q == 0) return 0;
     const size_t rows = p.n_q * (p.n_head / p.n_head_kv);
     const int rmax = rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8;
-    int grid = 1, p_max = 1;
-    decode_tma_plan(n_batch, p.n_head_kv, p.n_kv, sm_count, &grid, &p_max);
+    int grid = 1, p_max = 1, mode = 0, pieces = 1;
+    decode_tma_schedule(n_batch, p.n_head_kv, p.n_kv, sm_count, &grid, &p_max, &mode, &pieces);
     // the segment tickets follow the partials in the workspace; they must start at zero,
     // and the last CTA of each segment puts its ticket back to zero
     const size_t segs = n_batch * p.n_head_kv;
@@ -642,9 +674,9 @@ int decode_tma_launch(const DecodeParams& p, size_t n_batch, int sm_count, int* 
     if (cudaMemsetAsync(counters, 0, segs * sizeof(int), st) != cudaSuccess) return -1;
     const bool kt = p.kt_stride != 0;
     switch (p.d) {
-        case 32: return kt ? launch_d<32, true>(p, n_batch, rmax, grid, p_max, counters, err, st) : launch_d<32, false>(p, n_batch, rmax, grid, p_max, counters, err, st);
-        case 64: return kt ? launch_d<64, true>(p, n_batch, rmax, grid, p_max, counters, err, st) : launch_d<64, false>(p, n_batch, rmax, grid, p_max, counters, err, st);
-        case 128: return kt ? launch_d<128, true>(p, n_batch, rmax, grid, p_max, counters, err, st) : launch_d<128, false>(p, n_batch, rmax, grid, p_max, counters, err, st);
+        case 32: return kt ? launch_d<32, true>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st) : launch_d<32, false>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st);
+        case 64: return kt ? launch_d<64, true>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st) : launch_d<64, false>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st);
+        case 128: return kt ? launch_d<128, true>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st) : launch_d<128, false>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st);
     }
     return -1;
 }

@@ -231,6 +231,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mma_commit(&sm.s_full[t]);
                     return true;
                 };
+                // tile 1 starts one softmax phase behind tile 0, so the two warpgroups'
+                // exponential phases alternate on the MUFU instead of coinciding
+                if (t == 1 && !(ok = mbar_wait(&sm.p_full[0], g & 1, err))) break;
                 ok = issue_s(g);
                 for (int j = 0; ok && j < n_tiles; j++) {
                     const uint32_t gj = g + j;
