@@ -232,6 +232,12 @@ ZWG_API int zwg_llm_attn_prefill(zwg_llm_state* st, size_t layer, const float* q
 ZWG_API int zwg_llm_attn_decode(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, float* out,
                                 void* stream);
 
+/* Self-test of the timeout path every kernel relies on: launches one bounded device-side
+ * wait on a barrier nothing ever completes (a few seconds), then synchronizes. Returns
+ * ZWG_TIMEOUT when the wait ran out, was reported through the error word and left the
+ * context usable (the expected result); ZWG_ERROR otherwise. No reference counterpart. */
+ZWG_API int zwg_selftest_timeout(void);
+
 /* Synchronize the device and report the context's device-side error word, if set. */
 ZWG_API int zwg_sync(void);
 

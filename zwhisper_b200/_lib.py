@@ -64,6 +64,7 @@ SIGNATURES = {
                                           c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_size, c_size, c_ptr]),
     "zwg_sync": (ctypes.c_int, []),
     "zwg_set_math": (ctypes.c_int, [ctypes.c_int]),
+    "zwg_selftest_timeout": (ctypes.c_int, []),
     "zwg_q8_quantize": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr]),
     "zwg_linear_q8": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr, c_size, c_ptr, c_ptr]),
     "zwg_dec_state_create": (ctypes.c_int, [c_size, c_size, c_size, c_size, c_size, c_size, ctypes.POINTER(c_ptr)]),

@@ -384,6 +384,29 @@ int zwg_enc_attn_bf16(size_t n_batch, size_t n_ctx, size_t n_head, const uint16_
     return ZWG_OK;
 }
 
+int zwg_selftest_timeout(void) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    int* gave_up = nullptr;
+    cudaError_t e = cudaMalloc(&gave_up, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail("selftest allocation", e);
+    int h = 0;
+    if ((e = cudaMemsetAsync(gave_up, 0, sizeof(int), c->stream)) != cudaSuccess) {
+        cudaFree(gave_up);
+        return cuda_fail("selftest", e);
+    }
+    if (zwg::wait_timeout_selftest_launch(c->err, gave_up, c->stream)) {
+        cudaFree(gave_up);
+        return cuda_fail("selftest launch", cudaGetLastError());
+    }
+    const int rc = sync_and_check(c, c->stream);  // expected: ZWG_TIMEOUT, error word cleared
+    e = cudaMemcpy(&h, gave_up, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(gave_up);
+    if (e != cudaSuccess) return cuda_fail("selftest readback", e);
+    if (rc == ZWG_TIMEOUT && h == 1) return ZWG_TIMEOUT;
+    return fail("selftest: the bounded wait did not report a timeout (rc %d, gave_up %d)", rc, h);
+}
+
 int zwg_q8_quantize(const float* w, size_t n, size_t k, int8_t* q, float* scales, void* stream) {
     Ctx* c = cur();
     if (!c) return ZWG_ERROR;

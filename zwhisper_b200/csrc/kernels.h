@@ -75,6 +75,9 @@ int q8_quantize_launch(const float* w, size_t n, size_t k, int8_t* q, float* sca
 int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
                      size_t n, float* out, cudaStream_t st);
 
+// One bounded wait that nothing completes (selftest.cu); gave_up is set to 1 when it ran out.
+int wait_timeout_selftest_launch(int* err, int* gave_up, cudaStream_t st);
+
 // Elementwise helpers (misc.cu).
 int f32_to_bf16_launch(const float* x, uint16_t* y, size_t n, cudaStream_t st);
 
