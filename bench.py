@@ -571,7 +571,8 @@ def run_kernel_case(args):
     `decode_qwen05` = the same on 16 Qwen2.5-0.5B sequences (d 64, n_kv 2128);
     `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention;
     `prefill_qwen` = the tf32 prefill kernel on the last 208-query chunk of a 2000-token
-    prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2)."""
+    prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2);
+    `q8_logits` = the Q8 linear kernel on the Whisper base.en logits product (51864 x 512)."""
     import torch
 
     from zwhisper_b200 import ops
@@ -599,6 +600,17 @@ def run_kernel_case(args):
         def fn():
             ops.attention_dev(q, kt, v, sh, out, n_batch=B, workspace=ws)
         work = f"{B * n_kv * Hkv * d * 8 / 1e6:.1f} MB of K/V per launch"
+    elif args.kernel_case == "q8_logits":
+        n, k = 51864, 512
+        w = torch.randn(n, k, generator=g, device=dev) * 0.02
+        q, sc = ops.quantize_q8(w)
+        del w
+        x = torch.randn(1, k, generator=g, device=dev)
+        out = torch.empty(1, n, device=dev)
+
+        def fn():
+            ops.linear_q8(x, q, sc, out=out)
+        work = f"{n * k * 1.125 / 1e6:.1f} MB of Q8 weights per launch"
     elif args.kernel_case == "prefill_qwen":
         B, H, Hkv, d, n_ctx, n_past, n_q = 64, 12, 2, 128, 2048, 1792, 208
         q = torch.randn(B, n_q, H * d, generator=g, device=dev)
@@ -642,8 +654,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_whisper", "prefill_qwen"],
-                    default=None)
+    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_whisper", "prefill_qwen",
+                                             "q8_logits"], default=None)
     args = ap.parse_args()
     if args.kernel_case:
         run_kernel_case(args)
