@@ -17,7 +17,9 @@ Reported (one JSON line from rank 0):
   cpu_baseline  the C restatement of the reference attention (oracle/attn_ref.c) on the
              host cores, rank 0 at N=1;
   secondary  decode-attention workloads (configs 1, 3, 4) at N=1: tok/s and HBM roofline,
-             each decode step (all layers) replayed from a CUDA graph.
+             each decode step (all layers) replayed from a CUDA graph; prefill attention;
+             the Q8 projections; and the whole Qwen2.5-1.5B greedy decode step on the
+             device (B = 1 and 64).
 
 `--impl reference` times the reference's CPU attention (the C restatement; the Zig source
 cannot be built here) on the same workload and prints the same line with "impl".
@@ -444,6 +446,88 @@ def secondary_q8(dev, hbm_peak, steps=20, warmup=3):
     return res
 
 
+QWEN15 = dict(n_layer=28, n_head=12, n_head_kv=2, d=128, n_ff=8960, n_vocab=151936, eps=1e-6)
+
+
+def qwen15_weights(dev, seed=5, n_layer=None):
+    """Random Qwen2.5-1.5B weights in Q8 on the device (configs[4]: N(0, 0.02^2), tied
+    embedding/output), distinct per layer so a step's weight stream (1.74 GB) is far above L2."""
+    import torch
+
+    from zwhisper_b200 import ops
+    c = QWEN15
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    ne, kvw = c["n_head"] * c["d"], c["n_head_kv"] * c["d"]
+
+    def q8w(n, k):
+        return ops.quantize_q8(torch.randn(n, k, generator=g, device=dev) * 0.02)
+
+    def vec(n, mean, sd):
+        return mean + torch.randn(n, generator=g, device=dev) * sd
+
+    layers = [{"attn_norm": vec(ne, 1.0, 0.1), "wq": q8w(ne, ne), "wk": q8w(kvw, ne), "wv": q8w(kvw, ne),
+               "bq": vec(ne, 0.0, 0.1), "bk": vec(kvw, 0.0, 0.1), "bv": vec(kvw, 0.0, 0.1), "wo": q8w(ne, ne),
+               "ffn_norm": vec(ne, 1.0, 0.1), "w_gate": q8w(c["n_ff"], ne), "w_up": q8w(c["n_ff"], ne),
+               "w_down": q8w(ne, c["n_ff"])} for _ in range(n_layer or c["n_layer"])]
+    embd = q8w(c["n_vocab"] if n_layer is None else 64, ne)
+    return ops.LlmWeightsQ8(layers, embd, None, vec(ne, 1.0, 0.1), c["eps"], device=dev.index or 0)
+
+
+def qwen15_step_fn(W, B, n_ctx, n_past, dev, seed=6):
+    """One greedy decode step of B sequences through the C ABI (zwg_llm_forward_q8 then
+    zwg_llm_greedy), the chosen token written back as the next step's input."""
+    import torch
+
+    from zwhisper_b200 import ops
+    c = QWEN15
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    st = ops.LlmState(c["n_layer"], B, c["n_head"], c["n_head_kv"], c["d"], n_ctx, rope_base=1e6,
+                      device=dev.index or 0)
+    tok = torch.randint(0, c["n_vocab"], (B, 1), generator=g, device=dev, dtype=torch.int32)
+    recent = torch.randint(0, c["n_vocab"], (B, 64), generator=g, device=dev, dtype=torch.int32)
+    x = torch.empty(B, 1, W.n_embd, device=dev)
+    logits = torch.empty(B, W.n_vocab, device=dev)
+    scratch = st.scratch(1, W.n_ff)
+
+    def step():
+        st.forward_q8(W, tok, n_past, x=x, logits=logits, scratch=scratch)
+        ops.llm_greedy(logits, recent, n_recent=64, window=64, penalty=1.1, out=tok.view(-1))
+    return st, step
+
+
+def secondary_step(dev, hbm_peak, steps=10, warmup=3):
+    """The whole Qwen2.5-1.5B greedy decode step on the device (the "next" rows around the
+    attention, src/llm.zig:169-216, 313-321): embedding, 28 layers of RMSNorm, Q8 q/k/v with
+    bias + RoPE + K^T/V append in one launch, decode attention over n_kv = 2256, wo +
+    residual, RMSNorm, gate/up + SiLU*up in one launch, w_down + residual; final norm,
+    151936-row logits and the penalized argmax, the token fed back on the device. B = 1 (the
+    reference's own generate loop) and B = 64 (configs[4]'s batch). Algorithmic bytes: the
+    Q8 weights once (1.74 GB with the tied output matrix) plus each sequence's K/V reads."""
+    import torch
+    c = QWEN15
+    W = qwen15_weights(dev)
+    n_ctx, n_kv = 2560, 2256
+    wbytes = (c["n_layer"] * (2 * 1536 * 1536 + 2 * 256 * 1536 + 3 * c["n_ff"] * 1536) + c["n_vocab"] * 1536) * 1.125
+    res = []
+    for B in (1, 64):
+        st, step = qwen15_step_fn(W, B, n_ctx, n_kv - 1, dev)
+        t = time_graph(step, steps, warmup) / steps
+        kv = B * c["n_layer"] * n_kv * c["n_head_kv"] * c["d"] * 2 * 4
+        byts = wbytes + kv
+        res.append({"workload": f"Qwen2.5-1.5B greedy decode step on the device, {B} sequence(s) x 28 layers + logits "
+                                f"(vocab 151936) + penalized argmax, Q8 weights, n_kv={n_kv}",
+                    "metric": "qwen_decode_step_tok_per_s", "value": B / t, "unit": "tok/s", "ms_per_step": t * 1e3,
+                    "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                                 "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
+        st.close()
+        torch.cuda.empty_cache()
+    del W
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -528,7 +612,7 @@ def run_ours(args, rank, world, local):
     cpu = None
     if world == 1 and not args.no_secondary:
         secondary = (secondary_decode(dev, hbm_peak) + secondary_prefill(dev, tc_peak, peak_kind) +
-                     secondary_q8(dev, hbm_peak))
+                     secondary_q8(dev, hbm_peak) + secondary_step(dev, hbm_peak))
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_windows_per_s(min_seconds=args.cpu_seconds)
 
@@ -572,7 +656,11 @@ def run_kernel_case(args):
     `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention;
     `prefill_qwen` = the tf32 prefill kernel on the last 208-query chunk of a 2000-token
     prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2);
-    `q8_logits` = the Q8 linear kernel on the Whisper base.en logits product (51864 x 512)."""
+    `q8_logits` = the Q8 linear kernel on the Whisper base.en logits product (51864 x 512);
+    `step_qwen15` = one whole Qwen2.5-1.5B greedy decode step for one sequence (n_kv 2256),
+    every kernel of the step in launch order (about 200 launches); `pair_qwen15` = the two
+    paired-row Q8 kernels of one Qwen2.5-1.5B layer for one sequence: q/k/v + RoPE + cache
+    append (3.5 MB of weights) then gate/up + SiLU*up (31 MB)."""
     import torch
 
     from zwhisper_b200 import ops
@@ -611,6 +699,22 @@ def run_kernel_case(args):
         def fn():
             ops.linear_q8(x, q, sc, out=out)
         work = f"{n * k * 1.125 / 1e6:.1f} MB of Q8 weights per launch"
+    elif args.kernel_case == "step_qwen15":
+        W = qwen15_weights(dev)
+        st, fn = qwen15_step_fn(W, 1, 2560, 2255, dev)
+        work = "one decode step: 1.74 GB of Q8 weights + 129 MB of K/V"
+    elif args.kernel_case == "pair_qwen15":
+        W = qwen15_weights(dev, n_layer=1)
+        st = ops.LlmState(1, 1, QWEN15["n_head"], QWEN15["n_head_kv"], QWEN15["d"], 2560, device=0)
+        h = torch.randn(1, 1, W.n_embd, generator=g, device=dev)
+        qo = torch.empty_like(h)
+        L = W.layers[0]
+        gate = torch.empty(1, W.n_ff, device=dev)
+
+        def fn():
+            st.qkv_q8(0, h, W, 2255, q_out=qo)
+            ops.linear_q8_silu_mul(h.view(1, -1), L["w_gate"], L["w_up"], out=gate)
+        work = f"{(1536 + 512) * 1536 * 1.125 / 1e6:.1f} + {2 * 8960 * 1536 * 1.125 / 1e6:.1f} MB of Q8 weights"
     elif args.kernel_case == "prefill_qwen":
         B, H, Hkv, d, n_ctx, n_past, n_q = 64, 12, 2, 128, 2048, 1792, 208
         q = torch.randn(B, n_q, H * d, generator=g, device=dev)
@@ -655,7 +759,7 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_whisper", "prefill_qwen",
-                                             "q8_logits"], default=None)
+                                             "q8_logits", "step_qwen15", "pair_qwen15"], default=None)
     args = ap.parse_args()
     if args.kernel_case:
         run_kernel_case(args)

@@ -232,6 +232,98 @@ ZWG_API int zwg_llm_attn_prefill(zwg_llm_state* st, size_t layer, const float* q
 ZWG_API int zwg_llm_attn_decode(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, float* out,
                                 void* stream);
 
+/* ---- the Qwen2 decode step around the attention (src/llm.zig:168-216, 268-321) --------
+ * The rest of Model.forward, so a greedy decode keeps hidden states, caches and tokens on
+ * the device. All buffers are device pointers; calls are stream ordered. The projection,
+ * norm and sampling kernels start early when they follow one another on a stream: each
+ * streams its own weights while the kernel before it finishes, and reads that kernel's
+ * results only once it has completed. Q8 matrices are int8 [n][k] plus f32 scales
+ * [n][k/32] (gemm.Q8, src/gemm.zig:188-200). */
+typedef struct zwg_q8_mat {
+    const int8_t* q;
+    const float* scales;
+} zwg_q8_mat;
+
+/* One layer's weights (llm.Layer, src/llm.zig:15-30, without the caches): attn_norm and
+ * ffn_norm [n_embd]; wq [n_head*d][n_embd]; wk, wv [n_head_kv*d][n_embd]; wo
+ * [n_embd][n_head*d]; w_gate, w_up [n_ff][n_embd]; w_down [n_embd][n_ff]. bq, bk, bv are
+ * f32 or NULL. */
+typedef struct zwg_llm_layer_weights {
+    const float* attn_norm;
+    zwg_q8_mat wq, wk, wv, wo;
+    const float* bq;
+    const float* bk;
+    const float* bv;
+    const float* ffn_norm;
+    zwg_q8_mat w_gate, w_up, w_down;
+} zwg_llm_layer_weights;
+
+/* The model's weights (llm.Model, src/llm.zig:32-60): embd and output [n_vocab][n_embd] (the
+ * same matrix when tied), output_norm [n_embd], `layers` a HOST array of the state's n_layer
+ * entries. n_embd must equal n_head * d, as the reference's buffers assume; n_embd and n_ff
+ * are multiples of 32. */
+typedef struct zwg_llm_weights {
+    size_t n_vocab, n_embd, n_ff;
+    float eps;
+    zwg_q8_mat embd, output;
+    const float* output_norm;
+    const zwg_llm_layer_weights* layers;
+} zwg_llm_weights;
+
+/* ops.rmsNorm (src/ops.zig:408-425): out[i] = x[i] * (1 / sqrt(mean(x[i]^2) + eps)) * w for
+ * m rows of n (n a multiple of 4, 16-byte aligned buffers); out may be x. */
+ZWG_API int zwg_rms_norm(const float* x, size_t m, size_t n, const float* w, float eps, float* out, void* stream);
+
+/* ops.linear then ops.add (src/llm.zig:203-204, 209-210): out[m][n] += x[m][k] . W^T, with
+ * W Q8 as zwg_linear_q8 (the residual stream updated in place). */
+ZWG_API int zwg_linear_q8_add(const float* x, size_t m, size_t k, const int8_t* q, const float* scales, size_t n,
+                              float* out, void* stream);
+
+/* The gate and up projections and ops.siluMul (src/llm.zig:206-208, src/ops.zig:435-440) in
+ * one launch: out[m][n] = silu(x . Wg^T) * (x . Wu^T), silu(g) = g / (1 + exp(-g)). */
+ZWG_API int zwg_linear_q8_silu_mul(const float* x, size_t m, size_t k, const int8_t* gate_q,
+                                   const float* gate_scales, const int8_t* up_q, const float* up_scales, size_t n,
+                                   float* out, void* stream);
+
+/* Q8.row (src/gemm.zig:256-263) for each token: out[i][:] = q[tokens[i]][:] * scales, the
+ * embedding lookup of src/llm.zig:175, bit-identical. A token outside [0, n_vocab) gives a
+ * zero row and sets the device error word (reported by zwg_sync). */
+ZWG_API int zwg_embed_q8(const int32_t* tokens, size_t m, const int8_t* q, const float* scales, size_t n_vocab,
+                         size_t k, float* out, void* stream);
+
+/* Model.penalize then Model.argmax (src/llm.zig:268-273, 313-321) for m rows of logits
+ * [m][n_vocab], in place: when penalty > 1, the logits of row i's last `window` entries
+ * of recent[i * recent_stride + 0 .. n_recent) are divided by penalty (positive) or
+ * multiplied by it (otherwise), repeats again each time; then out[i * out_stride] = the
+ * first index of the largest logit. */
+ZWG_API int zwg_llm_greedy(float* logits, size_t m, size_t n_vocab, const int32_t* recent, size_t recent_stride,
+                           size_t n_recent, size_t window, float penalty, int32_t* out, size_t out_stride,
+                           void* stream);
+
+/* The q, k and v projections with their biases, RoPE at positions n_past.. and the cache
+ * append (src/llm.zig:179-190) in one launch: x [n_batch][n][n_head*d] (the normed hidden
+ * states) -> q_out [n_batch][n][n_head*d] rotated, k rotated into the layer's cache_kt and v
+ * into its cache_v. Uses w->wq, wk, wv, bq, bk, bv. */
+ZWG_API int zwg_llm_qkv_q8(zwg_llm_state* st, size_t layer, const float* x, const zwg_llm_layer_weights* w,
+                           size_t n_past, size_t n, float* q_out, void* stream);
+
+/* Scratch bytes zwg_llm_layer_q8 and zwg_llm_forward_q8 need for chunks of n tokens. */
+ZWG_API size_t zwg_llm_scratch_bytes(const zwg_llm_state* st, size_t n, size_t n_ff);
+
+/* One layer of Model.forward (src/llm.zig:177-210) for every sequence: x [n_batch][n][n_embd],
+ * the residual stream, updated in place; tokens at positions n_past..n_past+n-1. Runs
+ * rmsNorm, zwg_llm_qkv_q8, the attention (as zwg_llm_attn_prefill), wo + residual,
+ * rmsNorm, gate/up + siluMul, w_down + residual. */
+ZWG_API int zwg_llm_layer_q8(zwg_llm_state* st, size_t layer, const zwg_llm_weights* w, float* x, size_t n_past,
+                             size_t n, void* scratch, size_t scratch_bytes, void* stream);
+
+/* Model.forward (src/llm.zig:169-216) for every sequence: tokens [n_batch][n] (device int32)
+ * at positions n_past.., hidden states left in x [n_batch][n][n_embd], and the logits of
+ * each sequence's last token in logits [n_batch][n_vocab]. */
+ZWG_API int zwg_llm_forward_q8(zwg_llm_state* st, const zwg_llm_weights* w, const int32_t* tokens, size_t n_past,
+                               size_t n, float* x, float* logits, void* scratch, size_t scratch_bytes,
+                               void* stream);
+
 /* Self-test of the timeout path every kernel relies on: launches one bounded device-side
  * wait on a barrier nothing ever completes (a few seconds), then synchronizes. Returns
  * ZWG_TIMEOUT when the wait ran out, was reported through the error word and left the

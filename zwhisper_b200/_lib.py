@@ -42,6 +42,32 @@ class BatchC(ctypes.Structure):
     ]
 
 
+class Q8MatC(ctypes.Structure):
+    """zwg_q8_mat: int8 [n][k] and f32 scales [n][k/32] on the device (gemm.Q8)."""
+
+    _fields_ = [("q", c_ptr), ("scales", c_ptr)]
+
+
+class LlmLayerWeightsC(ctypes.Structure):
+    """zwg_llm_layer_weights (llm.Layer, src/llm.zig:15-30, without the caches)."""
+
+    _fields_ = [
+        ("attn_norm", c_ptr), ("wq", Q8MatC), ("wk", Q8MatC), ("wv", Q8MatC), ("wo", Q8MatC),
+        ("bq", c_ptr), ("bk", c_ptr), ("bv", c_ptr), ("ffn_norm", c_ptr),
+        ("w_gate", Q8MatC), ("w_up", Q8MatC), ("w_down", Q8MatC),
+    ]
+
+
+class LlmWeightsC(ctypes.Structure):
+    """zwg_llm_weights (llm.Model's weights, src/llm.zig:32-60)."""
+
+    _fields_ = [
+        ("n_vocab", c_size), ("n_embd", c_size), ("n_ff", c_size), ("eps", ctypes.c_float),
+        ("embd", Q8MatC), ("output", Q8MatC), ("output_norm", c_ptr),
+        ("layers", ctypes.POINTER(LlmLayerWeightsC)),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/zwgpu.h declares
 SIGNATURES = {
     "zwg_version": (ctypes.c_int, []),
@@ -81,6 +107,20 @@ SIGNATURES = {
     "zwg_llm_append_rope": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_ptr, c_ptr, c_size, c_size, c_ptr]),
     "zwg_llm_attn_prefill": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_size, c_size, c_ptr, c_ptr]),
     "zwg_llm_attn_decode": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_size, c_ptr, c_ptr]),
+    "zwg_rms_norm": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, ctypes.c_float, c_ptr, c_ptr]),
+    "zwg_linear_q8_add": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_size, c_ptr, c_ptr]),
+    "zwg_linear_q8_silu_mul": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_ptr,
+                                              c_ptr]),
+    "zwg_embed_q8": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_ptr, c_size, c_size, c_ptr, c_ptr]),
+    "zwg_llm_greedy": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_size, c_size, c_size, ctypes.c_float, c_ptr,
+                                      c_size, c_ptr]),
+    "zwg_llm_qkv_q8": (ctypes.c_int, [c_ptr, c_size, c_ptr, ctypes.POINTER(LlmLayerWeightsC), c_size, c_size, c_ptr,
+                                      c_ptr]),
+    "zwg_llm_scratch_bytes": (c_size, [c_ptr, c_size, c_size]),
+    "zwg_llm_layer_q8": (ctypes.c_int, [c_ptr, c_size, ctypes.POINTER(LlmWeightsC), c_ptr, c_size, c_size, c_ptr,
+                                        c_size, c_ptr]),
+    "zwg_llm_forward_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(LlmWeightsC), c_ptr, c_size, c_size, c_ptr, c_ptr,
+                                          c_ptr, c_size, c_ptr]),
 }
 
 ZWG_DEC_SELF = 0

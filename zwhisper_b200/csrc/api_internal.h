@@ -1,10 +1,12 @@
 // Internals of the C-ABI layer shared by its source files (api.cu: contexts and the
-// attention entry points; state.cu: the library-owned decoder and LLM states).
+// attention entry points; state.cu: the library-owned decoder and LLM states; llm_api.cu:
+// the Qwen2 decode step around the attention).
 #pragma once
 #include <cuda_runtime.h>
 #include <stddef.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "../../include/zwgpu.h"
 
@@ -55,5 +57,29 @@ size_t workspace_bytes(const zwg_attn_shape* sh, size_t n_batch, int sm_count);
 int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
             const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st);
 
+// The calling thread's context, which must be on `device` (the device a state lives on);
+// nullptr with the last error set otherwise.
+Ctx* ctx_for(int device);
+
+}  // namespace capi
+}  // namespace zwg
+
+// Qwen2 LLM state (state.cu): the caches of every layer for n_batch sequences and the RoPE
+// tables, on one device.
+struct zwg_llm_state {
+    int device = -1;
+    size_t n_layer = 0, n_batch = 0, n_head = 0, n_head_kv = 0, d = 0, n_ctx = 0;
+    // per layer: cache_kt [n_batch][n_head_kv][d][n_ctx] (zeroed), cache_v [n_batch][n_ctx][n_head_kv*d]
+    std::vector<float*> cache_kt, cache_v;
+    float* cos_tab = nullptr;  // [n_ctx][d/2]
+    float* sin_tab = nullptr;
+    zwg::capi::DevBuf ws;
+};
+
+namespace zwg {
+namespace capi {
+// Causal GQA attention of q [n_batch][n][n_head*d] over one layer's caches, n_kv = n_past + n
+// (the body of zwg_llm_attn_prefill / _decode).
+int llm_attn(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, size_t n, float* out, void* stream);
 }  // namespace capi
 }  // namespace zwg

@@ -72,8 +72,42 @@ int prefill_tc_launch(const FlashParams& p, size_t n_batch, int sm_count, int* e
 
 // Q8 weights (q8.cu): Q8.quantize and ops.linear over int8 blocks of 32.
 int q8_quantize_launch(const float* w, size_t n, size_t k, int8_t* q, float* scales, cudaStream_t st);
+// out = x . W^T (+ bias); accum != 0 adds the result into out instead (the residual).
 int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
-                     size_t n, float* out, cudaStream_t st);
+                     size_t n, int accum, float* out, cudaStream_t st);
+
+// Paired-row Q8 products with a fused epilogue (q8.cu): PAIR_ROPE = the q/k/v projections
+// with bias, RoPE and the K^T / V cache append; PAIR_SILU = silu(x . Wg^T) * (x . Wu^T).
+enum { PAIR_ROPE = 0, PAIR_SILU = 1 };
+struct PairParams {
+    const float* x;  // [m][k], row t of the call is sequence t / n_tok, token t % n_tok
+    int m, k;
+    int m0;          // row of the call x[0] is (the launcher walks m in chunks)
+    const int8_t* wq[3];
+    const float* ws[3];
+    const float* bias[3];  // per matrix, may be null
+    int n_pairs;           // ROPE: (n_head + 2 n_head_kv) * d / 2; SILU: n_ff
+    // ROPE
+    int n_head, n_head_kv, d, n_tok, n_past, n_ctx;
+    const float* cos_tab;
+    const float* sin_tab;
+    float* q_out;     // [m][n_head * d]
+    float* cache_kt;  // sequence s at s * cache_bs: [n_head_kv][d][n_ctx]
+    float* cache_v;   // sequence s at s * cache_bs: [n_ctx][n_head_kv * d]
+    size_t cache_bs;
+    // SILU
+    float* out;  // [m][n_ff]
+};
+int q8_pair_launch(const PairParams& p, int epi, cudaStream_t st);
+
+// Decode-step kernels around the projections (llm_step.cu), chained launches.
+int rms_norm_launch(const float* x, size_t x_stride, size_t m, size_t n, const float* w, float eps, float* out,
+                    size_t out_stride, cudaStream_t st);
+int embed_q8_launch(const int32_t* tokens, size_t m, const int8_t* q, const float* scales, size_t n_vocab,
+                    size_t k, float* out, int* err, cudaStream_t st);
+int greedy_launch(float* logits, size_t m, size_t n_vocab, const int32_t* recent, size_t recent_stride,
+                  size_t n_recent, size_t window, float penalty, int32_t* out, size_t out_stride, int* err,
+                  cudaStream_t st);
 
 // One bounded wait that nothing completes (selftest.cu); gave_up is set to 1 when it ran out.
 int wait_timeout_selftest_launch(int* err, int* gave_up, cudaStream_t st);

@@ -1,0 +1,169 @@
+// The small kernels of a Qwen2 decode step around the projections and the attention
+// (src/llm.zig:168-216, 268-273, 313-321), launched as chained launches (chain.cuh) so
+// each one's start overlaps the end of the kernel before it.
+//
+// rms_norm_kernel: ops.rmsNorm (src/ops.zig:408-425), one CTA per row: the sum of squares
+//   (f32, tree order), inv = 1 / sqrt(ss / n + eps) with correctly rounded division and
+//   square root, out = x * inv * w as two rounded products in the reference's order.
+// embed_q8_kernel: Q8.row (src/gemm.zig:256-263) for the token of each row: q * scale in
+//   f32, bit-identical to the reference. A token outside the vocabulary writes a zero row
+//   and sets the device error word.
+// greedy_kernel: Model.penalize then Model.argmax (src/llm.zig:313-321, 268-273), one CTA
+//   per sequence: the repeat penalty applied in order by one thread over the last `window`
+//   generated tokens (repeats are penalized again, as in the reference), then the first
+//   index of the largest logit (NaN never wins; a NaN in column 0 makes the answer 0, as
+//   the reference's strict comparison does).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <climits>
+
+#include "chain.cuh"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace zwg {
+
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, size_t x_stride, int n,
+                                                       const float* __restrict__ w, float eps, float* out,
+                                                       size_t out_stride) {
+    chain_release();
+    const int z = chain_wait();
+    const float* row = x + blockIdx.x * x_stride + z;
+    float* o = out + blockIdx.x * out_stride + z;
+    float ss = 0.f;
+    for (int j = threadIdx.x * 4; j < n; j += 1024) {
+        const float4 v = __ldca(reinterpret_cast<const float4*>(row + j));
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    __shared__ float part[8];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) tot += part[i];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+    for (int j = threadIdx.x * 4; j < n; j += 1024) {
+        const float4 v = __ldca(reinterpret_cast<const float4*>(row + j));
+        const float4 g = __ldg(reinterpret_cast<const float4*>(w + j));
+        float4 r;
+        r.x = __fmul_rn(__fmul_rn(v.x, inv), g.x);
+        r.y = __fmul_rn(__fmul_rn(v.y, inv), g.y);
+        r.z = __fmul_rn(__fmul_rn(v.z, inv), g.z);
+        r.w = __fmul_rn(__fmul_rn(v.w, inv), g.w);
+        *reinterpret_cast<float4*>(o + j) = r;
+    }
+}
+
+__global__ void __launch_bounds__(256) embed_q8_kernel(const int32_t* tokens, const int8_t* __restrict__ q,
+                                                       const float* __restrict__ scales, int n_vocab, int k,
+                                                       float* out, int* err) {
+    chain_release();
+    const int z = chain_wait();
+    const int t = __ldcg(tokens + blockIdx.x + z);
+    float* o = out + (size_t)blockIdx.x * k + z;
+    if (t < 0 || t >= n_vocab) {
+        for (int j = threadIdx.x; j < k; j += blockDim.x) o[j] = 0.f;
+        if (threadIdx.x == 0) set_error(err, kErrBounds);
+        return;
+    }
+    const int8_t* qr = q + (size_t)t * k;
+    const float* sr = scales + (size_t)t * (k / 32);
+    for (int j = threadIdx.x; j < k; j += blockDim.x) o[j] = __fmul_rn((float)__ldg(qr + j), __ldg(sr + (j >> 5)));
+}
+
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+__global__ void __launch_bounds__(1024) greedy_kernel(float* logits, int n_vocab, const int32_t* recent,
+                                                      size_t recent_stride, int n_recent, int window, float penalty,
+                                                      int32_t* out, size_t out_stride, int* err) {
+    chain_release();
+    const int z = chain_wait();
+    float* row = logits + (size_t)blockIdx.x * n_vocab + z;
+    if (threadIdx.x == 0 && penalty > 1.0f && n_recent > 0) {
+        const int32_t* rc = recent + blockIdx.x * recent_stride + z;
+        const int from = n_recent > window ? n_recent - window : 0;
+        for (int i = from; i < n_recent; i++) {
+            const int t = __ldcg(rc + i);
+            if (t < 0 || t >= n_vocab) {
+                set_error(err, kErrBounds);
+                continue;
+            }
+            const float v = __ldcg(row + t);
+            __stcg(row + t, v > 0.f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty));
+        }
+    }
+    __syncthreads();
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int j = threadIdx.x; j < n_vocab; j += blockDim.x) better(bv, bi, __ldcg(row + j), j);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        better(bv, bi, ov, oi);
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : INT_MAX;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            better(bv, bi, ov, oi);
+        }
+        if (lane == 0) {
+            const float first = __ldcg(row);
+            out[blockIdx.x * out_stride + z] = (isnan(first) || bi == INT_MAX) ? 0 : bi;
+        }
+    }
+}
+
+int rms_norm_launch(const float* x, size_t x_stride, size_t m, size_t n, const float* w, float eps, float* out,
+                    size_t out_stride, cudaStream_t st) {
+    if (m == 0) return 0;
+    return launch_chained(rms_norm_kernel, dim3((unsigned)m), dim3(256), st, x, x_stride, (int)n, w, eps, out,
+                          out_stride) == cudaSuccess
+               ? 0
+               : -1;
+}
+
+int embed_q8_launch(const int32_t* tokens, size_t m, const int8_t* q, const float* scales, size_t n_vocab, size_t k,
+                    float* out, int* err, cudaStream_t st) {
+    if (m == 0) return 0;
+    return launch_chained(embed_q8_kernel, dim3((unsigned)m), dim3(256), st, tokens, q, scales, (int)n_vocab, (int)k,
+                          out, err) == cudaSuccess
+               ? 0
+               : -1;
+}
+
+int greedy_launch(float* logits, size_t m, size_t n_vocab, const int32_t* recent, size_t recent_stride,
+                  size_t n_recent, size_t window, float penalty, int32_t* out, size_t out_stride, int* err,
+                  cudaStream_t st) {
+    if (m == 0) return 0;
+    return launch_chained(greedy_kernel, dim3((unsigned)m), dim3(1024), st, logits, (int)n_vocab, recent,
+                          recent_stride, (int)n_recent, (int)window, penalty, out, out_stride, err) == cudaSuccess
+               ? 0
+               : -1;
+}
+
+}  // namespace zwg

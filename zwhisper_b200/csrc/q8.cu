@@ -1,4 +1,4 @@
-// Q8 weights on the GPU: quantization and the linear layer over int8 blocks.
+// Q8 weights on the GPU: quantization and the linear layers over int8 blocks.
 //
 // Reference: gemm.Q8 (src/gemm.zig:188-263): a weight matrix [n][k] stored as int8 with one
 // f32 scale per block of 32 along k (scale = absmax / 127); ops.linear (src/ops.zig:280-306)
@@ -11,19 +11,37 @@
 //   max over the bit patterns of |v|, scale = absmax / 127 and q = clamp(round(v * (127 /
 //   absmax)), -127, 127) with the reference's f32 operations and round-half-away, so the
 //   int8 values and scales are bit-identical to Q8.quantize.
-// q8_linear_kernel<MR>: the decode-shaped product (m <= 8 rows of x per launch; larger m in
-//   chunks of 8). The weight bytes are the traffic (1.125 B per weight with the scales), so
-//   the kernel streams them once: a warp owns 1-4 weight rows, lane l reads 16 (8 for MR = 8)
-//   consecutive int8 of each row per step (one 128-bit load, a 512-byte coalesced row
-//   segment per warp), widens them to f32 exactly (byte permute into a 2^23 float, then one
-//   subtraction), takes the dot with the same k range of every x row (rows in pairs per
-//   packed f32x2 FMA) and scales it by the block's scale. Warp shuffles sum the lanes; the
-//   bias is added on the way out.
+// q8_linear_kernel<MR, RW>: the decode-shaped product (m <= 8 rows of x per launch; larger m
+//   in chunks of 8). The weight bytes are the traffic (1.125 B per weight with the scales),
+//   so the kernel streams them once: a warp owns RW = 1-4 weight rows, lane l reads 16 (8
+//   for MR = 8) consecutive int8 of each row per step (one 128-bit load, a 512-byte
+//   coalesced row segment per warp), widens them to f32 exactly (byte permute into a 2^23
+//   float, then one subtraction), takes the dot with the same k range of every x row (rows
+//   in pairs per packed f32x2 FMA) and scales it by the block's scale. Warp shuffles sum the
+//   lanes; the bias is added on the way out, or the result is added into `out` (the
+//   residual: ops.linear then ops.add, src/llm.zig:203-204, 209-210).
+// q8_pair_kernel<MR, RP, EPI>: the same dot products for two matrices' rows at once, a warp
+//   owning RP pairs of rows whose outputs one epilogue combines:
+//   - PAIR_ROPE: rows i and i + d/2 of one head of the q, k or v projection
+//     (src/llm.zig:179-181): bias, then the NeoX rotation at position n_past + t
+//     (src/llm.zig:221-238) for q and k; q goes to its output, k into the transposed cache
+//     and v into the value cache (src/llm.zig:182-190). One launch replaces three linears,
+//     two rope passes and the scatter.
+//   - PAIR_SILU: row j of w_gate and of w_up (src/llm.zig:206-208): silu(g) * u
+//     (ops.siluMul, src/ops.zig:435-440). One launch replaces two linears and the product.
+//
+// Launch chaining: every Q8 kernel is launched as a programmatic dependent launch. It
+// first hints its own weight rows into L2 (they are constants of the model, not outputs
+// of the kernel before it), lets the next kernel in the stream launch, and only then
+// waits for the previous kernel's results (griddepcontrol.wait) before reading x or
+// writing anything. In a chain of projections each kernel's weight stream therefore
+// starts while its predecessor is still running.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <algorithm>
 
+#include "chain.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -60,27 +78,42 @@ __device__ __forceinline__ float i8f(uint32_t ub, int j) {
     return __uint_as_float(__byte_perm(ub, 0x4B000000u, 0x7650u | (uint32_t)j)) - 8388736.0f;  // 2^23 + 128
 }
 
+// Programmatic dependent launch: hint this warp's weight rows and scales into L2, let the
+// next grid launch, then wait until the previous grid's writes are visible. Safe whether
+// or not the grid was launched as a dependent (the wait returns at once when it was not).
+// Returns the opaque zero of chain_wait, added to the row pointers here and to x by the
+// callers.
+template <int RW>
+__device__ __forceinline__ int chain_prologue(const int8_t* (&wr)[RW], const float* (&sr)[RW], int k, int lane) {
+    const int nb = k / BLOCK;
+#pragma unroll
+    for (int r = 0; r < RW; r++) {
+        const uintptr_t w0 = (uintptr_t)wr[r] & ~(uintptr_t)127;
+        const int wl = (int)(((uintptr_t)wr[r] + k - 1 - w0) >> 7) + 1;  // 128-byte lines of the row
+        for (int i = lane; i < wl; i += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(w0 + ((uintptr_t)i << 7)));
+        const uintptr_t s0 = (uintptr_t)sr[r] & ~(uintptr_t)127;
+        const int sl = (int)(((uintptr_t)sr[r] + nb * 4 - 1 - s0) >> 7) + 1;
+        for (int i = lane; i < sl; i += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(s0 + ((uintptr_t)i << 7)));
+    }
+    chain_release();
+    const int z = chain_wait();
+#pragma unroll
+    for (int r = 0; r < RW; r++) {
+        wr[r] += z;
+        sr[r] += z;
+    }
+    return z;
+}
+
+// The dot products of RW weight rows with MR rows of x (rows >= m read row 0 and count as
+// zero), summed over the warp: every lane ends with every total. acc[r][p] holds x rows
+// 2p and 2p + 1 against weight row r.
 template <int MR, int RW>
-__global__ void __launch_bounds__(256, MR >= 4 ? 1 : 3) q8_linear_kernel(const float* __restrict__ x, int m, int k,
-                                                        const int8_t* __restrict__ wq, const float* __restrict__ ws,
-                                                        const float* __restrict__ bias, int n,
-                                                        float* __restrict__ out) {
+__device__ __forceinline__ void dot_rows(const float* x, int m, int k, const int8_t* const (&wr)[RW],
+                                         const float* const (&sr)[RW], int lane, float2 (&acc)[RW][(MR + 1) / 2]) {
     constexpr int KL = MR >= 8 ? 8 : 16;  // k per lane per step
     constexpr int MP = (MR + 1) / 2;      // x row pairs
     constexpr int UNR = (MR <= 2 && RW == 1) ? 4 : 1;  // k steps unrolled per lane
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = (blockIdx.x * WARPS + warp) * RW;
-    if (row0 >= n) return;
-    const int nb = k / BLOCK;
-    const int8_t* wr[RW];
-    const float* sr[RW];
-#pragma unroll
-    for (int r = 0; r < RW; r++) {
-        const int row = min(row0 + r, n - 1);  // rows past n repeat the last row; not stored
-        wr[r] = wq + (size_t)row * k;
-        sr[r] = ws + (size_t)row * nb;
-    }
-    float2 acc[RW][MP];
 #pragma unroll
     for (int r = 0; r < RW; r++)
 #pragma unroll
@@ -95,7 +128,7 @@ __global__ void __launch_bounds__(256, MR >= 4 ? 1 : 3) q8_linear_kernel(const f
             const int row = mr < m ? mr : 0;
 #pragma unroll
             for (int i = 0; i < KL; i += 4) {
-                const float4 f = __ldg(reinterpret_cast<const float4*>(x + (size_t)row * k + k0 + i));
+                const float4 f = __ldca(reinterpret_cast<const float4*>(x + (size_t)row * k + k0 + i));
                 xv[mr][i] = mr < m ? f.x : 0.f;
                 xv[mr][i + 1] = mr < m ? f.y : 0.f;
                 xv[mr][i + 2] = mr < m ? f.z : 0.f;
@@ -145,16 +178,163 @@ __global__ void __launch_bounds__(256, MR >= 4 ? 1 : 3) q8_linear_kernel(const f
                 acc[r][p].x += __shfl_xor_sync(0xffffffffu, acc[r][p].x, off);
                 acc[r][p].y += __shfl_xor_sync(0xffffffffu, acc[r][p].y, off);
             }
+}
+
+template <int MR, int RW>
+__global__ void __launch_bounds__(256, MR >= 4 ? 1 : 3) q8_linear_kernel(const float* x, int m, int k,
+                                                        const int8_t* __restrict__ wq, const float* __restrict__ ws,
+                                                        const float* __restrict__ bias, int n, int accum,
+                                                        float* out) {
+    constexpr int MP = (MR + 1) / 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * WARPS + warp) * RW;
+    const int nb = k / BLOCK;
+    const int8_t* wr[RW];
+    const float* sr[RW];
+#pragma unroll
+    for (int r = 0; r < RW; r++) {
+        const int row = min(row0 + r, n - 1);  // rows past n repeat the last row; not stored
+        wr[r] = wq + (size_t)row * k;
+        sr[r] = ws + (size_t)row * nb;
+    }
+    const int z = chain_prologue<RW>(wr, sr, k, lane);
+    if (row0 >= n) return;
+    x += z;
+    out += z;
+    float2 acc[RW][MP];
+    dot_rows<MR, RW>(x, m, k, wr, sr, lane, acc);
     // lane r * MR + mr writes out[mr][row0 + r]
 #pragma unroll
     for (int r = 0; r < RW; r++)
 #pragma unroll
         for (int mr = 0; mr < MR; mr++) {
             if (lane == r * MR + mr && mr < m && row0 + r < n) {
-                const float v = (mr & 1) ? acc[r][mr >> 1].y : acc[r][mr >> 1].x;
-                out[(size_t)mr * n + row0 + r] = bias ? v + bias[row0 + r] : v;
+                float v = (mr & 1) ? acc[r][mr >> 1].y : acc[r][mr >> 1].x;
+                if (bias) v = __fadd_rn(v, bias[row0 + r]);
+                float* o = out + (size_t)mr * n + row0 + r;
+                *o = accum ? __fadd_rn(__ldcg(o), v) : v;
             }
         }
+}
+
+template <int MR, int RP, int EPI>
+__global__ void __launch_bounds__(256, MR >= 4 ? 1 : RP == 2 ? 2 : 3) q8_pair_kernel(const PairParams p) {
+    constexpr int RW = 2 * RP;
+    constexpr int MP = (MR + 1) / 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pair0 = (blockIdx.x * WARPS + warp) * RP;
+    const int k = p.k, nb = k / BLOCK;
+    // rows of the two matrices this warp reads: r < RP the first of each pair, r >= RP the second
+    int sec = 0, head = 0, i0 = 0;
+    const int8_t* wr[RW];
+    const float* sr[RW];
+    {
+        const int pc = min(pair0, p.n_pairs - 1);  // pairs past the end repeat the last; not stored
+        int ra, rb, ma, mb;
+        if (EPI == PAIR_ROPE) {
+            const int half = p.d >> 1;
+            const int hh = pc / half;
+            i0 = pc - hh * half;
+            sec = hh < p.n_head ? 0 : hh < p.n_head + p.n_head_kv ? 1 : 2;
+            head = sec == 0 ? hh : sec == 1 ? hh - p.n_head : hh - p.n_head - p.n_head_kv;
+            ra = head * p.d + i0;
+            rb = ra + half;
+            ma = mb = sec;
+        } else {
+            i0 = pc;
+            ra = rb = pc;
+            ma = 0;
+            mb = 1;
+        }
+        const int n_rows_a = EPI == PAIR_ROPE ? (sec == 0 ? p.n_head : p.n_head_kv) * p.d : p.n_pairs;
+#pragma unroll
+        for (int r = 0; r < RP; r++) {
+            const int a = min(ra + r, n_rows_a - 1), b = min(rb + r, n_rows_a - 1);
+            wr[r] = p.wq[ma] + (size_t)a * k;
+            sr[r] = p.ws[ma] + (size_t)a * nb;
+            wr[RP + r] = p.wq[mb] + (size_t)b * k;
+            sr[RP + r] = p.ws[mb] + (size_t)b * nb;
+        }
+    }
+    const int z = chain_prologue<RW>(wr, sr, k, lane);
+    if (pair0 >= p.n_pairs) return;
+    float2 acc[RW][MP];
+    dot_rows<MR, RW>(p.x + z, p.m, k, wr, sr, lane, acc);
+
+    // lane rp * MR + mr finishes pair pair0 + rp for x row mr
+    float va = 0.f, vb = 0.f;
+    int rp_sel = -1, mr_sel = 0;
+#pragma unroll
+    for (int rp = 0; rp < RP; rp++)
+#pragma unroll
+        for (int mr = 0; mr < MR; mr++)
+            if (lane == rp * MR + mr) {
+                va = (mr & 1) ? acc[rp][mr >> 1].y : acc[rp][mr >> 1].x;
+                vb = (mr & 1) ? acc[RP + rp][mr >> 1].y : acc[RP + rp][mr >> 1].x;
+                rp_sel = rp;
+                mr_sel = mr;
+            }
+    if (rp_sel < 0 || mr_sel >= p.m || pair0 + rp_sel >= p.n_pairs) return;
+    const int tok = p.m0 + mr_sel;  // row of x over the whole call: sequence * n_tok + t
+    if (EPI == PAIR_ROPE) {
+        const int half = p.d >> 1;
+        const int i = i0 + rp_sel;
+        const int ra = head * p.d + i;
+        const float* bias = p.bias[sec];
+        if (bias) {
+            va = __fadd_rn(va, bias[ra]);
+            vb = __fadd_rn(vb, bias[ra + half]);
+        }
+        const int seq = tok / p.n_tok, t = tok - seq * p.n_tok;
+        const size_t pos = (size_t)p.n_past + t;
+        const size_t kvw = (size_t)p.n_head_kv * p.d;
+        if (sec == 2) {
+            float* cv = p.cache_v + (size_t)seq * p.cache_bs + pos * kvw + ra;
+            cv[0] = va;
+            cv[half] = vb;
+            return;
+        }
+        // separately rounded products and sums, as the reference's rope
+        const float c = p.cos_tab[pos * half + i], s = p.sin_tab[pos * half + i];
+        const float lo = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+        const float hi = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
+        if (sec == 0) {
+            float* qo = p.q_out + (size_t)tok * p.n_head * p.d + ra;
+            qo[0] = lo;
+            qo[half] = hi;
+        } else {
+            float* kt = p.cache_kt + (size_t)seq * p.cache_bs;
+            kt[(size_t)ra * p.n_ctx + pos] = lo;
+            kt[(size_t)(ra + half) * p.n_ctx + pos] = hi;
+        }
+    } else {
+        // gate / (1 + exp(-gate)) * up
+        const float sg = __fdiv_rn(va, __fadd_rn(1.0f, expf(-va)));
+        p.out[(size_t)tok * p.n_pairs + i0 + rp_sel] = __fmul_rn(sg, vb);
+    }
+}
+
+// Weight rows per warp for an x chunk of mc rows and rows of k.
+inline int rows_per_warp(int mc, size_t k) {
+    if (mc > 2) return 4;
+    return k <= 512 ? 4 : k <= 1536 ? 2 : 1;
+}
+
+template <int MR>
+cudaError_t linear_chunk(int rw, unsigned grid, cudaStream_t st, const float* x, int mc, int k, const int8_t* wq,
+                         const float* ws, const float* bias, int n, int accum, float* out) {
+    if (rw == 4) return launch_chained(q8_linear_kernel<MR, 4>, dim3(grid), dim3(32 * WARPS), st, x, mc, k, wq, ws, bias, n, accum, out);
+    if constexpr (MR <= 2) {
+        if (rw == 2) return launch_chained(q8_linear_kernel<MR, 2>, dim3(grid), dim3(32 * WARPS), st, x, mc, k, wq, ws, bias, n, accum, out);
+        return launch_chained(q8_linear_kernel<MR, 1>, dim3(grid), dim3(32 * WARPS), st, x, mc, k, wq, ws, bias, n, accum, out);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int MR, int EPI>
+cudaError_t pair_chunk(int rp, unsigned grid, cudaStream_t st, const PairParams& p) {
+    if (rp == 2) return launch_chained(q8_pair_kernel<MR, 2, EPI>, dim3(grid), dim3(32 * WARPS), st, p);
+    return launch_chained(q8_pair_kernel<MR, 1, EPI>, dim3(grid), dim3(32 * WARPS), st, p);
 }
 
 }  // namespace q8
@@ -169,30 +349,49 @@ int q8_quantize_launch(const float* w, size_t n, size_t k, int8_t* q, float* sca
 }
 
 int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
-                     size_t n, float* out, cudaStream_t st) {
+                     size_t n, int accum, float* out, cudaStream_t st) {
     if (m == 0 || n == 0) return 0;
-    const int rw = k <= 512 ? 4 : k <= 1536 ? 2 : 1;  // weight rows per warp for 1-2 x rows
     for (size_t m0 = 0; m0 < m; m0 += 8) {
         const int mc = (int)std::min<size_t>(8, m - m0);
         const float* xc = x + m0 * k;
         float* oc = out + m0 * n;
-        const int r = mc <= 2 ? rw : 4;
+        const int r = q8::rows_per_warp(mc, k);
         const unsigned grid = (unsigned)((n + q8::WARPS * r - 1) / (q8::WARPS * r));
         const int ik = (int)k, in = (int)n;
-        if (mc == 1) {
-            if (r == 4) q8::q8_linear_kernel<1, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
-            else if (r == 2) q8::q8_linear_kernel<1, 2><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
-            else q8::q8_linear_kernel<1, 1><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
-        } else if (mc == 2) {
-            if (r == 4) q8::q8_linear_kernel<2, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
-            else if (r == 2) q8::q8_linear_kernel<2, 2><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
-            else q8::q8_linear_kernel<2, 1><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
-        } else if (mc <= 4) {
-            q8::q8_linear_kernel<4, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+        cudaError_t e;
+        if (mc == 1) e = q8::linear_chunk<1>(r, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
+        else if (mc == 2) e = q8::linear_chunk<2>(r, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
+        else if (mc <= 4) e = q8::linear_chunk<4>(r, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
+        else e = q8::linear_chunk<8>(r, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
+        if (e != cudaSuccess) return -1;
+    }
+    return 0;
+}
+
+int q8_pair_launch(const PairParams& p0, int epi, cudaStream_t st) {
+    if (p0.m == 0 || p0.n_pairs == 0) return 0;
+    PairParams p = p0;
+    for (int m0 = 0; m0 < p0.m; m0 += 8) {
+        const int mc = std::min(8, p0.m - m0);
+        p.x = p0.x + (size_t)m0 * p0.k;
+        p.m = mc;
+        p.m0 = p0.m0 + m0;
+        int rp = q8::rows_per_warp(mc, (size_t)p0.k) >= 4 ? 2 : 1;
+        if (epi == PAIR_ROPE && (p0.d / 2) % rp) rp = 1;
+        const unsigned grid = (unsigned)((p0.n_pairs + q8::WARPS * rp - 1) / (q8::WARPS * rp));
+        cudaError_t e;
+        if (epi == PAIR_ROPE) {
+            if (mc == 1) e = q8::pair_chunk<1, PAIR_ROPE>(rp, grid, st, p);
+            else if (mc == 2) e = q8::pair_chunk<2, PAIR_ROPE>(rp, grid, st, p);
+            else if (mc <= 4) e = q8::pair_chunk<4, PAIR_ROPE>(rp, grid, st, p);
+            else e = q8::pair_chunk<8, PAIR_ROPE>(rp, grid, st, p);
         } else {
-            q8::q8_linear_kernel<8, 4><<<grid, 256, 0, st>>>(xc, mc, ik, wq, ws, bias, in, oc);
+            if (mc == 1) e = q8::pair_chunk<1, PAIR_SILU>(rp, grid, st, p);
+            else if (mc == 2) e = q8::pair_chunk<2, PAIR_SILU>(rp, grid, st, p);
+            else if (mc <= 4) e = q8::pair_chunk<4, PAIR_SILU>(rp, grid, st, p);
+            else e = q8::pair_chunk<8, PAIR_SILU>(rp, grid, st, p);
         }
-        if (cudaPeekAtLastError() != cudaSuccess) return -1;
+        if (e != cudaSuccess) return -1;
     }
     return 0;
 }

@@ -23,16 +23,6 @@ struct zwg_dec_state {
     DevBuf ws;
 };
 
-struct zwg_llm_state {
-    int device = -1;
-    size_t n_layer = 0, n_batch = 0, n_head = 0, n_head_kv = 0, d = 0, n_ctx = 0;
-    // per layer: cache_kt [n_batch][n_head_kv][d][n_ctx] (zeroed), cache_v [n_batch][n_ctx][n_head_kv*d]
-    std::vector<float*> cache_kt, cache_v;
-    float* cos_tab = nullptr;  // [n_ctx][d/2]
-    float* sin_tab = nullptr;
-    DevBuf ws;
-};
-
 namespace {
 
 void free_all(std::vector<float*>& v) {
@@ -51,15 +41,6 @@ int alloc_layers(std::vector<float*>& v, size_t n_layer, size_t floats, bool zer
     return ZWG_OK;
 }
 
-// The calling thread's context, which must be on the state's device.
-Ctx* ctx_for(int device) {
-    Ctx* c = cur();
-    if (c && c->device != device) {
-        fail("state belongs to device %d, the calling thread is bound to device %d", device, c->device);
-        return nullptr;
-    }
-    return c;
-}
 
 zwg_attn_shape mha(size_t n_q, size_t n_kv, size_t n_state, size_t n_head, bool causal) {
     return zwg_attn_shape{n_q, n_kv, n_head, n_head, n_state / n_head, n_state, n_state, n_state, causal ? 1 : 0, 0};
@@ -74,6 +55,34 @@ int ensure_ws(DevBuf& ws, const zwg_attn_shape* sh, size_t n_batch, int sm_count
 }
 
 }  // namespace
+
+Ctx* zwg::capi::ctx_for(int device) {
+    Ctx* c = cur();
+    if (c && c->device != device) {
+        fail("state belongs to device %d, the calling thread is bound to device %d", device, c->device);
+        return nullptr;
+    }
+    return c;
+}
+
+int zwg::capi::llm_attn(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, size_t n, float* out,
+                        void* stream) {
+    if (!st || layer >= st->n_layer) return fail("llm attention: bad state or layer");
+    if (n == 0) return ZWG_OK;
+    if (!q || !out) return fail("llm attention: null q/out");
+    if (n_past + n > st->n_ctx) return fail("llm attention: context full (%zu + %zu > %zu)", n_past, n, st->n_ctx);
+    Ctx* c = ctx_for(st->device);
+    if (!c) return ZWG_ERROR;
+    const size_t H = st->n_head, Hkv = st->n_head_kv, d = st->d, n_ctx = st->n_ctx;
+    // the reference's call (src/llm.zig:191-202), over every sequence of the batch
+    zwg_attn_shape sh{n, n_past + n, H, Hkv, d, H * d, Hkv * d, H * d, 1, n_ctx};
+    zwg_batch b{st->n_batch, n * H * d, Hkv * d * n_ctx, n_ctx * Hkv * d, n * H * d};
+    int rc = check_shape(&sh);
+    if (!rc) rc = ensure_ws(st->ws, &sh, st->n_batch, c->sm_count);
+    if (rc) return rc;
+    return run_dev(c, &sh, &b, q, st->cache_kt[layer], st->cache_v[layer], out, st->ws.ptr, st->ws.cap,
+                   (cudaStream_t)stream);
+}
 
 extern "C" {
 
@@ -285,24 +294,6 @@ int zwg_llm_append_rope(zwg_llm_state* st, size_t layer, float* q, const float* 
     return ZWG_OK;
 }
 
-static int llm_attn(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, size_t n, float* out,
-                    void* stream) {
-    if (!st || layer >= st->n_layer) return fail("llm attention: bad state or layer");
-    if (n == 0) return ZWG_OK;
-    if (!q || !out) return fail("llm attention: null q/out");
-    if (n_past + n > st->n_ctx) return fail("llm attention: context full (%zu + %zu > %zu)", n_past, n, st->n_ctx);
-    Ctx* c = ctx_for(st->device);
-    if (!c) return ZWG_ERROR;
-    const size_t H = st->n_head, Hkv = st->n_head_kv, d = st->d, n_ctx = st->n_ctx;
-    // the reference's call (src/llm.zig:191-202), over every sequence of the batch
-    zwg_attn_shape sh{n, n_past + n, H, Hkv, d, H * d, Hkv * d, H * d, 1, n_ctx};
-    zwg_batch b{st->n_batch, n * H * d, Hkv * d * n_ctx, n_ctx * Hkv * d, n * H * d};
-    int rc = check_shape(&sh);
-    if (!rc) rc = ensure_ws(st->ws, &sh, st->n_batch, c->sm_count);
-    if (rc) return rc;
-    return run_dev(c, &sh, &b, q, st->cache_kt[layer], st->cache_v[layer], out, st->ws.ptr, st->ws.cap,
-                   (cudaStream_t)stream);
-}
 
 int zwg_llm_attn_prefill(zwg_llm_state* st, size_t layer, const float* q, size_t n_past, size_t n, float* out,
                          void* stream) {

@@ -11,7 +11,11 @@ Same names, argument meaning and error behaviour as the reference:
 Shape violations the reference asserts on (src/ops.zig:564-568) raise ValueError here.
 
 Device entry points (torch tensors on a CUDA device, stream ordered on the current torch
-stream): `attention_dev`, `enc_attn_bf16`, `rope_kt_append`, `f32_to_bf16`.
+stream): `attention_dev`, `enc_attn_bf16`, `rope_kt_append`, `f32_to_bf16`; the library-owned
+states `DecoderState` and `LlmState`; the Q8 projections `quantize_q8`, `linear_q8`,
+`linear_q8_add`, `linear_q8_silu_mul`; and the rest of the Qwen2 decode step (src/llm.zig:
+168-216, 268-321): `rms_norm`, `embed_q8`, `llm_greedy`, `LlmWeightsQ8` with
+`LlmState.qkv_q8 / layer_q8 / forward_q8`.
 """
 from __future__ import annotations
 
@@ -339,6 +343,14 @@ class DecoderState:
         return out
 
 
+class _DeviceArray:
+    """A float32 device buffer described by __cuda_array_interface__ (for zero-copy views)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
 class LlmState:
     """Qwen2 attention state on one device (zwg_llm_state): per layer cache_kt
     [n_batch][n_head_kv][d][n_ctx] and cache_v [n_batch][n_ctx][n_head_kv*d], RoPE tables in
@@ -371,6 +383,16 @@ class LlmState:
         _lib.check(_lib.load().zwg_llm_state_cache(self._h, layer, ctypes.byref(kt), ctypes.byref(v)))
         return kt.value, v.value
 
+    def cache_views(self, layer: int):
+        """Torch views (no copy) of one layer's caches: cache_kt [n_batch][n_head_kv][d][n_ctx]
+        and cache_v [n_batch][n_ctx][n_head_kv*d]. Valid until close()."""
+        torch = _torch()
+        kt, v = self.cache_ptrs(layer)
+        dev = torch.device("cuda", self.device)
+        shapes = ((self.n_batch, self.n_head_kv, self.d, self.n_ctx),
+                  (self.n_batch, self.n_ctx, self.n_head_kv * self.d))
+        return tuple(torch.as_tensor(_DeviceArray(p, shp), device=dev) for p, shp in zip((kt, v), shapes))
+
     def append_rope(self, layer: int, q, k, v, n_past: int) -> None:
         """RoPE on q (in place) and k, cache append at n_past.. (src/llm.zig:180-190)."""
         torch = _torch()
@@ -398,6 +420,62 @@ class LlmState:
                                           _dev_ptr(out, torch.float32, "out"), _stream_of(q))
         _lib.check(rc)
         return out
+
+    def qkv_q8(self, layer: int, x, weights: "LlmWeightsQ8", n_past: int, q_out=None):
+        """The q/k/v projections with bias, RoPE and the cache append in one launch
+        (src/llm.zig:179-190): x [n_batch][n][n_head*d] normed hidden states; returns the rotated
+        q and writes k, v into the layer's caches at n_past.."""
+        torch = _torch()
+        width = self.n_head * self.d
+        n = x.numel() // (self.n_batch * width)
+        _check_rows(x, self.n_batch, n, width, "x")
+        q_out = torch.empty_like(x) if q_out is None else q_out
+        lw = weights.layer_c(layer)
+        _lib.check(_lib.load().zwg_llm_qkv_q8(self._h, layer, _dev_ptr(x, torch.float32, "x"), ctypes.byref(lw), n_past,
+                                              n, _dev_ptr(q_out, torch.float32, "q_out"), _stream_of(x)))
+        return q_out
+
+
+    def scratch(self, n: int, n_ff: int, scratch=None):
+        """A CUDA uint8 buffer of at least zwg_llm_scratch_bytes for chunks of n tokens."""
+        torch = _torch()
+        need = _lib.load().zwg_llm_scratch_bytes(self._h, n, n_ff)
+        if scratch is None or scratch.numel() < need:
+            scratch = torch.empty(max(need, 256), dtype=torch.uint8, device=torch.device("cuda", self.device))
+        return scratch
+
+
+    def layer_q8(self, layer: int, weights: "LlmWeightsQ8", x, n_past: int, scratch=None):
+        """One layer of Model.forward (src/llm.zig:177-210) on x [n_batch][n][n_embd], in place."""
+        torch = _torch()
+        n = x.numel() // (self.n_batch * weights.n_embd)
+        _check_rows(x, self.n_batch, n, weights.n_embd, "x")
+        scratch = self.scratch(n, weights.n_ff, scratch)
+        _lib.check(_lib.load().zwg_llm_layer_q8(self._h, layer, ctypes.byref(weights.c_struct()),
+                                                _dev_ptr(x, torch.float32, "x"), n_past, n, scratch.data_ptr(),
+                                                scratch.numel(), _stream_of(x)))
+        return x
+
+
+    def forward_q8(self, weights: "LlmWeightsQ8", tokens, n_past: int, x=None, logits=None, scratch=None):
+        """Model.forward (src/llm.zig:169-216) for every sequence: tokens CUDA int32
+        [n_batch][n] at positions n_past..; returns (x [n_batch][n][n_embd], logits
+        [n_batch][n_vocab] of each sequence's last token)."""
+        torch = _torch()
+        if tokens.dtype != torch.int32 or not tokens.is_contiguous() or tokens.numel() % self.n_batch:
+            raise ValueError("tokens must be a contiguous int32 [n_batch][n] tensor")
+        n = tokens.numel() // self.n_batch
+        dev = tokens.device
+        if x is None:
+            x = torch.empty(self.n_batch, n, weights.n_embd, dtype=torch.float32, device=dev)
+        if logits is None:
+            logits = torch.empty(self.n_batch, weights.n_vocab, dtype=torch.float32, device=dev)
+        scratch = self.scratch(n, weights.n_ff, scratch)
+        _lib.check(_lib.load().zwg_llm_forward_q8(self._h, ctypes.byref(weights.c_struct()), tokens.data_ptr(), n_past,
+                                                  n, _dev_ptr(x, torch.float32, "x"),
+                                                  _dev_ptr(logits, torch.float32, "logits"), scratch.data_ptr(),
+                                                  scratch.numel(), _stream_of(tokens)))
+        return x, logits
 
 
 # ---- Q8 weights (zwg_q8_quantize / zwg_linear_q8) ------------------------------------------
@@ -431,3 +509,154 @@ def linear_q8(x, q, scales, bias=None, out=None):
         _dev_ptr(bias, torch.float32, "bias") if bias is not None else None, n,
         _dev_ptr(out, torch.float32, "out"), _stream_of(x)))
     return out
+
+
+# ---- the Qwen2 decode step around the attention (src/llm.zig:168-216, 268-321) -----------
+
+def _q8_pair(w, name):
+    """(q int8 [n][k], scales f32 [n][k/32]) on the device, checked."""
+    torch = _torch()
+    q, s = w
+    if q.dtype != torch.int8 or not q.is_cuda or not q.is_contiguous():
+        raise ValueError(f"{name}: q must be a contiguous CUDA int8 tensor")
+    if s.numel() != q.shape[0] * (q.shape[1] // 32):
+        raise ValueError(f"{name}: scales must hold n * k / 32 floats")
+    return q, _dev_ptr(s, torch.float32, f"{name} scales")
+
+
+def rms_norm(x, w, eps: float, out=None):
+    """ops.rmsNorm (src/ops.zig:408-425) of the rows of a CUDA f32 [m][n] tensor."""
+    torch = _torch()
+    n = x.shape[-1]
+    m = x.numel() // n
+    out = torch.empty_like(x) if out is None else out
+    _lib.ensure_init(x.device.index or 0)
+    _lib.check(_lib.load().zwg_rms_norm(_dev_ptr(x, torch.float32, "x"), m, n, _dev_ptr(w, torch.float32, "w"),
+                                        float(eps), _dev_ptr(out, torch.float32, "out"), _stream_of(x)))
+    return out
+
+
+def linear_q8_add(x, q, scales, out):
+    """out += x . W^T (ops.linear then ops.add, src/llm.zig:203-204) with Q8 W; returns out."""
+    torch = _torch()
+    m, k = x.shape
+    q, sp = _q8_pair((q, scales), "w")
+    if q.shape[1] != k:
+        raise ValueError("q must be [n][k]")
+    _lib.ensure_init(x.device.index or 0)
+    _lib.check(_lib.load().zwg_linear_q8_add(_dev_ptr(x, torch.float32, "x"), m, k, q.data_ptr(), sp, q.shape[0],
+                                             _dev_ptr(out, torch.float32, "out"), _stream_of(x)))
+    return out
+
+
+def linear_q8_silu_mul(x, gate, up, out=None):
+    """silu(x . Wg^T) * (x . Wu^T) in one launch (src/llm.zig:206-208, src/ops.zig:435-440);
+    gate and up are (q, scales) pairs of the same shape."""
+    torch = _torch()
+    m, k = x.shape
+    gq, gs = _q8_pair(gate, "gate")
+    uq, us = _q8_pair(up, "up")
+    if gq.shape != uq.shape or gq.shape[1] != k:
+        raise ValueError("gate and up must both be [n][k]")
+    n = gq.shape[0]
+    out = torch.empty(m, n, dtype=torch.float32, device=x.device) if out is None else out
+    _lib.ensure_init(x.device.index or 0)
+    _lib.check(_lib.load().zwg_linear_q8_silu_mul(_dev_ptr(x, torch.float32, "x"), m, k, gq.data_ptr(), gs,
+                                                  uq.data_ptr(), us, n, _dev_ptr(out, torch.float32, "out"),
+                                                  _stream_of(x)))
+    return out
+
+
+def embed_q8(tokens, q, scales, out=None):
+    """Q8.row (src/gemm.zig:256-263) of each token id (CUDA int32): out [m][k] f32."""
+    torch = _torch()
+    if tokens.dtype != torch.int32 or not tokens.is_cuda or not tokens.is_contiguous():
+        raise ValueError("tokens must be a contiguous CUDA int32 tensor")
+    q, sp = _q8_pair((q, scales), "embd")
+    m = tokens.numel()
+    out = torch.empty(m, q.shape[1], dtype=torch.float32, device=tokens.device) if out is None else out
+    _lib.ensure_init(tokens.device.index or 0)
+    _lib.check(_lib.load().zwg_embed_q8(tokens.data_ptr(), m, q.data_ptr(), sp, q.shape[0], q.shape[1],
+                                        _dev_ptr(out, torch.float32, "out"), _stream_of(tokens)))
+    return out
+
+
+def llm_greedy(logits, recent=None, n_recent: int = 0, window: int = 64, penalty: float = 1.1, out=None):
+    """Model.penalize then Model.argmax (src/llm.zig:268-273, 313-321) for each row of
+    logits [m][n_vocab] (penalized in place). recent: CUDA int32 [m][>= n_recent], the tokens
+    generated so far; out: a CUDA int32 [m] tensor or a column view such as recent[:, i]."""
+    torch = _torch()
+    m, n_vocab = logits.shape
+    if not logits.is_contiguous():
+        raise ValueError("logits must be contiguous")
+    if out is None:
+        out = torch.empty(m, dtype=torch.int32, device=logits.device)
+    if out.dtype != torch.int32 or out.numel() != m:
+        raise ValueError("out must hold m int32 values")
+    rp, rs = None, 0
+    if recent is not None and n_recent:
+        if recent.dtype != torch.int32 or recent.stride(-1) != 1:
+            raise ValueError("recent must be int32 with unit stride along the tokens")
+        rp, rs = recent.data_ptr(), recent.stride(0) if recent.dim() > 1 else 0
+    _lib.ensure_init(logits.device.index or 0)
+    _lib.check(_lib.load().zwg_llm_greedy(logits.data_ptr(), m, n_vocab, rp, rs, n_recent, window, float(penalty),
+                                          out.data_ptr(), out.stride(0) if out.dim() else 1, _stream_of(logits)))
+    return out
+
+
+class LlmWeightsQ8:
+    """A Qwen2 model's weights on the device (llm.Model / llm.Layer, src/llm.zig:15-60) and
+    the zwg_llm_weights struct that points at them. `layers` is a list of dicts with keys
+    attn_norm, wq, bq, wk, bk, wv, bv, wo, ffn_norm, w_gate, w_up, w_down; Q8 matrices are
+    (q int8 [n][k], scales f32 [n][k/32]) pairs, the rest f32 vectors (biases may be None).
+    Arrays may be numpy or torch; they are copied to `device` once."""
+
+    Q8_KEYS = ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")
+    VEC_KEYS = ("attn_norm", "bq", "bk", "bv", "ffn_norm")
+
+    def __init__(self, layers, embd, output, output_norm, eps: float, device: int = 0):
+        torch = _torch()
+        dev = torch.device("cuda", device)
+
+        def t(a, dtype):
+            if a is None:
+                return None
+            if not isinstance(a, torch.Tensor):
+                a = torch.from_numpy(np.ascontiguousarray(a))
+            return a.to(device=dev, dtype=dtype).contiguous()
+
+        def q8(pair):
+            return t(pair[0], torch.int8), t(pair[1], torch.float32)
+
+        self.layers = []
+        for L in layers:
+            d = {k: q8(L[k]) for k in self.Q8_KEYS}
+            d.update({k: t(L.get(k), torch.float32) for k in self.VEC_KEYS})
+            self.layers.append(d)
+        self.embd = q8(embd)
+        self.output = self.embd if output is None else q8(output)
+        self.output_norm = t(output_norm, torch.float32)
+        self.eps = float(eps)
+        self.n_vocab, self.n_embd = self.embd[0].shape
+        self.n_ff = self.layers[0]["w_gate"][0].shape[0]
+        self._c = None
+
+    @staticmethod
+    def _mat(pair):
+        return _lib.Q8MatC(pair[0].data_ptr(), pair[1].data_ptr())
+
+    def layer_c(self, i: int) -> _lib.LlmLayerWeightsC:
+        L = self.layers[i]
+        p = lambda a: a.data_ptr() if a is not None else None  # noqa: E731
+        return _lib.LlmLayerWeightsC(p(L["attn_norm"]), self._mat(L["wq"]), self._mat(L["wk"]), self._mat(L["wv"]),
+                                     self._mat(L["wo"]), p(L["bq"]), p(L["bk"]), p(L["bv"]), p(L["ffn_norm"]),
+                                     self._mat(L["w_gate"]), self._mat(L["w_up"]), self._mat(L["w_down"]))
+
+    def c_struct(self) -> _lib.LlmWeightsC:
+        if self._c is None:
+            arr = (_lib.LlmLayerWeightsC * len(self.layers))(*[self.layer_c(i) for i in range(len(self.layers))])
+            self._arr = arr  # keeps the host array alive as long as the struct
+            self._c = _lib.LlmWeightsC(self.n_vocab, self.n_embd, self.n_ff, self.eps, self._mat(self.embd),
+                                       self._mat(self.output), self.output_norm.data_ptr(),
+                                       ctypes.cast(arr, ctypes.POINTER(_lib.LlmLayerWeightsC)))
+        return self._c
