@@ -9,10 +9,10 @@
 //   f32, bit-identical to the reference. A token outside the vocabulary writes a zero row
 //   and sets the device error word.
 // greedy_kernel: Model.penalize then Model.argmax (src/llm.zig:313-321, 268-273), one CTA
-//   per sequence: the repeat penalty applied in order by one thread over the last `window`
-//   generated tokens (repeats are penalized again, as in the reference), then the first
-//   index of the largest logit (NaN never wins; a NaN in column 0 makes the answer 0, as
-//   the reference's strict comparison does).
+//   per sequence: the repeat penalty over the last `window` generated tokens (repeats are
+//   penalized again, as in the reference), then the first index of the largest logit (NaN
+//   never wins; a NaN in column 0 makes the answer 0, as the reference's strict comparison
+//   does).
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -84,29 +84,61 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
     }
 }
 
+// One CTA per row. The penalty: thread i takes window entry i; the first occurrence of a
+// token applies the penalty as many times as the token occurs in the window, in order, so
+// the result equals the reference's loop over the window. The argmax: 8 independent 16-byte
+// loads per thread per round, then a block reduction keeping the largest value and, among
+// equal values, the smallest index.
 __global__ void __launch_bounds__(1024) greedy_kernel(float* logits, int n_vocab, const int32_t* recent,
                                                       size_t recent_stride, int n_recent, int window, float penalty,
                                                       int32_t* out, size_t out_stride, int* err) {
     chain_release();
     const int z = chain_wait();
     float* row = logits + (size_t)blockIdx.x * n_vocab + z;
-    if (threadIdx.x == 0 && penalty > 1.0f && n_recent > 0) {
+    if (penalty > 1.0f && n_recent > 0) {
         const int32_t* rc = recent + blockIdx.x * recent_stride + z;
         const int from = n_recent > window ? n_recent - window : 0;
-        for (int i = from; i < n_recent; i++) {
-            const int t = __ldcg(rc + i);
+        const int w = n_recent - from;
+        for (int i = threadIdx.x; i < w; i += blockDim.x) {
+            const int t = __ldcg(rc + from + i);
             if (t < 0 || t >= n_vocab) {
                 set_error(err, kErrBounds);
                 continue;
             }
-            const float v = __ldcg(row + t);
-            __stcg(row + t, v > 0.f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty));
+            bool first = true;
+            for (int j = 0; j < i && first; j++) first = __ldcg(rc + from + j) != t;
+            if (!first) continue;
+            int count = 1;
+            for (int j = i + 1; j < w; j++) count += __ldcg(rc + from + j) == t;
+            float v = __ldcg(row + t);
+            for (int c = 0; c < count; c++) v = v > 0.f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty);
+            __stcg(row + t, v);
         }
+        __syncthreads();
     }
-    __syncthreads();
     float bv = -INFINITY;
     int bi = INT_MAX;
-    for (int j = threadIdx.x; j < n_vocab; j += blockDim.x) better(bv, bi, __ldcg(row + j), j);
+    constexpr int B = 8;
+    const bool vec = (n_vocab % 4) == 0 && (((uintptr_t)row) & 15) == 0;
+    const int n4 = vec ? n_vocab / 4 : 0;
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    for (int base = threadIdx.x; base < n4; base += B * blockDim.x) {
+        float4 v[B];
+#pragma unroll
+        for (int u = 0; u < B; u++) {
+            const int j = base + u * blockDim.x;
+            v[u] = j < n4 ? __ldcg(row4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        }
+#pragma unroll
+        for (int u = 0; u < B; u++) {
+            const int j = 4 * (base + u * blockDim.x);
+            better(bv, bi, v[u].x, j);
+            better(bv, bi, v[u].y, j + 1);
+            better(bv, bi, v[u].z, j + 2);
+            better(bv, bi, v[u].w, j + 3);
+        }
+    }
+    for (int j = 4 * n4 + threadIdx.x; j < n_vocab; j += blockDim.x) better(bv, bi, __ldcg(row + j), j);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
