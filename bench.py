@@ -328,16 +328,23 @@ def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
         def step(kts=kts, vs=vs, q=q, o=o, sh=sh, ws=ws, bs=bs, B=B):
             for layer in range(len(kts)):
                 ops.attention_dev(q, kts[layer], vs[layer], sh, o, n_batch=B, batch_strides=bs, workspace=ws)
-        t = time_graph(step, steps, warmup) / steps
-        achieved = layers * byts / t / 1e9
-        traffic = profiled_traffic("decode_tma_qwen15_b16.txt", B) if d == 128 else None
-        res.append({"workload": f"{cfg} decode attention, {B} sequences x {layers} layers, n_kv={n_kv} "
-                                f"(mean of the decode), K^T cache n_ctx={n_ctx}",
-                    "metric": "qwen_decode_attention_tok_per_s", "value": B / t, "unit": "tok/s",
-                    "ms_per_step": t * 1e3,
-                    "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                                 "frac": achieved / hbm_peak, "traffic": traffic,
-                                 "bytes_per_launch": byts}})
+        # math "f32": the SIMT split-K kernel (the reference's arithmetic); "tf32": the
+        # tcgen05 kernel (tf32 operands, f32 accumulation; parity within max-abs 2e-3)
+        for math, kernel in (("f32", "decode_tma_kernel"), ("tf32", "decode_tc_kernel")):
+            ops.set_math(math)
+            try:
+                t = time_graph(step, steps, warmup) / steps
+            finally:
+                ops.set_math("f32")
+            achieved = layers * byts / t / 1e9
+            traffic = profiled_traffic("decode_tma_qwen15_b16.txt", B) if (d == 128 and math == "f32") else None
+            res.append({"workload": f"{cfg} decode attention, {B} sequences x {layers} layers, n_kv={n_kv} "
+                                    f"(mean of the decode), K^T cache n_ctx={n_ctx}, math {math} ({kernel})",
+                        "metric": "qwen_decode_attention_tok_per_s", "value": B / t, "unit": "tok/s",
+                        "ms_per_step": t * 1e3, "math": math,
+                        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                                     "frac": achieved / hbm_peak, "traffic": traffic,
+                                     "bytes_per_launch": byts}})
         del kts, vs
     torch.cuda.empty_cache()
     return res
@@ -511,16 +518,25 @@ def secondary_step(dev, hbm_peak, steps=10, warmup=3):
     n_ctx, n_kv = 2560, 2256
     wbytes = (c["n_layer"] * (2 * 1536 * 1536 + 2 * 256 * 1536 + 3 * c["n_ff"] * 1536) + c["n_vocab"] * 1536) * 1.125
     res = []
+    from zwhisper_b200 import ops
     for B in (1, 64):
         st, step = qwen15_step_fn(W, B, n_ctx, n_kv - 1, dev)
-        t = time_graph(step, steps, warmup) / steps
         kv = B * c["n_layer"] * n_kv * c["n_head_kv"] * c["d"] * 2 * 4
         byts = wbytes + kv
-        res.append({"workload": f"Qwen2.5-1.5B greedy decode step on the device, {B} sequence(s) x 28 layers + logits "
-                                f"(vocab 151936) + penalized argmax, Q8 weights, n_kv={n_kv}",
-                    "metric": "qwen_decode_step_tok_per_s", "value": B / t, "unit": "tok/s", "ms_per_step": t * 1e3,
-                    "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                                 "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
+        # math "tf32" changes only the attention (the tcgen05 decode kernel)
+        for math in ("f32", "tf32"):
+            ops.set_math(math)
+            try:
+                t = time_graph(step, steps, warmup) / steps
+            finally:
+                ops.set_math("f32")
+            res.append({"workload": f"Qwen2.5-1.5B greedy decode step on the device, {B} sequence(s) x 28 layers + "
+                                    f"logits (vocab 151936) + penalized argmax, Q8 weights, n_kv={n_kv}, "
+                                    f"attention math {math}",
+                        "metric": "qwen_decode_step_tok_per_s", "value": B / t, "unit": "tok/s",
+                        "ms_per_step": t * 1e3, "math": math,
+                        "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                                     "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
         st.close()
         torch.cuda.empty_cache()
     del W
@@ -653,6 +669,7 @@ def run_kernel_case(args):
     on 16 small.en windows (one layer, 184 MB of inputs and output, above L2); `decode_qwen`
     = the split-K decode kernel on 16 Qwen2.5-1.5B sequences (n_kv 2256, K^T cache 2560);
     `decode_qwen05` = the same on 16 Qwen2.5-0.5B sequences (d 64, n_kv 2128);
+    `decode_qwen_b1` = the same on one Qwen2.5-1.5B sequence (the reference's own batch);
     `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention;
     `prefill_qwen` = the tf32 prefill kernel on the last 208-query chunk of a 2000-token
     prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2);
@@ -675,9 +692,10 @@ def run_kernel_case(args):
         def fn():
             ops.enc_attn_bf16(q, k, v, N_HEAD, out)
         work = f"{FLOP_PER_WINDOW_LAYER * B / 1e9:.1f} GFLOP per launch"
-    elif args.kernel_case in ("decode_qwen", "decode_qwen05"):
-        B, H, Hkv, d, n_ctx, n_kv = (16, 12, 2, 128, 2560, 2256) if args.kernel_case == "decode_qwen" else \
-            (16, 14, 2, 64, 2560, 2128)
+    elif args.kernel_case in ("decode_qwen", "decode_qwen05", "decode_qwen_b1"):
+        B, H, Hkv, d, n_ctx, n_kv = {"decode_qwen": (16, 12, 2, 128, 2560, 2256),
+                                     "decode_qwen05": (16, 14, 2, 64, 2560, 2128),
+                                     "decode_qwen_b1": (1, 12, 2, 128, 2560, 2256)}[args.kernel_case]
         q = torch.randn(B, H * d, generator=g, device=dev)
         kt = torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev)
         v = torch.randn(B, n_ctx, Hkv * d, generator=g, device=dev)
@@ -758,7 +776,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_whisper", "prefill_qwen",
+    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_whisper", "prefill_qwen",
                                              "q8_logits", "step_qwen15", "pair_qwen15"], default=None)
     args = ap.parse_args()
     if args.kernel_case:

@@ -94,6 +94,9 @@ Plan plan_for(const zwg_attn_shape* sh, size_t n_batch, int sm_count) {
         zwg::decode_tma_plan(n_batch, sh->n_head_kv, sh->n_kv, sm_count, &grid, &p_max);
         const size_t rows = sh->n_q * (sh->n_head / sh->n_head_kv);
         pl.ws_bytes = zwg::decode_tma_workspace_bytes(n_batch, sh->n_head_kv, rows, sh->d, p_max);
+        // enough for the tensor-core decode too (tf32 math mode), whichever mode runs
+        if (sh->n_q == 1 && sh->kt_stride)
+            pl.ws_bytes = std::max(pl.ws_bytes, zwg::decode_tc_workspace_bytes(n_batch, sh->n_head_kv, rows, sh->d));
     }
     return pl;
 }
@@ -121,8 +124,12 @@ int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q
         p.n_splits = pl.n_splits; p.chunk = pl.chunk;
         if (b) { p.q_bs = b->q_batch_stride; p.k_bs = b->k_batch_stride; p.v_bs = b->v_batch_stride; p.out_bs = b->out_batch_stride; }
         if (p.k_bs % 4 || p.v_bs % 4 || p.q_bs % 4) return fail("decode kernel needs batch strides that are multiples of 4");
-        if (!zwg::decode_tma_supported(p)) return fail("decode shape not supported by the TMA decode kernel");
-        rc = zwg::decode_tma_launch(p, nb, c->sm_count, c->err, st);
+        if ((c->math & ZWG_MATH_TF32) && zwg::decode_tc_supported(p, nb)) {
+            rc = zwg::decode_tc_launch(p, nb, c->sm_count, c->err, st);
+        } else {
+            if (!zwg::decode_tma_supported(p)) return fail("decode shape not supported by the TMA decode kernel");
+            rc = zwg::decode_tma_launch(p, nb, c->sm_count, c->err, st);
+        }
     } else {
         zwg::FlashParams p{};
         p.q = q; p.k = k; p.v = v; p.out = out;

@@ -590,8 +590,12 @@ bool decode_tma_supported(const DecodeParams& p) {
 
 // The schedule: one CTA per SM (fewer when there are fewer tiles). With at least as many
 // segments as CTAs each CTA takes whole segments; with at least twice as many SMs as
-// segments every segment is cut into floor(SMs / segments) pieces (at most one per tile),
-// one per CTA; otherwise equal ranges over all tiles. p_max bounds the pieces of a segment.
+// segments every segment is cut into min(SMs / segments, kMaxPieces) pieces (at most one
+// per tile), one per CTA; otherwise equal ranges over all tiles. p_max bounds the pieces of
+// a segment. The cap keeps the last CTA's merge short: it folds the pieces 8 at a time, one
+// dependent round of L2 loads per 8, so at one sequence (2 segments of 71 tiles at
+// Qwen2.5-1.5B) 16 pieces of ~4 tiles beat 71 pieces of one tile.
+constexpr long long kMaxPieces = 16;
 static void decode_tma_schedule(size_t n_batch, size_t n_head_kv, size_t n_kv, int sm_count, int* grid, int* p_max,
                                 int* mode, int* pieces) {
     const long long n_t = std::max<long long>(1, (long long)((n_kv + dec_tma::TK - 1) / dec_tma::TK));
@@ -604,7 +608,7 @@ static void decode_tma_schedule(size_t n_batch, size_t n_head_kv, size_t n_kv, i
         *mode = 1;
         *p_max = 1;
     } else if (2 * segs <= sms && n_t >= 2) {
-        const long long pc = std::min<long long>(sms / segs, n_t);
+        const long long pc = std::min<long long>(std::min<long long>(sms / segs, n_t), kMaxPieces);
         *grid = (int)(segs * pc);
         *mode = 2;
         *pieces = (int)pc;

@@ -54,6 +54,12 @@ void decode_tma_plan(size_t n_batch, size_t n_head_kv, size_t n_kv, int sm_count
 size_t decode_tma_workspace_bytes(size_t n_batch, size_t n_head_kv, size_t rows, size_t d, int p_max);
 int decode_tma_launch(const DecodeParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st);
 
+// Qwen2 decode on tcgen05 tensor cores, kind::tf32 over the transposed f32 key cache, split
+// over the keys (attn_decode_tc.cu): one query token, d 64 or 128, group <= 32.
+bool decode_tc_supported(const DecodeParams& p, size_t n_batch);
+size_t decode_tc_workspace_bytes(size_t n_batch, size_t n_head_kv, size_t group, size_t d);
+int decode_tc_launch(const DecodeParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st);
+
 // Encoder tensor-core attention (attn_tc.cu).
 struct EncTcParams {
     const uint16_t* q;

@@ -96,20 +96,30 @@ __global__ void __launch_bounds__(1024) greedy_kernel(float* logits, int n_vocab
     const int z = chain_wait();
     float* row = logits + (size_t)blockIdx.x * n_vocab + z;
     if (penalty > 1.0f && n_recent > 0) {
+        // the window in shared memory (windows longer than kWin are read from global memory)
+        constexpr int kWin = 2048;
+        __shared__ int win[kWin];
         const int32_t* rc = recent + blockIdx.x * recent_stride + z;
         const int from = n_recent > window ? n_recent - window : 0;
         const int w = n_recent - from;
+        const bool in_smem = w <= kWin;
+        if (in_smem)
+            for (int i = threadIdx.x; i < w; i += blockDim.x) win[i] = __ldcg(rc + from + i);
+        __syncthreads();
         for (int i = threadIdx.x; i < w; i += blockDim.x) {
-            const int t = __ldcg(rc + from + i);
+            const int t = in_smem ? win[i] : __ldcg(rc + from + i);
             if (t < 0 || t >= n_vocab) {
                 set_error(err, kErrBounds);
                 continue;
             }
             bool first = true;
-            for (int j = 0; j < i && first; j++) first = __ldcg(rc + from + j) != t;
-            if (!first) continue;
             int count = 1;
-            for (int j = i + 1; j < w; j++) count += __ldcg(rc + from + j) == t;
+            for (int j = 0; j < w; j++) {
+                const int u = in_smem ? win[j] : __ldcg(rc + from + j);
+                first = first && !(j < i && u == t);
+                count += j > i && u == t;
+            }
+            if (!first) continue;
             float v = __ldcg(row + t);
             for (int c = 0; c < count; c++) v = v > 0.f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty);
             __stcg(row + t, v);
