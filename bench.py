@@ -670,6 +670,8 @@ def run_kernel_case(args):
     = the split-K decode kernel on 16 Qwen2.5-1.5B sequences (n_kv 2256, K^T cache 2560);
     `decode_qwen05` = the same on 16 Qwen2.5-0.5B sequences (d 64, n_kv 2128);
     `decode_qwen_b1` = the same on one Qwen2.5-1.5B sequence (the reference's own batch);
+    `decode_tc_qwen64` / `decode_tc_qwen_b1` = the tf32 tcgen05 decode kernel on 64 / one
+    Qwen2.5-1.5B sequences (296 MB / 4.6 MB of K/V per launch);
     `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention;
     `prefill_qwen` = the tf32 prefill kernel on the last 208-query chunk of a 2000-token
     prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2);
@@ -692,10 +694,14 @@ def run_kernel_case(args):
         def fn():
             ops.enc_attn_bf16(q, k, v, N_HEAD, out)
         work = f"{FLOP_PER_WINDOW_LAYER * B / 1e9:.1f} GFLOP per launch"
-    elif args.kernel_case in ("decode_qwen", "decode_qwen05", "decode_qwen_b1"):
+    elif args.kernel_case in ("decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64", "decode_tc_qwen_b1"):
         B, H, Hkv, d, n_ctx, n_kv = {"decode_qwen": (16, 12, 2, 128, 2560, 2256),
                                      "decode_qwen05": (16, 14, 2, 64, 2560, 2128),
-                                     "decode_qwen_b1": (1, 12, 2, 128, 2560, 2256)}[args.kernel_case]
+                                     "decode_qwen_b1": (1, 12, 2, 128, 2560, 2256),
+                                     "decode_tc_qwen64": (64, 12, 2, 128, 2560, 2256),
+                                     "decode_tc_qwen_b1": (1, 12, 2, 128, 2560, 2256)}[args.kernel_case]
+        if args.kernel_case.startswith("decode_tc"):
+            ops.set_math("tf32")
         q = torch.randn(B, H * d, generator=g, device=dev)
         kt = torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev)
         v = torch.randn(B, n_ctx, Hkv * d, generator=g, device=dev)
@@ -776,7 +782,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_whisper", "prefill_qwen",
+    ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64",
+                                             "decode_tc_qwen_b1", "decode_whisper", "prefill_qwen",
                                              "q8_logits", "step_qwen15", "pair_qwen15"], default=None)
     args = ap.parse_args()
     if args.kernel_case:

@@ -18,17 +18,23 @@
 //     ranges of 64-key tiles, one per CTA. A CTA with the whole segment writes the output;
 //     otherwise it writes a partial (max, sum, unnormalised O) per row and the last CTA of
 //     the segment (atomic ticket, reset by that CTA) merges them with all its threads.
-//   - Q: one 4-d TMA box per 32-column chunk ([1][group][32 floats], 128-byte swizzle), the
-//     K-major A operand; K^T tiles: two [d][32 keys] boxes, the MN-major B operand of
-//     S = Q K^T; V tiles: [64 keys][32 columns] boxes, the MN-major B operand of O += P V
-//     (both in the 128-byte swizzle with 32-byte atoms, descriptor layout 1).
+//   - Q lives in TMEM, not shared memory: the softmax warp writes the group's rows (tf32,
+//     rows >= group zero) with tcgen05.st and S = Q K^T takes its A operand from TMEM, as
+//     O += P V does. The 64 KB a 128-row Q tile would take in shared memory go to the K/V
+//     rings instead: three stages each, so a CTA has three tiles of loads ahead of its
+//     MMAs (with two, every tile waited a whole load latency: ~1.3 us per tile).
+//   - K^T tiles: two [d][32 keys] boxes, the MN-major B operand of S = Q K^T; V tiles:
+//     [64 keys][32 columns] boxes, the MN-major B operand of O += P V (both in the 128-byte
+//     swizzle with 32-byte atoms, descriptor layout 1).
 //   - TMEM: two 64-column score buffers (P written back over S as tf32, the TMEM A operand
-//     of the PV MMA) and a d-column O accumulator: 256 columns.
-//   - Warp 0: TMA producers (lane 0: Q and K^T, lane 1: V, two stages each). Warp 1: TMEM
-//     allocation and the MMA thread (S0 S1 | PV0 S2 | PV1 S3 ...). Warp 4 (TMEM lanes
-//     0..31): the softmax of the group's rows, one thread per row, online max in base 2 kept
-//     stale unless it grows by more than 2^8, P rounded to tf32. Warps 2, 3 and 5 only join
-//     the merge.
+//     of the PV MMA), a d-column O accumulator and the d-column Q.
+//   - Warp 0: TMA producers (lane 0: K^T, lane 1: V). Warp 1: TMEM allocation and the MMA
+//     thread (S0 S1 | PV0 S2 | PV1 S3 ...). Warp 4 (TMEM lanes 0..31): Q into TMEM, then the
+//     softmax of the group's rows, one thread per row, online max in base 2 kept stale
+//     unless it grows by more than 2^8, P rounded to tf32. Warps 2, 3 and 5 only join the
+//     merge. (Spreading the softmax over four warps, one per lane quarter with a copy of Q
+//     each, measured slower: at batch the kernel is at the DRAM stream's pace after the
+//     first tile, and the extra combine only adds.)
 // Every wait is bounded; a wait that runs out records kErrTimeout, the CTA drains its own
 // copies and MMAs with bounded waits, frees TMEM and returns.
 #include <cuda.h>
@@ -49,30 +55,29 @@ using namespace sm100;
 constexpr int BM = 128;                // rows per tile = TMEM lanes
 constexpr int BN = 64;                 // keys per tile
 constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warp 4 softmax, all merge
-constexpr uint32_t TMEM_COLS = 256;    // S/P buffers 2 x 64 columns, O up to 128 columns
-constexpr uint32_t O_COL = 2 * BN;
+constexpr int NST = 3;                 // K and V ring stages
+constexpr uint32_t O_COL = 2 * BN;     // S/P buffers 2 x 64 columns, then O, then Q
 constexpr int MAX_PIECES = 16;         // pieces per segment the workspace holds
 constexpr int PM = 8;                  // pieces merged per batch of loads
 
 template <int D>
 struct Cfg {
-    static constexpr uint32_t Q_CHUNK = BM * 128;           // [128 rows][32 floats]
-    static constexpr uint32_t Q_BYTES = (D / 32) * Q_CHUNK;
     static constexpr uint32_t K_CHUNK = D * 128;            // [D rows][32 keys]
     static constexpr uint32_t K_BYTES = 2 * K_CHUNK;
     static constexpr uint32_t V_CHUNK = BN * 128;           // [64 keys][32 floats]
     static constexpr uint32_t V_BYTES = (D / 32) * V_CHUNK;
-    // d = 64: 96 KB of tiles, two CTAs per SM; d = 128: 192 KB, one
+    static constexpr uint32_t Q_COL = O_COL + D;
+    static constexpr uint32_t TMEM_COLS = D == 128 ? 512 : 256;  // a power of two >= 2 * 64 + 2 * D
+    // d = 64: 96 KB of rings, two CTAs per SM; d = 128: 192 KB, one
     static constexpr int CTAS_PER_SM = D == 64 ? 2 : 1;
 };
 
 template <int D>
 struct Smem {
-    alignas(1024) uint8_t q[Cfg<D>::Q_BYTES];
-    alignas(1024) uint8_t k[2][Cfg<D>::K_BYTES];
-    alignas(1024) uint8_t v[2][Cfg<D>::V_BYTES];
+    alignas(1024) uint8_t k[NST][Cfg<D>::K_BYTES];
+    alignas(1024) uint8_t v[NST][Cfg<D>::V_BYTES];
     uint64_t q_full;
-    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t k_full[NST], k_empty[NST], v_full[NST], v_empty[NST];
     uint64_t s_full[2], p_full[2], pv_done, drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -85,6 +90,8 @@ constexpr size_t smem_bytes() {
 }
 
 struct Args {
+    const float* q;  // [batch][1][n_head * D] at q_bs per item
+    size_t q_bs;
     float* out;
     size_t out_stride, out_bs;
     int n_kv, n_head_kv, group, n_t, pieces, n_items;
@@ -95,8 +102,8 @@ struct Args {
 
 template <int D>
 __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
-    decode_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, const Args a) {
+    decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                     const Args a) {
     using C = Cfg<D>;
     extern __shared__ uint8_t smem_raw[];
     Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -117,22 +124,15 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
     __syncthreads();
     if (sm.abort_flag || n_t <= 0) return;
 
-    // rows of the Q tile the loads never write (group..127) are zeroed, so their scores are 0
-    {
-        const int n16 = (BM - a.group) * 8;  // 16-byte words per chunk
-        for (int c = 0; c < D / 32; c++) {
-            uint4* p = reinterpret_cast<uint4*>(sm.q + c * C::Q_CHUNK + a.group * 128);
-            for (int i = threadIdx.x; i < n16; i += THREADS) p[i] = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-    }
     if (threadIdx.x == 0) {
-        mbar_init(&sm.q_full, 1);
-        for (int s = 0; s < 2; s++) {
+        mbar_init(&sm.q_full, 32);
+        for (int s = 0; s < NST; s++) {
             mbar_init(&sm.k_full[s], 1);
             mbar_init(&sm.k_empty[s], 1);
             mbar_init(&sm.v_full[s], 1);
             mbar_init(&sm.v_empty[s], 1);
+        }
+        for (int s = 0; s < 2; s++) {
             mbar_init(&sm.s_full[s], 1);
             mbar_init(&sm.p_full[s], 32);
         }
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(&sm.tmem_base, TMEM_COLS);
+        tmem_alloc(&sm.tmem_base, C::TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -156,40 +156,36 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
         // Each lane waits at exit for the last load it issued, so no copy is in flight when
         // the CTA releases its memory.
         if (lane == 0) {
-            prefetch_tmap(&tm_q);
             prefetch_tmap(&tm_k);
             uint32_t n_k_loads = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(&sm.q_full, (D / 32) * a.group * 128);
-            for (int c = 0; c < D / 32; c++)
-                tma_load_4d(&tm_q, &sm.q_full, sm.q + c * C::Q_CHUNK, c * 32, kh * a.group, 0, b);
             for (int j = 0; ok && j < n_t; j++) {
-                const uint32_t s = j & 1;
-                if (j >= 2 && !(ok = mbar_wait(&sm.k_empty[s], ((j >> 1) - 1) & 1, err))) break;
+                const uint32_t s = j % NST;
+                if (j >= NST && !(ok = mbar_wait(&sm.k_empty[s], ((j / NST) - 1) & 1, err))) break;
                 const int key0 = (t_first + j) * BN;
                 mbar_arrive_expect_tx(&sm.k_full[s], C::K_BYTES);
                 tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s], key0, kh * D, b);
                 tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s] + C::K_CHUNK, key0 + 32, kh * D, b);
                 n_k_loads++;
             }
-            mbar_wait_drain(&sm.q_full, 0);
-            if (n_k_loads > 0) mbar_wait_drain(&sm.k_full[0], (((n_k_loads + 1) >> 1) - 1) & 1);
-            if (n_k_loads > 1) mbar_wait_drain(&sm.k_full[1], ((n_k_loads >> 1) - 1) & 1);
+            // the last load of each stage: stage st took loads st, st + NST, ...
+            for (uint32_t st = 0; st < NST && st < n_k_loads; st++)
+                mbar_wait_drain(&sm.k_full[st], ((n_k_loads - 1 - st) / NST) & 1);
         } else if (lane == 1) {
             prefetch_tmap(&tm_v);
             uint32_t n_v_loads = 0;
             bool ok = true;
             for (int j = 0; ok && j < n_t; j++) {
-                const uint32_t s = j & 1;
-                if (j >= 2 && !(ok = mbar_wait(&sm.v_empty[s], ((j >> 1) - 1) & 1, err))) break;
+                const uint32_t s = j % NST;
+                if (j >= NST && !(ok = mbar_wait(&sm.v_empty[s], ((j / NST) - 1) & 1, err))) break;
                 const int key0 = (t_first + j) * BN;
                 mbar_arrive_expect_tx(&sm.v_full[s], C::V_BYTES);
                 for (int c = 0; c < D / 32; c++)
                     tma_load_3d(&tm_v, &sm.v_full[s], sm.v[s] + c * C::V_CHUNK, kh * D + c * 32, key0, b);
                 n_v_loads++;
             }
-            if (n_v_loads > 0) mbar_wait_drain(&sm.v_full[0], (((n_v_loads + 1) >> 1) - 1) & 1);
-            if (n_v_loads > 1) mbar_wait_drain(&sm.v_full[1], ((n_v_loads >> 1) - 1) & 1);
+            for (uint32_t st = 0; st < NST && st < n_v_loads; st++)
+                mbar_wait_drain(&sm.v_full[st], ((n_v_loads - 1 - st) / NST) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -197,38 +193,37 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
             constexpr uint32_t idesc_s = idesc_tf32(BM, BN, false, true);
             constexpr uint32_t idesc_o = idesc_tf32(BM, D, false, true);
             bool ok = mbar_wait(&sm.q_full, 0, err);
-            const uint32_t q_addr = smem_u32(sm.q);
-            // S(j) = Q K^T(j) into score buffer j % 2
+            tc_fence_after();
+            // S(j) = Q K^T(j) into score buffer j % 2, Q from TMEM
             auto issue_s = [&](int j) -> bool {
-                const uint32_t s = j & 1;
-                if (!mbar_wait(&sm.k_full[s], (j >> 1) & 1, err)) return false;
+                const uint32_t st = j % NST, s = j & 1;
+                if (!mbar_wait(&sm.k_full[st], (j / NST) & 1, err)) return false;
                 tc_fence_after();
-                const uint32_t k_addr = smem_u32(sm.k[s]);
+                const uint32_t k_addr = smem_u32(sm.k[st]);
 #pragma unroll
                 for (int kk = 0; kk < D / 8; kk++) {
-                    const uint64_t ad = smem_desc_sw128(q_addr + (kk >> 2) * C::Q_CHUNK + (kk & 3) * 32, 16, 1024);
                     const uint64_t bd = smem_desc_sw128_32b(k_addr + kk * 1024, C::K_CHUNK, 512);
-                    mma_tf32_ss(tmem + s * BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+                    mma_tf32_ts(tmem + s * BN, tmem + C::Q_COL + kk * 8, bd, idesc_s, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(&sm.k_empty[s]);
+                mma_commit(&sm.k_empty[st]);
                 mma_commit(&sm.s_full[s]);
                 return true;
             };
             if (ok) ok = issue_s(0);
             if (ok && n_t > 1) ok = issue_s(1);
             for (int j = 0; ok && j < n_t; j++) {
-                const uint32_t s = j & 1;
+                const uint32_t st = j % NST, s = j & 1;
                 if (!(ok = mbar_wait(&sm.p_full[s], (j >> 1) & 1, err))) break;
-                if (!(ok = mbar_wait(&sm.v_full[s], (j >> 1) & 1, err))) break;
+                if (!(ok = mbar_wait(&sm.v_full[st], (j / NST) & 1, err))) break;
                 tc_fence_after();
-                const uint32_t v_addr = smem_u32(sm.v[s]);
+                const uint32_t v_addr = smem_u32(sm.v[st]);
 #pragma unroll
                 for (int kk = 0; kk < BN / 8; kk++) {
                     const uint64_t bd = smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512);
                     mma_tf32_ts(tmem + O_COL, tmem + s * BN + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&sm.pv_done);
-                mma_commit(&sm.v_empty[s]);
+                mma_commit(&sm.v_empty[st]);
                 if (j + 2 < n_t && !(ok = issue_s(j + 2))) break;
             }
             // every MMA issued so far completes before TMEM is released
@@ -240,6 +235,27 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
         // (a warp reaches the TMEM lanes of its index mod 4: warp 4 has lanes 0..31)
         const int row = lane;
         const bool valid = row < a.group;
+        // Q rows of the group into TMEM lanes 0..31 as tf32 (rows >= group zero)
+        {
+            const float4* qrow = reinterpret_cast<const float4*>(
+                a.q + (size_t)b * a.q_bs + (size_t)(kh * a.group + (valid ? row : 0)) * D);
+#pragma unroll
+            for (int cc = 0; cc < D / 32; cc++) {
+                uint32_t r[32];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const float4 f = valid ? __ldg(qrow + cc * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    r[4 * e] = to_tf32(f.x);
+                    r[4 * e + 1] = to_tf32(f.y);
+                    r[4 * e + 2] = to_tf32(f.z);
+                    r[4 * e + 3] = to_tf32(f.w);
+                }
+                tmem_st32(tmem + C::Q_COL + cc * 32, r);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&sm.q_full);
+        }
         bool ok = true;
         for (int j = 0; j < n_t; j++) {
             const uint32_t s = j & 1;
@@ -290,13 +306,15 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
                 sr[e] = p;
             }
             l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
-            // the previous PV must be done before O is rescaled
-            if (j > 0) {
+            // PV(j - 1) must be done before O is rescaled; without a rescale P(j) is handed to
+            // the MMA thread first (its buffer's last reader, PV(j - 2), is already done) and
+            // the wait comes after, so PV(j) queues behind PV(j - 1) at once. Either way the
+            // warp waits for every PV once, in order, which keeps the parity waits exact.
+            // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows must.
+            const bool any_rescale = __any_sync(0xffffffffu, rescale);
+            if (j > 0 && any_rescale) {
                 if (!(ok = mbar_wait_warp(&sm.pv_done, (j - 1) & 1, err))) break;
                 tc_fence_after();
-            }
-            // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows must
-            if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
                 for (int cc = 0; cc < D / 32; cc++) {
                     uint32_t o[32];
@@ -320,6 +338,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&sm.p_full[s]);
+            if (j > 0 && !any_rescale) {
+                if (!(ok = mbar_wait_warp(&sm.pv_done, (j - 1) & 1, err))) break;
+                tc_fence_after();
+            }
         }
         if (ok) ok = mbar_wait_warp(&sm.pv_done, (n_t - 1) & 1, err);
         if (ok) {
@@ -415,7 +437,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
     }
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
@@ -449,6 +471,8 @@ template <int D>
 int launch_d(const DecodeParams& p, size_t n_batch, int sm_count, cudaStream_t st, int* err) {
     using namespace decode_tc;
     Args a{};
+    a.q = p.q;
+    a.q_bs = n_batch > 1 ? p.q_bs : 0;
     a.out = p.out;
     a.out_stride = p.out_stride;
     a.out_bs = p.out_bs;
@@ -468,16 +492,9 @@ int launch_d(const DecodeParams& p, size_t n_batch, int sm_count, cudaStream_t s
     if (a.pieces > 1 && cudaMemsetAsync(a.counters, 0, segs * sizeof(int), st) != cudaSuccess) return -1;
 
     // a single item: any valid batch stride
-    const size_t q_bs = n_batch > 1 ? p.q_bs : p.q_stride;
     const size_t k_bs = n_batch > 1 ? p.k_bs : p.n_head_kv * D * p.kt_stride;
     const size_t v_bs = n_batch > 1 ? p.v_bs : p.n_kv * p.kv_stride;
-    CUtensorMap mq, mk, mv;
-    {
-        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)p.n_head, 1, (cuuint64_t)n_batch};
-        cuuint64_t strides[3] = {(cuuint64_t)D * 4, (cuuint64_t)p.q_stride * 4, (cuuint64_t)q_bs * 4};
-        cuuint32_t box[4] = {32, (cuuint32_t)a.group, 1, 1};
-        if (!encode_map(&mq, 4, p.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
-    }
+    CUtensorMap mk, mv;
     {
         cuuint64_t dims[3] = {(cuuint64_t)p.n_kv, (cuuint64_t)(p.n_head_kv * D), (cuuint64_t)n_batch};
         cuuint64_t strides[2] = {(cuuint64_t)p.kt_stride * 4, (cuuint64_t)k_bs * 4};
@@ -504,7 +521,7 @@ int launch_d(const DecodeParams& p, size_t n_batch, int sm_count, cudaStream_t s
             attr_set[dev] = true;
         }
     }
-    decode_tc_kernel<D><<<a.n_items, THREADS, smem_bytes<D>(), st>>>(mq, mk, mv, a);
+    decode_tc_kernel<D><<<a.n_items, THREADS, smem_bytes<D>(), st>>>(mk, mv, a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -336,14 +336,18 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
                     sr[e] = p;
                 }
                 l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
-                // the previous PV must be done before O is rescaled
-                if (j > 0) {
+                // PV(j - 1) must be done before O is rescaled; without a rescale P(j) is handed
+                // to the MMA thread first (its buffer's last reader, PV(j - 2), is already done)
+                // and the wait comes after, so PV(j) queues behind PV(j - 1) at once. Either way
+                // the warp waits for every PV once, in order, which keeps the parity waits exact.
+                // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows must
+                // (corr is 1 in the others).
+                const bool any_rescale = __any_sync(0xffffffffu, rescale);
+                if (j > 0 && any_rescale) {
                     if (!(ok = mbar_wait_warp(&sm.pv_done, (gj - 1) & 1, err))) break;
                     tc_fence_after();
                 }
-                // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows
-                // must (corr is 1 in the others)
-                if (__any_sync(0xffffffffu, rescale)) {
+                if (any_rescale) {
 #pragma unroll
                     for (int cc = 0; cc < D / 32; cc++) {
                         uint32_t o[32];
@@ -367,6 +371,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&sm.p_full[s]);
+                if (j > 0 && !any_rescale) {
+                    if (!(ok = mbar_wait_warp(&sm.pv_done, (gj - 1) & 1, err))) break;
+                    tc_fence_after();
+                }
             }
             if (!ok) break;
             // ---- epilogue: O / l -> out[b][i][(kh * group + hg) * D ..]
