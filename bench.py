@@ -504,6 +504,37 @@ def qwen15_step_fn(W, B, n_ctx, n_past, dev, seed=6):
     return st, step
 
 
+def whisper_base_decoder(dev, seed=7):
+    """Random Whisper base.en decoder weights on the device (configs[1]: n_state 512, 8 heads,
+    6 layers, vocab 51864; N(0, 0.02^2) matrices quantized to Q8, LayerNorm gains 1)."""
+    import torch
+
+    from zwhisper_b200 import ops
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    ns, nv, nl, nctx = 512, 51864, 6, 448
+
+    def r(*shape):
+        return torch.randn(*shape, generator=g, device=dev) * 0.02
+
+    t = {"decoder.token_embedding.weight": r(nv, ns), "decoder.positional_embedding": r(nctx, ns),
+         "decoder.ln.weight": torch.ones(ns, device=dev), "decoder.ln.bias": torch.zeros(ns, device=dev)}
+    for i in range(nl):
+        p = f"decoder.blocks.{i}."
+        for ln in ("attn_ln", "cross_attn_ln", "mlp_ln"):
+            t[p + ln + ".weight"] = torch.ones(ns, device=dev)
+            t[p + ln + ".bias"] = torch.zeros(ns, device=dev)
+        for a in ("attn", "cross_attn"):
+            for m in ("query", "key", "value", "out"):
+                t[p + f"{a}.{m}.weight"] = r(ns, ns)
+                t[p + f"{a}.{m}.bias"] = r(ns)
+        t[p + "mlp.0.weight"], t[p + "mlp.0.bias"] = r(4 * ns, ns), r(4 * ns)
+        t[p + "mlp.2.weight"], t[p + "mlp.2.bias"] = r(ns, 4 * ns), r(ns)
+    W = ops.DecoderWeightsQ8(t, nl, device=dev.index or 0)
+    del t
+    return W
+
+
 def secondary_step(dev, hbm_peak, steps=10, warmup=3):
     """The whole Qwen2.5-1.5B greedy decode step on the device (the "next" rows around the
     attention, src/llm.zig:169-216, 313-321): embedding, 28 layers of RMSNorm, Q8 q/k/v with
@@ -540,6 +571,39 @@ def secondary_step(dev, hbm_peak, steps=10, warmup=3):
         st.close()
         torch.cuda.empty_cache()
     del W
+    torch.cuda.empty_cache()
+    # the Whisper base.en decoder step: 32 windows, 6 layers, 224 of 448 cache
+    # positions filled, cross-attention over 1500 frames, Q8 weights, logits and argmax
+    B, n_past, na, ns = 32, 224, 1500, 512
+    Wd = whisper_base_decoder(dev)
+    from zwhisper_b200 import ops
+    st = ops.DecoderState(6, B, ns, 8, 448, na, device=dev.index or 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(8)
+    for w in range(B):
+        st.set_audio_q8(Wd, w, torch.randn(na, ns, generator=g, device=dev))
+    tok = torch.randint(0, 51864, (B, 1), generator=g, device=dev, dtype=torch.int32)
+    x = torch.empty(B, 1, ns, device=dev)
+    logits = torch.empty(B, 51864, device=dev)
+    scratch = st.scratch(1)
+
+    def wstep():
+        st.forward_q8(Wd, tok, n_past, x=x, logits=logits, scratch=scratch)
+        ops.llm_greedy(logits, penalty=1.0, out=tok.view(-1))
+    t = time_graph(wstep, steps, warmup) / steps
+    # per layer q, k, v, o, cq, co (n_state^2 each) and the two mlp matrices (4 n_state^2
+    # each); ck and cv are read only by set_audio
+    wbytes = (6 * (6 * ns * ns + 8 * ns * ns) + 51864 * ns) * 1.125
+    kv = B * 6 * (n_past + 1 + na) * ns * 4 * 2
+    byts = wbytes + kv
+    res.append({"workload": f"Whisper base.en decoder step on the device (configs[1]): {B} windows x 6 layers "
+                            f"(self over {n_past + 1} of 448, cross over {na}) + logits (vocab 51864) + argmax, "
+                            f"Q8 weights",
+                "metric": "whisper_decoder_step_tok_per_s", "value": B / t, "unit": "tok/s", "ms_per_step": t * 1e3,
+                "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
+    st.close()
+    del Wd
     torch.cuda.empty_cache()
     return res
 

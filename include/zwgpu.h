@@ -90,11 +90,12 @@ ZWG_API int zwg_device_count(void);
  *   n_q == n_kv, d == 64, MHA, rows of exactly n_head*64, keys as rows, not causal)
  *   convert Q/K/V to bf16 on the device and run the tcgen05 kernel with f32 softmax and
  *   accumulation.
- * ZWG_MATH_TF32 (host- and device-pointer entry points): prefill-shaped calls over a
- *   transposed key cache (kt_stride > 0, more than 8 query rows per kv head, d 64 or 128,
- *   16-byte aligned buffers and strides that are multiples of 4) run the tcgen05 kernel
- *   with kind::tf32 operands read straight from the f32 caches (10-bit mantissa) and f32
- *   softmax and accumulation. Other shapes stay f32. */
+ * ZWG_MATH_TF32 (host- and device-pointer entry points): calls over a transposed key cache
+ *   (kt_stride > 0, d 64 or 128, 16-byte aligned buffers and strides that are multiples of
+ *   4) run tcgen05 kernels with kind::tf32 operands read straight from the f32 caches
+ *   (10-bit mantissa) and f32 softmax and accumulation: prefill-shaped calls (more than 8
+ *   query rows per kv head) the prefill kernel, one-token calls with a GQA group of at most
+ *   32 heads the split-K decode kernel. Other shapes stay f32. */
 #define ZWG_MATH_F32 0
 #define ZWG_MATH_BF16 1
 #define ZWG_MATH_TF32 2
@@ -323,6 +324,76 @@ ZWG_API int zwg_llm_layer_q8(zwg_llm_state* st, size_t layer, const zwg_llm_weig
 ZWG_API int zwg_llm_forward_q8(zwg_llm_state* st, const zwg_llm_weights* w, const int32_t* tokens, size_t n_past,
                                size_t n, float* x, float* logits, void* scratch, size_t scratch_bytes,
                                void* stream);
+
+/* ---- the Whisper decoder step on the device (src/decoder.zig:150-206) -----------------
+ * Decoder.forward and setAudio around the state's attention calls, for n_batch windows:
+ * LayerNorm, Q8 projections with their biases, GELU, the residual adds, the token and
+ * position embeddings and the tied logits. Q8 matrices as zwg_q8_mat; vectors f32 [n_state]
+ * (mlp0_b [4 n_state]); all device pointers. */
+typedef struct zwg_dec_layer_weights {
+    const float* attn_ln_w;
+    const float* attn_ln_b;
+    zwg_q8_mat q;               /* [n_state][n_state] */
+    const float* q_b;
+    zwg_q8_mat k;               /* no bias, as the model */
+    zwg_q8_mat v;
+    const float* v_b;
+    zwg_q8_mat o;
+    const float* o_b;
+    const float* cross_ln_w;
+    const float* cross_ln_b;
+    zwg_q8_mat cq;
+    const float* cq_b;
+    zwg_q8_mat ck;              /* no bias */
+    zwg_q8_mat cv;
+    const float* cv_b;
+    zwg_q8_mat co;
+    const float* co_b;
+    const float* mlp_ln_w;
+    const float* mlp_ln_b;
+    zwg_q8_mat mlp0;            /* [4 n_state][n_state] */
+    const float* mlp0_b;
+    zwg_q8_mat mlp1;            /* [n_state][4 n_state] */
+    const float* mlp1_b;
+} zwg_dec_layer_weights;
+
+/* The decoder's weights (decoder.Decoder, src/decoder.zig:45-60): te [n_vocab][n_state] (the
+ * token embedding and the tied logits matrix), pe [n_text_ctx][n_state], the final LayerNorm,
+ * `layers` a HOST array of the state's n_layer entries. n_state a multiple of 32. */
+typedef struct zwg_dec_weights {
+    size_t n_vocab;
+    zwg_q8_mat te;
+    const float* pe;
+    const float* ln_w;
+    const float* ln_b;
+    const zwg_dec_layer_weights* layers;
+} zwg_dec_weights;
+
+/* ops.layerNorm (src/ops.zig:355-398): out[i] = (x[i] - mean) / sqrt(var + eps) * w + b for m
+ * rows of n (population variance; n a multiple of 4, 16-byte aligned buffers). */
+ZWG_API int zwg_layer_norm(const float* x, size_t m, size_t n, const float* w, const float* b, float eps, float* out,
+                           void* stream);
+
+/* ops.linear then ops.gelu (src/decoder.zig:197-198): out[m][n] = gelu(x . W^T + bias), ggml's
+ * tanh GELU (src/ops.zig:312-327). */
+ZWG_API int zwg_linear_q8_gelu(const float* x, size_t m, size_t k, const int8_t* q, const float* scales,
+                               const float* bias, size_t n, float* out, void* stream);
+
+/* setAudio (src/decoder.zig:151-159) for one window: enc [n_audio_ctx][n_state] (device) ->
+ * every layer's cross K = enc . ck^T and cross V = enc . cv^T + cv_b in the state. */
+ZWG_API int zwg_dec_set_audio_q8(zwg_dec_state* st, const zwg_dec_weights* w, size_t window, const float* enc,
+                                 void* stream);
+
+/* Scratch bytes zwg_dec_forward_q8 needs for chunks of n tokens. */
+ZWG_API size_t zwg_dec_scratch_bytes(const zwg_dec_state* st, size_t n);
+
+/* Decoder.forward (src/decoder.zig:166-206) for every window: tokens [n_batch][n] (device
+ * int32) at positions n_past..; hidden states left in x [n_batch][n][n_state]; the logits of
+ * each window's last token in logits [n_batch][n_vocab]. The self K/V rows are appended to
+ * the state's cache; cross-attention reads the state's cross K/V (zwg_cross_kv_set or
+ * zwg_dec_set_audio_q8). */
+ZWG_API int zwg_dec_forward_q8(zwg_dec_state* st, const zwg_dec_weights* w, const int32_t* tokens, size_t n_past,
+                               size_t n, float* x, float* logits, void* scratch, size_t scratch_bytes, void* stream);
 
 /* Self-test of the timeout path every kernel relies on: launches one bounded device-side
  * wait on a barrier nothing ever completes (a few seconds), then synchronizes. Returns

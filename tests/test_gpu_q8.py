@@ -53,11 +53,18 @@ def check_linear(torch, ops, m, n, k, bias, seed):
     assert (err <= 2e-6 * mag + 1e-30).all(), float((err / (mag + 1e-30)).max())
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 13])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 13, 37])
 @pytest.mark.parametrize("n,k", [(1, 32), (7, 64), (512, 512), (1536, 1536), (101, 8960)])
 def test_linear_matches_oracle(env, m, n, k):
+    """m >= 16 runs every full chunk of 8 x rows in one launch (grid.y) and the rest in another."""
     torch, ops = env
     check_linear(torch, ops, m, n, k, bias=(m % 2 == 1), seed=m * 100 + n + k)
+
+
+def test_linear_set_audio_shape(env):
+    """1500 rows of x, the Whisper decoder's cross K/V projection (src/decoder.zig:154-155)."""
+    torch, ops = env
+    check_linear(torch, ops, 1500, 96, 128, bias=True, seed=5)
 
 
 def test_whisper_logits_matvec_shape(env):

@@ -68,6 +68,27 @@ class LlmWeightsC(ctypes.Structure):
     ]
 
 
+class DecLayerWeightsC(ctypes.Structure):
+    """zwg_dec_layer_weights (decoder.Layer, src/decoder.zig:13-43, without the state)."""
+
+    _fields_ = [
+        ("attn_ln_w", c_ptr), ("attn_ln_b", c_ptr), ("q", Q8MatC), ("q_b", c_ptr), ("k", Q8MatC), ("v", Q8MatC),
+        ("v_b", c_ptr), ("o", Q8MatC), ("o_b", c_ptr), ("cross_ln_w", c_ptr), ("cross_ln_b", c_ptr),
+        ("cq", Q8MatC), ("cq_b", c_ptr), ("ck", Q8MatC), ("cv", Q8MatC), ("cv_b", c_ptr), ("co", Q8MatC),
+        ("co_b", c_ptr), ("mlp_ln_w", c_ptr), ("mlp_ln_b", c_ptr), ("mlp0", Q8MatC), ("mlp0_b", c_ptr),
+        ("mlp1", Q8MatC), ("mlp1_b", c_ptr),
+    ]
+
+
+class DecWeightsC(ctypes.Structure):
+    """zwg_dec_weights (decoder.Decoder's weights, src/decoder.zig:45-60)."""
+
+    _fields_ = [
+        ("n_vocab", c_size), ("te", Q8MatC), ("pe", c_ptr), ("ln_w", c_ptr), ("ln_b", c_ptr),
+        ("layers", ctypes.POINTER(DecLayerWeightsC)),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/zwgpu.h declares
 SIGNATURES = {
     "zwg_version": (ctypes.c_int, []),
@@ -120,6 +141,12 @@ SIGNATURES = {
     "zwg_llm_layer_q8": (ctypes.c_int, [c_ptr, c_size, ctypes.POINTER(LlmWeightsC), c_ptr, c_size, c_size, c_ptr,
                                         c_size, c_ptr]),
     "zwg_llm_forward_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(LlmWeightsC), c_ptr, c_size, c_size, c_ptr, c_ptr,
+                                          c_ptr, c_size, c_ptr]),
+    "zwg_layer_norm": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, ctypes.c_float, c_ptr, c_ptr]),
+    "zwg_linear_q8_gelu": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr, c_size, c_ptr, c_ptr]),
+    "zwg_dec_set_audio_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(DecWeightsC), c_size, c_ptr, c_ptr]),
+    "zwg_dec_scratch_bytes": (c_size, [c_ptr, c_size]),
+    "zwg_dec_forward_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(DecWeightsC), c_ptr, c_size, c_size, c_ptr, c_ptr,
                                           c_ptr, c_size, c_ptr]),
 }
 

@@ -434,7 +434,7 @@ int zwg_linear_q8(const float* x, size_t m, size_t k, const int8_t* q, const flo
     if (((uintptr_t)x | (uintptr_t)q) & 15) return fail("linear_q8: x and q must be 16-byte aligned");
     if (((uintptr_t)scales | (uintptr_t)out | (uintptr_t)bias) & 3) return fail("linear_q8: f32 buffers must be 4-byte aligned");
     if (n >= (1u << 30) || k >= (1u << 30)) return fail("linear_q8: matrix too large");
-    if (zwg::q8_linear_launch(x, m, k, q, scales, bias, n, 0, out, (cudaStream_t)stream))
+    if (zwg::q8_linear_launch(x, m, k, q, scales, bias, n, zwg::LIN_STORE, out, (cudaStream_t)stream))
         return cuda_fail("linear_q8 launch", cudaGetLastError());
     return ZWG_OK;
 }

@@ -1,6 +1,6 @@
 // Internals of the C-ABI layer shared by its source files (api.cu: contexts and the
 // attention entry points; state.cu: the library-owned decoder and LLM states; llm_api.cu:
-// the Qwen2 decode step around the attention).
+// the Qwen2 decode step around the attention; dec_api.cu: the Whisper decoder step).
 #pragma once
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -63,6 +63,16 @@ Ctx* ctx_for(int device);
 
 }  // namespace capi
 }  // namespace zwg
+
+// Whisper decoder state (state.cu): per layer the self K/V cache and the cross K/V of
+// n_batch windows, on one device.
+struct zwg_dec_state {
+    int device = -1;
+    size_t n_layer = 0, n_batch = 0, n_state = 0, n_head = 0, n_text_ctx = 0, n_audio_ctx = 0;
+    // per layer: self K/V [n_batch][n_text_ctx][n_state], cross K/V [n_batch][n_audio_ctx][n_state]
+    std::vector<float*> self_k, self_v, cross_k, cross_v;
+    zwg::capi::DevBuf ws;
+};
 
 // Qwen2 LLM state (state.cu): the caches of every layer for n_batch sequences and the RoPE
 // tables, on one device.

@@ -78,9 +78,11 @@ int prefill_tc_launch(const FlashParams& p, size_t n_batch, int sm_count, int* e
 
 // Q8 weights (q8.cu): Q8.quantize and ops.linear over int8 blocks of 32.
 int q8_quantize_launch(const float* w, size_t n, size_t k, int8_t* q, float* scales, cudaStream_t st);
-// out = x . W^T (+ bias); accum != 0 adds the result into out instead (the residual).
+// out = x . W^T (+ bias), then by mode: LIN_STORE writes it, LIN_ADD adds it into out (the
+// residual), LIN_GELU writes gelu of it.
+enum { LIN_STORE = 0, LIN_ADD = 1, LIN_GELU = 2 };
 int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
-                     size_t n, int accum, float* out, cudaStream_t st);
+                     size_t n, int mode, float* out, cudaStream_t st);
 
 // Paired-row Q8 products with a fused epilogue (q8.cu): PAIR_ROPE = the q/k/v projections
 // with bias, RoPE and the K^T / V cache append; PAIR_SILU = silu(x . Wg^T) * (x . Wu^T).
@@ -109,8 +111,11 @@ int q8_pair_launch(const PairParams& p, int epi, cudaStream_t st);
 // Decode-step kernels around the projections (llm_step.cu), chained launches.
 int rms_norm_launch(const float* x, size_t x_stride, size_t m, size_t n, const float* w, float eps, float* out,
                     size_t out_stride, cudaStream_t st);
+int layer_norm_launch(const float* x, size_t x_stride, size_t m, size_t n, const float* w, const float* b, float eps,
+                      float* out, size_t out_stride, cudaStream_t st);
+// rows of the Q8 table for each token; with pe, row i also adds pe[(pos0 + i % n_tok) * k ..]
 int embed_q8_launch(const int32_t* tokens, size_t m, const int8_t* q, const float* scales, size_t n_vocab,
-                    size_t k, float* out, int* err, cudaStream_t st);
+                    size_t k, const float* pe, size_t pos0, size_t n_tok, float* out, int* err, cudaStream_t st);
 int greedy_launch(float* logits, size_t m, size_t n_vocab, const int32_t* recent, size_t recent_stride,
                   size_t n_recent, size_t window, float penalty, int32_t* out, size_t out_stride, int* err,
                   cudaStream_t st);

@@ -122,7 +122,7 @@ int layer_body(zwg_llm_state* st, size_t layer, const zwg_llm_weights* w, float*
     rc = llm_attn(st, layer, sc.q, n_past, n, sc.attn, s);
     if (rc) return rc;
     // src/llm.zig:203-204
-    if (zwg::q8_linear_launch(sc.attn, M, ne, L.wo.q, L.wo.scales, nullptr, ne, 1, x, s))
+    if (zwg::q8_linear_launch(sc.attn, M, ne, L.wo.q, L.wo.scales, nullptr, ne, zwg::LIN_ADD, x, s))
         return cuda_fail("wo launch", cudaGetLastError());
     // src/llm.zig:206-210
     if (zwg::rms_norm_launch(x, ne, M, ne, L.ffn_norm, w->eps, sc.h, ne, s)) return cuda_fail("rms_norm launch", cudaGetLastError());
@@ -135,7 +135,7 @@ int layer_body(zwg_llm_state* st, size_t layer, const zwg_llm_weights* w, float*
     p.n_pairs = (int)n_ff;
     p.out = sc.g;
     if (zwg::q8_pair_launch(p, zwg::PAIR_SILU, s)) return cuda_fail("gate/up launch", cudaGetLastError());
-    if (zwg::q8_linear_launch(sc.g, M, n_ff, L.w_down.q, L.w_down.scales, nullptr, ne, 1, x, s))
+    if (zwg::q8_linear_launch(sc.g, M, n_ff, L.w_down.q, L.w_down.scales, nullptr, ne, zwg::LIN_ADD, x, s))
         return cuda_fail("w_down launch", cudaGetLastError());
     return ZWG_OK;
 }
@@ -166,7 +166,7 @@ int zwg_linear_q8_add(const float* x, size_t m, size_t k, const int8_t* q, const
     if (!al16(x) || !al16(q)) return fail("linear_q8_add: x and q must be 16-byte aligned");
     if (!al4(scales) || !al4(out)) return fail("linear_q8_add: f32 buffers must be 4-byte aligned");
     if (n >= (1u << 30) || k >= (1u << 30) || m >= (1u << 30)) return fail("linear_q8_add: matrix too large");
-    if (zwg::q8_linear_launch(x, m, k, q, scales, nullptr, n, 1, out, (cudaStream_t)stream))
+    if (zwg::q8_linear_launch(x, m, k, q, scales, nullptr, n, zwg::LIN_ADD, out, (cudaStream_t)stream))
         return cuda_fail("linear_q8_add launch", cudaGetLastError());
     return ZWG_OK;
 }
@@ -202,7 +202,7 @@ int zwg_embed_q8(const int32_t* tokens, size_t m, const int8_t* q, const float* 
     if (!tokens || !q || !scales || !out) return fail("embed_q8: null buffer");
     if (!al4(tokens) || !al4(scales) || !al4(out)) return fail("embed_q8: 4-byte alignment required");
     if (m >= (1u << 31) || n_vocab >= (1u << 31) || k >= (1u << 30)) return fail("embed_q8: too large");
-    if (zwg::embed_q8_launch(tokens, m, q, scales, n_vocab, k, out, c->err, (cudaStream_t)stream))
+    if (zwg::embed_q8_launch(tokens, m, q, scales, n_vocab, k, nullptr, 0, 1, out, c->err, (cudaStream_t)stream))
         return cuda_fail("embed_q8 launch", cudaGetLastError());
     return ZWG_OK;
 }
@@ -284,7 +284,7 @@ int zwg_llm_forward_q8(zwg_llm_state* st, const zwg_llm_weights* w, const int32_
     if (scratch_bytes < sc.bytes) return fail("llm_forward_q8: scratch %zu bytes, %zu needed", scratch_bytes, sc.bytes);
     const cudaStream_t s = (cudaStream_t)stream;
     // src/llm.zig:175
-    if (zwg::embed_q8_launch(tokens, M, w->embd.q, w->embd.scales, w->n_vocab, ne, x, c->err, s))
+    if (zwg::embed_q8_launch(tokens, M, w->embd.q, w->embd.scales, w->n_vocab, ne, nullptr, 0, 1, x, c->err, s))
         return cuda_fail("embed launch", cudaGetLastError());
     for (size_t l = 0; l < st->n_layer; l++) {
         rc = layer_body(st, l, w, x, n_past, n, sc, s);
@@ -293,7 +293,8 @@ int zwg_llm_forward_q8(zwg_llm_state* st, const zwg_llm_weights* w, const int32_
     // src/llm.zig:212-215: the last token of each sequence
     if (zwg::rms_norm_launch(x + (n - 1) * ne, n * ne, st->n_batch, ne, w->output_norm, w->eps, sc.h, ne, s))
         return cuda_fail("rms_norm launch", cudaGetLastError());
-    if (zwg::q8_linear_launch(sc.h, st->n_batch, ne, w->output.q, w->output.scales, nullptr, w->n_vocab, 0, logits, s))
+    if (zwg::q8_linear_launch(sc.h, st->n_batch, ne, w->output.q, w->output.scales, nullptr, w->n_vocab, zwg::LIN_STORE,
+                              logits, s))
         return cuda_fail("logits launch", cudaGetLastError());
     return ZWG_OK;
 }

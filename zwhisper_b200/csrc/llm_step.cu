@@ -1,13 +1,18 @@
-// The small kernels of a Qwen2 decode step around the projections and the attention
-// (src/llm.zig:168-216, 268-273, 313-321), launched as chained launches (chain.cuh) so
-// each one's start overlaps the end of the kernel before it.
+// The small kernels of a decode step around the projections and the attention (Qwen2:
+// src/llm.zig:168-216, 268-273, 313-321; the Whisper decoder: src/decoder.zig:166-206),
+// launched as chained launches (chain.cuh) so each one's start overlaps the end of the
+// kernel before it.
 //
 // rms_norm_kernel: ops.rmsNorm (src/ops.zig:408-425), one CTA per row: the sum of squares
 //   (f32, tree order), inv = 1 / sqrt(ss / n + eps) with correctly rounded division and
 //   square root, out = x * inv * w as two rounded products in the reference's order.
+// layer_norm_kernel: ops.layerNorm (src/ops.zig:355-398), one CTA per row: the mean, then
+//   the population variance about it, inv = 1 / sqrt(var + eps), out = fma((x - mean) * inv,
+//   w, b) as the reference's vector loop.
 // embed_q8_kernel: Q8.row (src/gemm.zig:256-263) for the token of each row: q * scale in
-//   f32, bit-identical to the reference. A token outside the vocabulary writes a zero row
-//   and sets the device error word.
+//   f32, bit-identical to the reference; with a positional table the row then adds its
+//   position's row, as the Whisper decoder does (src/decoder.zig:172-176). A token outside
+//   the vocabulary writes a zero row and sets the device error word.
 // greedy_kernel: Model.penalize then Model.argmax (src/llm.zig:313-321, 268-273), one CTA
 //   per sequence: the repeat penalty over the last `window` generated tokens (repeats are
 //   penalized again, as in the reference), then the first index of the largest logit (NaN
@@ -17,6 +22,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <climits>
 
 #include "chain.cuh"
@@ -60,8 +66,61 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, size_t x_
     }
 }
 
+__global__ void __launch_bounds__(256) layer_norm_kernel(const float* x, size_t x_stride, int n,
+                                                         const float* __restrict__ w, const float* __restrict__ bias,
+                                                         float eps, float* out, size_t out_stride) {
+    chain_release();
+    const int z = chain_wait();
+    const float* row = x + blockIdx.x * x_stride + z;
+    float* o = out + blockIdx.x * out_stride + z;
+    __shared__ float part[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // mean, then the population variance about it (two passes, as the reference)
+    float s = 0.f;
+    for (int j = threadIdx.x * 4; j < n; j += 1024) {
+        const float4 v = __ldca(reinterpret_cast<const float4*>(row + j));
+        s += (v.x + v.y) + (v.z + v.w);
+    }
+    s = warp_sum(s);
+    if (lane == 0) part[warp] = s;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) tot += part[i];
+    const float mean = __fdiv_rn(tot, (float)n);
+    __syncthreads();
+    float q = 0.f;
+    for (int j = threadIdx.x * 4; j < n; j += 1024) {
+        const float4 v = __ldca(reinterpret_cast<const float4*>(row + j));
+        const float a = __fsub_rn(v.x, mean), b = __fsub_rn(v.y, mean), c = __fsub_rn(v.z, mean), d = __fsub_rn(v.w, mean);
+        q = fmaf(a, a, q);
+        q = fmaf(b, b, q);
+        q = fmaf(c, c, q);
+        q = fmaf(d, d, q);
+    }
+    q = warp_sum(q);
+    if (lane == 0) part[warp] = q;
+    __syncthreads();
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) sq += part[i];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)n), eps)));
+    for (int j = threadIdx.x * 4; j < n; j += 1024) {
+        const float4 v = __ldca(reinterpret_cast<const float4*>(row + j));
+        const float4 g = __ldg(reinterpret_cast<const float4*>(w + j));
+        const float4 h = __ldg(reinterpret_cast<const float4*>(bias + j));
+        float4 r;
+        r.x = fmaf(__fmul_rn(__fsub_rn(v.x, mean), inv), g.x, h.x);
+        r.y = fmaf(__fmul_rn(__fsub_rn(v.y, mean), inv), g.y, h.y);
+        r.z = fmaf(__fmul_rn(__fsub_rn(v.z, mean), inv), g.z, h.z);
+        r.w = fmaf(__fmul_rn(__fsub_rn(v.w, mean), inv), g.w, h.w);
+        *reinterpret_cast<float4*>(o + j) = r;
+    }
+}
+
 __global__ void __launch_bounds__(256) embed_q8_kernel(const int32_t* tokens, const int8_t* __restrict__ q,
                                                        const float* __restrict__ scales, int n_vocab, int k,
+                                                       const float* __restrict__ pe, int pos0, int n_tok,
                                                        float* out, int* err) {
     chain_release();
     const int z = chain_wait();
@@ -74,7 +133,11 @@ __global__ void __launch_bounds__(256) embed_q8_kernel(const int32_t* tokens, co
     }
     const int8_t* qr = q + (size_t)t * k;
     const float* sr = scales + (size_t)t * (k / 32);
-    for (int j = threadIdx.x; j < k; j += blockDim.x) o[j] = __fmul_rn((float)__ldg(qr + j), __ldg(sr + (j >> 5)));
+    const float* pr = pe ? pe + (size_t)(pos0 + (int)(blockIdx.x % n_tok)) * k : nullptr;
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+        const float v = __fmul_rn((float)__ldg(qr + j), __ldg(sr + (j >> 5)));
+        o[j] = pr ? __fadd_rn(v, __ldg(pr + j)) : v;
+    }
 }
 
 __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
@@ -189,11 +252,20 @@ int rms_norm_launch(const float* x, size_t x_stride, size_t m, size_t n, const f
                : -1;
 }
 
+int layer_norm_launch(const float* x, size_t x_stride, size_t m, size_t n, const float* w, const float* b, float eps,
+                      float* out, size_t out_stride, cudaStream_t st) {
+    if (m == 0) return 0;
+    return launch_chained(layer_norm_kernel, dim3((unsigned)m), dim3(256), st, x, x_stride, (int)n, w, b, eps, out,
+                          out_stride) == cudaSuccess
+               ? 0
+               : -1;
+}
+
 int embed_q8_launch(const int32_t* tokens, size_t m, const int8_t* q, const float* scales, size_t n_vocab, size_t k,
-                    float* out, int* err, cudaStream_t st) {
+                    const float* pe, size_t pos0, size_t n_tok, float* out, int* err, cudaStream_t st) {
     if (m == 0) return 0;
     return launch_chained(embed_q8_kernel, dim3((unsigned)m), dim3(256), st, tokens, q, scales, (int)n_vocab, (int)k,
-                          out, err) == cudaSuccess
+                          pe, (int)pos0, (int)std::max<size_t>(1, n_tok), out, err) == cudaSuccess
                ? 0
                : -1;
 }

@@ -20,8 +20,10 @@
 //   widens them to f32 exactly (byte permute into a 2^23 float, then one packed
 //   subtraction), takes the dot with the same k range of every x row (packed f32x2 FMAs)
 //   and scales it by the block's scale. Warp shuffles sum the lanes; the bias is added on
-//   the way out, or the result is added into `out` (the residual: ops.linear then ops.add,
-//   src/llm.zig:203-204, 209-210).
+//   the way out; the epilogue then stores, adds into `out` (the residual: ops.linear then
+//   ops.add, src/llm.zig:203-204, 209-210; src/decoder.zig:185-186) or applies GELU
+//   (ops.linear then ops.gelu, src/decoder.zig:197-198). One launch covers all full chunks of
+//   8 x rows (grid.y), the remainder a second.
 // q8_pair_kernel<MR, RP, KS, UNR, EPI>: the same dot products for two matrices' rows at once, a warp
 //   owning RP pairs of rows whose outputs one epilogue combines:
 //   - PAIR_ROPE: rows i and i + d/2 of one head of the q, k or v projection
@@ -269,10 +271,17 @@ __device__ __forceinline__ void reduce_splits(float2 (&acc)[RW][(MR + 1) / 2], i
     }
 }
 
+// ggml's GELU, the tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) with the
+// reference's operation order (src/ops.zig:312-327); tanh is CUDA's tanhf.
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float u = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(u)));
+}
+
 template <int MR, int RW, int KS, int UNR>
 __global__ void __launch_bounds__(256, MR >= 4 ? 1 : (RW * UNR >= 8 || (MR == 2 && RW >= 4)) ? 2 : 3) q8_linear_kernel(const float* x, int m, int k,
                                                         const int8_t* __restrict__ wq, const float* __restrict__ ws,
-                                                        const float* __restrict__ bias, int n, int accum,
+                                                        const float* __restrict__ bias, int n, int mode,
                                                         float* out) {
     constexpr int MP = (MR + 1) / 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -290,8 +299,9 @@ __global__ void __launch_bounds__(256, MR >= 4 ? 1 : (RW * UNR >= 8 || (MR == 2 
         sr[r] = ws + (size_t)row * nb;
     }
     const int z = chain_prologue<RW>(wr, sr, kbeg, kend, lane);
-    x += z;
-    out += z;
+    // blockIdx.y walks chunks of MR rows of x (one launch for all full chunks)
+    x += z + (size_t)blockIdx.y * MR * k;
+    out += z + (size_t)blockIdx.y * MR * n;
     float2 acc[RW][MP];
     dot_rows<MR, RW, UNR>(x, m, k, kbeg, kend, wr, sr, lane, acc);
     reduce_splits<MR, RW, KS>(acc, warp, lane);
@@ -305,7 +315,9 @@ __global__ void __launch_bounds__(256, MR >= 4 ? 1 : (RW * UNR >= 8 || (MR == 2 
                 float v = (mr & 1) ? acc[r][mr >> 1].y : acc[r][mr >> 1].x;
                 if (bias) v = __fadd_rn(v, bias[row0 + r]);
                 float* o = out + (size_t)mr * n + row0 + r;
-                *o = accum ? __fadd_rn(__ldcg(o), v) : v;
+                if (mode == LIN_ADD) v = __fadd_rn(__ldcg(o), v);
+                else if (mode == LIN_GELU) v = gelu_tanh(v);
+                *o = v;
             }
         }
 }
@@ -436,26 +448,26 @@ inline Plan plan(int mc, size_t rows, int pair, int sms) {
 }
 
 template <int MR, int UNR, int KS>
-cudaError_t linear_cfg(unsigned grid, cudaStream_t st, const float* x, int mc, int k, const int8_t* wq,
-                       const float* ws, const float* bias, int n, int accum, float* out) {
-    return launch_chained(q8_linear_kernel<MR, 4, KS, UNR>, dim3(grid), dim3(32 * WARPS), st, x, mc, k, wq, ws, bias, n,
-                          accum, out);
+cudaError_t linear_cfg(dim3 grid, cudaStream_t st, const float* x, int mc, int k, const int8_t* wq, const float* ws,
+                       const float* bias, int n, int mode, float* out) {
+    return launch_chained(q8_linear_kernel<MR, 4, KS, UNR>, grid, dim3(32 * WARPS), st, x, mc, k, wq, ws, bias, n,
+                          mode, out);
 }
 
 template <int MR>
-cudaError_t linear_chunk(Plan pl, unsigned grid, cudaStream_t st, const float* x, int mc, int k, const int8_t* wq,
-                         const float* ws, const float* bias, int n, int accum, float* out) {
+cudaError_t linear_chunk(Plan pl, dim3 grid, cudaStream_t st, const float* x, int mc, int k, const int8_t* wq,
+                         const float* ws, const float* bias, int n, int mode, float* out) {
     if constexpr (MR <= 2) {
         switch (pl.ks) {
-            case 2: return linear_cfg<MR, 1, 2>(grid, st, x, mc, k, wq, ws, bias, n, accum, out);
-            case 4: return linear_cfg<MR, 1, 4>(grid, st, x, mc, k, wq, ws, bias, n, accum, out);
-            case 8: return linear_cfg<MR, 1, 8>(grid, st, x, mc, k, wq, ws, bias, n, accum, out);
+            case 2: return linear_cfg<MR, 1, 2>(grid, st, x, mc, k, wq, ws, bias, n, mode, out);
+            case 4: return linear_cfg<MR, 1, 4>(grid, st, x, mc, k, wq, ws, bias, n, mode, out);
+            case 8: return linear_cfg<MR, 1, 8>(grid, st, x, mc, k, wq, ws, bias, n, mode, out);
             default:
-                if (pl.unr == 2) return linear_cfg<MR, 2, 1>(grid, st, x, mc, k, wq, ws, bias, n, accum, out);
-                return linear_cfg<MR, 1, 1>(grid, st, x, mc, k, wq, ws, bias, n, accum, out);
+                if (pl.unr == 2) return linear_cfg<MR, 2, 1>(grid, st, x, mc, k, wq, ws, bias, n, mode, out);
+                return linear_cfg<MR, 1, 1>(grid, st, x, mc, k, wq, ws, bias, n, mode, out);
         }
     } else {
-        return linear_cfg<MR, 1, 1>(grid, st, x, mc, k, wq, ws, bias, n, accum, out);
+        return linear_cfg<MR, 1, 1>(grid, st, x, mc, k, wq, ws, bias, n, mode, out);
     }
 }
 
@@ -495,22 +507,33 @@ static int sm_count_current() {
 }
 
 int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
-                     size_t n, int accum, float* out, cudaStream_t st) {
+                     size_t n, int mode, float* out, cudaStream_t st) {
     if (m == 0 || n == 0) return 0;
     const int sms = sm_count_current();
-    for (size_t m0 = 0; m0 < m; m0 += 8) {
+    const int ik = (int)k, in = (int)n;
+    size_t m0 = 0;
+    if (m >= 16) {
+        // all full chunks of 8 rows in one launch (grid.y = chunk)
+        const size_t full = m / 8;
+        if (full >= 65536) return -1;
+        const q8::Plan pl = q8::plan(8, n, 0, sms);
+        const size_t rows_per_cta = (size_t)(q8::WARPS / pl.ks) * pl.rw;
+        const dim3 grid((unsigned)((n + rows_per_cta - 1) / rows_per_cta), (unsigned)full);
+        if (q8::linear_chunk<8>(pl, grid, st, x, 8, ik, wq, ws, bias, in, mode, out) != cudaSuccess) return -1;
+        m0 = full * 8;
+    }
+    for (; m0 < m; m0 += 8) {
         const int mc = (int)std::min<size_t>(8, m - m0);
         const float* xc = x + m0 * k;
         float* oc = out + m0 * n;
         const q8::Plan pl = q8::plan(mc, n, 0, sms);
         const size_t rows_per_cta = (size_t)(q8::WARPS / pl.ks) * pl.rw;
-        const unsigned grid = (unsigned)((n + rows_per_cta - 1) / rows_per_cta);
-        const int ik = (int)k, in = (int)n;
+        const dim3 grid((unsigned)((n + rows_per_cta - 1) / rows_per_cta));
         cudaError_t e;
-        if (mc == 1) e = q8::linear_chunk<1>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
-        else if (mc == 2) e = q8::linear_chunk<2>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
-        else if (mc <= 4) e = q8::linear_chunk<4>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
-        else e = q8::linear_chunk<8>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, accum, oc);
+        if (mc == 1) e = q8::linear_chunk<1>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, mode, oc);
+        else if (mc == 2) e = q8::linear_chunk<2>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, mode, oc);
+        else if (mc <= 4) e = q8::linear_chunk<4>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, mode, oc);
+        else e = q8::linear_chunk<8>(pl, grid, st, xc, mc, ik, wq, ws, bias, in, mode, oc);
         if (e != cudaSuccess) return -1;
     }
     return 0;

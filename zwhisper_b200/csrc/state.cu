@@ -15,14 +15,6 @@
 
 using namespace zwg::capi;
 
-struct zwg_dec_state {
-    int device = -1;
-    size_t n_layer = 0, n_batch = 0, n_state = 0, n_head = 0, n_text_ctx = 0, n_audio_ctx = 0;
-    // per layer: self K/V [n_batch][n_text_ctx][n_state], cross K/V [n_batch][n_audio_ctx][n_state]
-    std::vector<float*> self_k, self_v, cross_k, cross_v;
-    DevBuf ws;
-};
-
 namespace {
 
 void free_all(std::vector<float*>& v) {

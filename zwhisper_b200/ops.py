@@ -15,7 +15,9 @@ stream): `attention_dev`, `enc_attn_bf16`, `rope_kt_append`, `f32_to_bf16`; the 
 states `DecoderState` and `LlmState`; the Q8 projections `quantize_q8`, `linear_q8`,
 `linear_q8_add`, `linear_q8_silu_mul`; and the rest of the Qwen2 decode step (src/llm.zig:
 168-216, 268-321): `rms_norm`, `embed_q8`, `llm_greedy`, `LlmWeightsQ8` with
-`LlmState.qkv_q8 / layer_q8 / forward_q8`.
+`LlmState.qkv_q8 / layer_q8 / forward_q8`; and the Whisper decoder step (src/decoder.zig:
+151-206): `layer_norm`, `linear_q8_gelu`, `DecoderWeightsQ8` with
+`DecoderState.set_audio_q8 / forward_q8`.
 """
 from __future__ import annotations
 
@@ -309,6 +311,15 @@ class DecoderState:
         _lib.check(_lib.load().zwg_dec_state_cache(self._h, layer, *(ctypes.byref(x) for x in p)))
         return tuple(x.value for x in p)
 
+    def cache_views(self, layer: int):
+        """Torch views (no copy) of one layer's buffers: self K, self V [n_batch][n_text_ctx]
+        [n_state] and cross K, cross V [n_batch][n_audio_ctx][n_state]. Valid until close()."""
+        torch = _torch()
+        ptrs = self.cache_ptrs(layer)
+        dev = torch.device("cuda", self.device)
+        shapes = [(self.n_batch, self.n_text_ctx, self.n_state)] * 2 + [(self.n_batch, self.n_audio_ctx, self.n_state)] * 2
+        return tuple(torch.as_tensor(_DeviceArray(p, shp), device=dev) for p, shp in zip(ptrs, shapes))
+
     def set_cross(self, layer: int, window: int, k, v) -> None:
         """setAudio for one window and layer (src/decoder.zig:150-156): k, v [n_audio_ctx][n_state]."""
         torch = _torch()
@@ -342,6 +353,43 @@ class DecoderState:
             _dev_ptr(out, torch.float32, "out"), _stream_of(q)))
         return out
 
+
+    def set_audio_q8(self, weights: "DecoderWeightsQ8", window: int, enc) -> None:
+        """setAudio (src/decoder.zig:151-159) on the device: enc [n_audio_ctx][n_state] (CUDA
+        f32) -> every layer's cross K/V of `window`."""
+        torch = _torch()
+        if enc.numel() != self.n_audio_ctx * self.n_state:
+            raise ValueError("enc must hold n_audio_ctx * n_state floats")
+        _lib.check(_lib.load().zwg_dec_set_audio_q8(self._h, ctypes.byref(weights.c_struct()), window,
+                                                    _dev_ptr(enc, torch.float32, "enc"), _stream_of(enc)))
+
+    def scratch(self, n: int, scratch=None):
+        """A CUDA uint8 buffer of at least zwg_dec_scratch_bytes for chunks of n tokens."""
+        torch = _torch()
+        need = _lib.load().zwg_dec_scratch_bytes(self._h, n)
+        if scratch is None or scratch.numel() < need:
+            scratch = torch.empty(max(need, 256), dtype=torch.uint8, device=torch.device("cuda", self.device))
+        return scratch
+
+    def forward_q8(self, weights: "DecoderWeightsQ8", tokens, n_past: int, x=None, logits=None, scratch=None):
+        """Decoder.forward (src/decoder.zig:166-206) for every window: tokens CUDA int32
+        [n_batch][n] at positions n_past..; returns (x [n_batch][n][n_state], logits
+        [n_batch][n_vocab] of each window's last token)."""
+        torch = _torch()
+        if tokens.dtype != torch.int32 or not tokens.is_contiguous() or tokens.numel() % self.n_batch:
+            raise ValueError("tokens must be a contiguous int32 [n_batch][n] tensor")
+        n = tokens.numel() // self.n_batch
+        dev = tokens.device
+        if x is None:
+            x = torch.empty(self.n_batch, n, self.n_state, dtype=torch.float32, device=dev)
+        if logits is None:
+            logits = torch.empty(self.n_batch, weights.n_vocab, dtype=torch.float32, device=dev)
+        scratch = self.scratch(n, scratch)
+        _lib.check(_lib.load().zwg_dec_forward_q8(self._h, ctypes.byref(weights.c_struct()), tokens.data_ptr(),
+                                                  n_past, n, _dev_ptr(x, torch.float32, "x"),
+                                                  _dev_ptr(logits, torch.float32, "logits"), scratch.data_ptr(),
+                                                  scratch.numel(), _stream_of(tokens)))
+        return x, logits
 
 class _DeviceArray:
     """A float32 device buffer described by __cuda_array_interface__ (for zero-copy views)."""
@@ -659,4 +707,104 @@ class LlmWeightsQ8:
             self._c = _lib.LlmWeightsC(self.n_vocab, self.n_embd, self.n_ff, self.eps, self._mat(self.embd),
                                        self._mat(self.output), self.output_norm.data_ptr(),
                                        ctypes.cast(arr, ctypes.POINTER(_lib.LlmLayerWeightsC)))
+        return self._c
+
+
+
+def layer_norm(x, w, b, eps: float = 1e-5, out=None):
+    """ops.layerNorm (src/ops.zig:355-398) of the rows of a CUDA f32 [m][n] tensor."""
+    torch = _torch()
+    n = x.shape[-1]
+    m = x.numel() // n
+    out = torch.empty_like(x) if out is None else out
+    _lib.ensure_init(x.device.index or 0)
+    _lib.check(_lib.load().zwg_layer_norm(_dev_ptr(x, torch.float32, "x"), m, n, _dev_ptr(w, torch.float32, "w"),
+                                          _dev_ptr(b, torch.float32, "b"), float(eps),
+                                          _dev_ptr(out, torch.float32, "out"), _stream_of(x)))
+    return out
+
+
+def linear_q8_gelu(x, q, scales, bias=None, out=None):
+    """gelu(x . W^T + b) with Q8 W (src/decoder.zig:197-198, ggml's tanh GELU)."""
+    torch = _torch()
+    m, k = x.shape
+    q, sp = _q8_pair((q, scales), "w")
+    n = q.shape[0]
+    out = torch.empty(m, n, dtype=torch.float32, device=x.device) if out is None else out
+    _lib.ensure_init(x.device.index or 0)
+    _lib.check(_lib.load().zwg_linear_q8_gelu(_dev_ptr(x, torch.float32, "x"), m, k, q.data_ptr(), sp,
+                                              _dev_ptr(bias, torch.float32, "bias") if bias is not None else None,
+                                              n, _dev_ptr(out, torch.float32, "out"), _stream_of(x)))
+    return out
+
+
+class DecoderWeightsQ8:
+    """The Whisper decoder's weights on the device (decoder.Decoder / decoder.Layer,
+    src/decoder.zig:13-60) and the zwg_dec_weights struct that points at them. `tensors` maps
+    the model file's names (decoder.token_embedding.weight, decoder.positional_embedding,
+    decoder.ln.weight/bias, decoder.blocks.{i}.attn.query.weight, ...) to numpy or torch
+    arrays (f16 or f32). The 2-d decoder matrices are quantized to Q8 on the device as the
+    reference's loader does (Q8.quantize from the f16 values, src/decoder.zig:220-229); norms,
+    biases and the position table stay f32."""
+
+    ATTN = ("query", "key", "value", "out")
+
+    def __init__(self, tensors, n_layer: int, device: int = 0):
+        torch = _torch()
+        dev = torch.device("cuda", device)
+        _lib.ensure_init(device)
+
+        def f32(name):
+            a = tensors[name]
+            if not isinstance(a, torch.Tensor):
+                a = torch.from_numpy(np.ascontiguousarray(a))
+            return a.to(device=dev, dtype=torch.float32).contiguous()
+
+        def q8(name):
+            return quantize_q8(f32(name))
+
+        self.te = q8("decoder.token_embedding.weight")
+        self.pe = f32("decoder.positional_embedding")
+        self.ln_w, self.ln_b = f32("decoder.ln.weight"), f32("decoder.ln.bias")
+        self.n_vocab, self.n_state = self.te[0].shape
+        self.layers = []
+        for i in range(n_layer):
+            p = f"decoder.blocks.{i}."
+            L = {
+                "attn_ln_w": f32(p + "attn_ln.weight"), "attn_ln_b": f32(p + "attn_ln.bias"),
+                "q": q8(p + "attn.query.weight"), "q_b": f32(p + "attn.query.bias"),
+                "k": q8(p + "attn.key.weight"),
+                "v": q8(p + "attn.value.weight"), "v_b": f32(p + "attn.value.bias"),
+                "o": q8(p + "attn.out.weight"), "o_b": f32(p + "attn.out.bias"),
+                "cross_ln_w": f32(p + "cross_attn_ln.weight"), "cross_ln_b": f32(p + "cross_attn_ln.bias"),
+                "cq": q8(p + "cross_attn.query.weight"), "cq_b": f32(p + "cross_attn.query.bias"),
+                "ck": q8(p + "cross_attn.key.weight"),
+                "cv": q8(p + "cross_attn.value.weight"), "cv_b": f32(p + "cross_attn.value.bias"),
+                "co": q8(p + "cross_attn.out.weight"), "co_b": f32(p + "cross_attn.out.bias"),
+                "mlp_ln_w": f32(p + "mlp_ln.weight"), "mlp_ln_b": f32(p + "mlp_ln.bias"),
+                "mlp0": q8(p + "mlp.0.weight"), "mlp0_b": f32(p + "mlp.0.bias"),
+                "mlp1": q8(p + "mlp.2.weight"), "mlp1_b": f32(p + "mlp.2.bias"),
+            }
+            self.layers.append(L)
+        self._c = None
+
+    @staticmethod
+    def _mat(pair):
+        return _lib.Q8MatC(pair[0].data_ptr(), pair[1].data_ptr())
+
+    def c_struct(self) -> _lib.DecWeightsC:
+        if self._c is None:
+            m = self._mat
+            arr = (_lib.DecLayerWeightsC * len(self.layers))(*[
+                _lib.DecLayerWeightsC(
+                    L["attn_ln_w"].data_ptr(), L["attn_ln_b"].data_ptr(), m(L["q"]), L["q_b"].data_ptr(), m(L["k"]),
+                    m(L["v"]), L["v_b"].data_ptr(), m(L["o"]), L["o_b"].data_ptr(), L["cross_ln_w"].data_ptr(),
+                    L["cross_ln_b"].data_ptr(), m(L["cq"]), L["cq_b"].data_ptr(), m(L["ck"]), m(L["cv"]),
+                    L["cv_b"].data_ptr(), m(L["co"]), L["co_b"].data_ptr(), L["mlp_ln_w"].data_ptr(),
+                    L["mlp_ln_b"].data_ptr(), m(L["mlp0"]), L["mlp0_b"].data_ptr(), m(L["mlp1"]),
+                    L["mlp1_b"].data_ptr())
+                for L in self.layers])
+            self._arr = arr  # keeps the host array alive as long as the struct
+            self._c = _lib.DecWeightsC(self.n_vocab, m(self.te), self.pe.data_ptr(), self.ln_w.data_ptr(),
+                                       self.ln_b.data_ptr(), ctypes.cast(arr, ctypes.POINTER(_lib.DecLayerWeightsC)))
         return self._c
