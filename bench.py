@@ -312,22 +312,23 @@ def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
              [(sh_s, q, ck, cv, o, ws_s, (ns, 448 * ns, 448 * ns, ns), B * 224 * ns * 4 * 2),
               (sh_c, q, xk, xv, o, ws_c, (ns, 1500 * ns, 1500 * ns, ns), B * 1500 * ns * 4 * 2)])
     del ck, cv, xk, xv
-    # configs 3 and 4: Qwen2 decode over the transposed key cache at the mean cache length
+    # configs 3 and 4: Qwen2 decode over the transposed key cache at the mean cache length,
+    # through the state's decode entry point (zwg_llm_attn_decode, src/llm.zig:191-202) over
+    # the state's own per-layer caches
     for cfg, B, layers, H, Hkv, d, n_kv in (("configs[3] Qwen2.5-0.5B", 16, 24, 14, 2, 64, 2128),
                                            ("configs[4] Qwen2.5-1.5B", 64, 28, 12, 2, 128, 2256)):
         n_ctx = 2560
         kvw = Hkv * d
-        kts = [randn(B, Hkv, d, n_ctx) for _ in range(layers)]
-        vs = [randn(B, n_ctx, kvw) for _ in range(layers)]
-        q, o = randn(B, H * d), torch.empty(B, H * d, device=dev)
-        sh = ops.AttnShape(1, n_kv, H, Hkv, d, H * d, kvw, H * d, True, n_ctx)
-        ws = torch.empty(max(1, ops.attention_workspace_bytes(sh, B)), dtype=torch.uint8, device=dev)
-        bs = (H * d, Hkv * d * n_ctx, n_ctx * kvw, H * d)
+        st = ops.LlmState(layers, B, H, Hkv, d, n_ctx, device=dev.index or 0)
+        for layer in range(layers):
+            for t_ in st.cache_views(layer):
+                t_.normal_(generator=g)
+        q, o = randn(B, 1, H * d), torch.empty(B, 1, H * d, device=dev)
         byts = B * n_kv * kvw * 4 * 2
 
-        def step(kts=kts, vs=vs, q=q, o=o, sh=sh, ws=ws, bs=bs, B=B):
-            for layer in range(len(kts)):
-                ops.attention_dev(q, kts[layer], vs[layer], sh, o, n_batch=B, batch_strides=bs, workspace=ws)
+        def step(st=st, q=q, o=o, layers=layers, n_kv=n_kv):
+            for layer in range(layers):
+                st.attn(layer, q, n_kv - 1, out=o)
         # math "f32": the SIMT split-K kernel (the reference's arithmetic); "tf32": the
         # tcgen05 kernel (tf32 operands, f32 accumulation; parity within max-abs 2e-3)
         for math, kernel in (("f32", "decode_tma_kernel"), ("tf32", "decode_tc_kernel")):
@@ -345,7 +346,7 @@ def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
                         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                                      "frac": achieved / hbm_peak, "traffic": traffic,
                                      "bytes_per_launch": byts}})
-        del kts, vs
+        st.close()
     torch.cuda.empty_cache()
     return res
 
@@ -741,7 +742,9 @@ def run_kernel_case(args):
     prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2);
     `q8_logits` = the Q8 linear kernel on the Whisper base.en logits product (51864 x 512);
     `step_qwen15` = one whole Qwen2.5-1.5B greedy decode step for one sequence (n_kv 2256),
-    every kernel of the step in launch order (about 200 launches); `pair_qwen15` = the two
+    every kernel of the step in launch order (about 200 launches); `step_whisper_base` = one
+    Whisper base.en decoder step for 32 windows (config 1: 224 cached positions, 1500 audio
+    frames); `pair_qwen15` = the two
     paired-row Q8 kernels of one Qwen2.5-1.5B layer for one sequence: q/k/v + RoPE + cache
     append (3.5 MB of weights) then gate/up + SiLU*up (31 MB)."""
     import torch
@@ -791,6 +794,21 @@ def run_kernel_case(args):
         W = qwen15_weights(dev)
         st, fn = qwen15_step_fn(W, 1, 2560, 2255, dev)
         work = "one decode step: 1.74 GB of Q8 weights + 129 MB of K/V"
+    elif args.kernel_case == "step_whisper_base":
+        B, n_past, na, ns = 32, 224, 1500, 512
+        Wd = whisper_base_decoder(dev)
+        st = ops.DecoderState(6, B, ns, 8, 448, na, device=0)
+        for w in range(B):
+            st.set_audio_q8(Wd, w, torch.randn(na, ns, generator=g, device=dev))
+        tok = torch.randint(0, 51864, (B, 1), generator=g, device=dev, dtype=torch.int32)
+        x = torch.empty(B, 1, ns, device=dev)
+        logits = torch.empty(B, 51864, device=dev)
+        scratch = st.scratch(1)
+
+        def fn():
+            st.forward_q8(Wd, tok, n_past, x=x, logits=logits, scratch=scratch)
+            ops.llm_greedy(logits, penalty=1.0, out=tok.view(-1))
+        work = "one decoder step for 32 windows: 27 MB of Q8 weights + 259 MB of K/V"
     elif args.kernel_case == "pair_qwen15":
         W = qwen15_weights(dev, n_layer=1)
         st = ops.LlmState(1, 1, QWEN15["n_head"], QWEN15["n_head_kv"], QWEN15["d"], 2560, device=0)
@@ -848,7 +866,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64",
                                              "decode_tc_qwen_b1", "decode_whisper", "prefill_qwen",
-                                             "q8_logits", "step_qwen15", "pair_qwen15"], default=None)
+                                             "q8_logits", "step_qwen15", "step_whisper_base", "pair_qwen15"],
+                    default=None)
     args = ap.parse_args()
     if args.kernel_case:
         run_kernel_case(args)

@@ -106,7 +106,7 @@ size_t workspace_bytes(const zwg_attn_shape* sh, size_t n_batch, int sm_count) {
 }
 
 int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
-            const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st) {
+            const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st, int* tickets) {
     const size_t nb = b ? b->n_batch : 1;
     if (nb == 0 || sh->n_q == 0) return ZWG_OK;
     const Plan pl = plan_for(sh, nb, c->sm_count);
@@ -122,6 +122,7 @@ int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q
         p.q_stride = sh->q_stride; p.kv_stride = sh->kv_stride; p.out_stride = sh->out_stride;
         p.kt_stride = sh->kt_stride; p.causal = sh->causal ? 1 : 0;
         p.n_splits = pl.n_splits; p.chunk = pl.chunk;
+        p.tickets = tickets;
         if (b) { p.q_bs = b->q_batch_stride; p.k_bs = b->k_batch_stride; p.v_bs = b->v_batch_stride; p.out_bs = b->out_batch_stride; }
         if (p.k_bs % 4 || p.v_bs % 4 || p.q_bs % 4) return fail("decode kernel needs batch strides that are multiples of 4");
         if ((c->math & ZWG_MATH_TF32) && zwg::decode_tc_supported(p, nb)) {
@@ -155,6 +156,7 @@ int sync_and_check(Ctx* c, cudaStream_t st) {
     if (e != cudaSuccess) return cuda_fail("error word read", e);
     if (h) {
         cudaMemset(c->err, 0, sizeof(int));
+        c->err_gen.fetch_add(1, std::memory_order_relaxed);
         if (h == zwg::kErrTimeout) {
             fail("a device-side wait timed out");
             return ZWG_TIMEOUT;

@@ -6,6 +6,7 @@
 #include <stddef.h>
 
 #include <algorithm>
+#include <atomic>
 #include <vector>
 
 #include "../../include/zwgpu.h"
@@ -39,9 +40,42 @@ struct Ctx {
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;  // second stream for pipelined host batches
     int* err = nullptr;           // device error word
+    // Counts the device errors sync_and_check has reported. A kernel that gave up may have
+    // left a segment ticket behind, so kept-zero ticket buffers are cleared again when this
+    // moved since their last clearing.
+    std::atomic<unsigned> err_gen{0};
     int math = ZWG_MATH_F32;
     DevBuf q[2], k[2], v[2], out[2], ws[2];
     DevBuf qh[2], kh[2], vh[2];   // bf16 copies for the tensor-core path
+};
+
+// Segment tickets of the split decode kernels, kept by a state for its own calls (which run
+// in one stream order): zero after every completed call, since the merging CTA resets its
+// ticket, so a call clears them only when a device error was reported since the last
+// clearing. Allocated and cleared when the state is made, so no call allocates (graph
+// capture stays legal); a clearing issued while the stream is being captured runs only when
+// the graph does, so it leaves the buffer marked for clearing by the next eager call.
+struct Tickets {
+    DevBuf buf;
+    unsigned gen = 0;  // Ctx::err_gen at the last clearing
+    bool init(const Ctx* c, size_t n) {
+        if (!buf.ensure(std::max<size_t>(n, 1) * sizeof(int))) return false;
+        if (cudaMemset(buf.ptr, 0, buf.cap) != cudaSuccess) return false;
+        gen = c->err_gen.load(std::memory_order_relaxed);
+        return true;
+    }
+    // n tickets, zero in `st`'s order, or nullptr (more than init made, or clearing failed).
+    int* get(const Ctx* c, size_t n, cudaStream_t st) {
+        if (!buf.ptr || n * sizeof(int) > buf.cap) return nullptr;
+        const unsigned now = c->err_gen.load(std::memory_order_relaxed);
+        if (gen != now) {
+            cudaStreamCaptureStatus cs = cudaStreamCaptureStatusActive;
+            const bool eager = cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
+            if (cudaMemsetAsync(buf.ptr, 0, buf.cap, st) != cudaSuccess) return nullptr;
+            if (eager) gen = now;
+        }
+        return static_cast<int*>(buf.ptr);
+    }
 };
 
 // The calling thread's context (zwg_init), or nullptr with the last error set.
@@ -54,8 +88,10 @@ int check_shape(const zwg_attn_shape* sh);
 // Workspace bytes run_dev needs for this shape and batch.
 size_t workspace_bytes(const zwg_attn_shape* sh, size_t n_batch, int sm_count);
 // One batched attention call on device pointers (the body of zwg_attention_dev).
+// tickets: n_batch * n_head_kv kept-zero ints (a state's Tickets), or nullptr to clear the
+// workspace's own before a split decode kernel.
 int run_dev(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
-            const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st);
+            const float* v, float* out, void* ws, size_t ws_bytes, cudaStream_t st, int* tickets = nullptr);
 
 // The calling thread's context, which must be on `device` (the device a state lives on);
 // nullptr with the last error set otherwise.
@@ -72,6 +108,7 @@ struct zwg_dec_state {
     // per layer: self K/V [n_batch][n_text_ctx][n_state], cross K/V [n_batch][n_audio_ctx][n_state]
     std::vector<float*> self_k, self_v, cross_k, cross_v;
     zwg::capi::DevBuf ws;
+    zwg::capi::Tickets tickets;
 };
 
 // Qwen2 LLM state (state.cu): the caches of every layer for n_batch sequences and the RoPE
@@ -84,6 +121,7 @@ struct zwg_llm_state {
     float* cos_tab = nullptr;  // [n_ctx][d/2]
     float* sin_tab = nullptr;
     zwg::capi::DevBuf ws;
+    zwg::capi::Tickets tickets;
 };
 
 namespace zwg {

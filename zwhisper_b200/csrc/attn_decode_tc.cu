@@ -487,9 +487,13 @@ int launch_d(const DecodeParams& p, size_t n_batch, int sm_count, cudaStream_t s
     a.n_items = (int)n_items;
     a.part = p.ws;
     const size_t parts = segs * MAX_PIECES * (size_t)a.group * (D + 2) * sizeof(float);
-    a.counters = reinterpret_cast<int*>(reinterpret_cast<char*>(p.ws) + ((parts + 255) / 256) * 256);
     a.err = err;
-    if (a.pieces > 1 && cudaMemsetAsync(a.counters, 0, segs * sizeof(int), st) != cudaSuccess) return -1;
+    if (p.tickets) {
+        a.counters = p.tickets;
+    } else {
+        a.counters = reinterpret_cast<int*>(reinterpret_cast<char*>(p.ws) + ((parts + 255) / 256) * 256);
+        if (a.pieces > 1 && cudaMemsetAsync(a.counters, 0, segs * sizeof(int), st) != cudaSuccess) return -1;
+    }
 
     // a single item: any valid batch stride
     const size_t k_bs = n_batch > 1 ? p.k_bs : p.n_head_kv * D * p.kt_stride;

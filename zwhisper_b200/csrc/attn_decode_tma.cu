@@ -670,12 +670,16 @@ int decode_tma_launch(const DecodeParams& p, size_t n_batch, int sm_count, int* 
     const int rmax = rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8;
     int grid = 1, p_max = 1, mode = 0, pieces = 1;
     decode_tma_schedule(n_batch, p.n_head_kv, p.n_kv, sm_count, &grid, &p_max, &mode, &pieces);
-    // the segment tickets follow the partials in the workspace; they must start at zero,
-    // and the last CTA of each segment puts its ticket back to zero
+    // the segment tickets must start at zero, and the last CTA of each segment puts its
+    // ticket back to zero: a kept-zero buffer of the caller's, or the workspace's tail
+    // cleared here. Mode 1 (whole segments per CTA) splits no segment and takes no ticket.
     const size_t segs = n_batch * p.n_head_kv;
     const size_t parts = segs * (size_t)p_max * rows * (p.d + 2) * sizeof(float);
-    int* counters = reinterpret_cast<int*>(reinterpret_cast<char*>(p.ws) + ((parts + 255) / 256) * 256);
-    if (cudaMemsetAsync(counters, 0, segs * sizeof(int), st) != cudaSuccess) return -1;
+    int* counters = p.tickets;
+    if (!counters) {
+        counters = reinterpret_cast<int*>(reinterpret_cast<char*>(p.ws) + ((parts + 255) / 256) * 256);
+        if (mode != 1 && cudaMemsetAsync(counters, 0, segs * sizeof(int), st) != cudaSuccess) return -1;
+    }
     const bool kt = p.kt_stride != 0;
     switch (p.d) {
         case 32: return kt ? launch_d<32, true>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st) : launch_d<32, false>(p, n_batch, rmax, grid, p_max, mode, pieces, counters, err, st);

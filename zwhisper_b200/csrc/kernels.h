@@ -33,6 +33,11 @@ struct DecodeParams {
     int n_splits;
     int chunk;  // keys per split
     size_t q_bs, k_bs, v_bs, out_bs;
+    // Segment tickets of the split decode kernels, n_batch * n_head_kv ints that are zero
+    // at launch; the last CTA of each segment puts its ticket back to zero, so a buffer the
+    // caller keeps for this alone needs no clearing between calls. nullptr: the tickets
+    // follow the partials in ws and are cleared on the stream before the kernel.
+    int* tickets;
 };
 
 int flash_f32_launch(const FlashParams& p, size_t n_batch, cudaStream_t st);

@@ -72,8 +72,10 @@ int zwg::capi::llm_attn(zwg_llm_state* st, size_t layer, const float* q, size_t 
     int rc = check_shape(&sh);
     if (!rc) rc = ensure_ws(st->ws, &sh, st->n_batch, c->sm_count);
     if (rc) return rc;
+    int* tk = st->tickets.get(c, st->n_batch * Hkv, (cudaStream_t)stream);
+    if (!tk) return fail("llm attention: ticket buffer");
     return run_dev(c, &sh, &b, q, st->cache_kt[layer], st->cache_v[layer], out, st->ws.ptr, st->ws.cap,
-                   (cudaStream_t)stream);
+                   (cudaStream_t)stream, tk);
 }
 
 extern "C" {
@@ -107,6 +109,7 @@ int zwg_dec_state_create(size_t n_layer, size_t n_batch, size_t n_state, size_t 
         zwg_attn_shape s2 = mha(rows, n_audio_ctx, n_state, n_head, false);
         rc = ensure_ws(st->ws, &s1, n_batch, c->sm_count);
         if (!rc) rc = ensure_ws(st->ws, &s2, n_batch, c->sm_count);
+        if (!rc && !st->tickets.init(c, n_batch * n_head)) rc = fail("decoder state: ticket buffer");
     }
     if (rc) {
         zwg_dec_state_destroy(st);
@@ -127,6 +130,7 @@ int zwg_dec_state_destroy(zwg_dec_state* st) {
     free_all(st->cross_k);
     free_all(st->cross_v);
     st->ws.release();
+    st->tickets.buf.release();
     if (dev >= 0) cudaSetDevice(dev);
     delete st;
     return ZWG_OK;
@@ -192,7 +196,9 @@ int zwg_dec_step_attn(zwg_dec_state* st, size_t layer, int kind, const float* q,
     int rc = check_shape(&sh);
     if (!rc) rc = ensure_ws(st->ws, &sh, nb, c->sm_count);
     if (rc) return rc;
-    return run_dev(c, &sh, &b, q, kp, vp, out, st->ws.ptr, st->ws.cap, s);
+    int* tk = st->tickets.get(c, nb * st->n_head, s);
+    if (!tk) return fail("dec_step_attn: ticket buffer");
+    return run_dev(c, &sh, &b, q, kp, vp, out, st->ws.ptr, st->ws.cap, s, tk);
 }
 
 // ---- Qwen2 LLM ----------------------------------------------------------------------------
@@ -239,6 +245,7 @@ int zwg_llm_state_create(size_t n_layer, size_t n_batch, size_t n_head, size_t n
         // worst case of a decode step: one query over the whole context
         zwg_attn_shape s1{1, n_ctx, n_head, n_head_kv, d, n_head * d, n_head_kv * d, n_head * d, 1, n_ctx};
         rc = ensure_ws(st->ws, &s1, n_batch, c->sm_count);
+        if (!rc && !st->tickets.init(c, n_batch * n_head_kv)) rc = fail("llm state: ticket buffer");
     }
     if (rc) {
         zwg_llm_state_destroy(st);
@@ -259,6 +266,7 @@ int zwg_llm_state_destroy(zwg_llm_state* st) {
     if (st->cos_tab) cudaFree(st->cos_tab);
     if (st->sin_tab) cudaFree(st->sin_tab);
     st->ws.release();
+    st->tickets.buf.release();
     if (dev >= 0) cudaSetDevice(dev);
     delete st;
     return ZWG_OK;
