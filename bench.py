@@ -18,8 +18,8 @@ Reported (one JSON line from rank 0):
              host cores, rank 0 at N=1;
   secondary  decode-attention workloads (configs 1, 3, 4) at N=1: tok/s and HBM roofline,
              each decode step (all layers) replayed from a CUDA graph; prefill attention;
-             the Q8 projections; and the whole Qwen2.5-1.5B greedy decode step on the
-             device (B = 1 and 64).
+             the whole small.en encoder on the device (configs[2]); the Q8 projections;
+             and the whole Qwen2.5-1.5B greedy decode step on the device (B = 1 and 64).
 
 `--impl reference` times the reference's CPU attention (the C restatement; the Zig source
 cannot be built here) on the same workload and prints the same line with "impl".
@@ -404,6 +404,39 @@ def secondary_prefill(dev, tc_peak, peak_kind, steps=2, warmup=1):
     return res
 
 
+def secondary_encoder(dev, tc_peak, peak_kind, steps=3, warmup=2):
+    """The whole Whisper small.en encoder on the device for 64 consecutive
+    windows: mel rows, both convolutions, 12 pre-norm blocks (f16 tcgen05 GEMMs with fused
+    bias / GELU / residual epilogues, the bf16 attention kernel) and ln_post
+    (zwg_enc_forward_f16), random-init f16 weights N(0, 0.02^2), a synthetic mel."""
+    import torch
+
+    from oracle import whisper as W
+    from zwhisper_b200 import ops
+    hp = W.SMALL_EN
+    B, n_ctx, ns, L = 64, hp.n_audio_ctx, hp.n_audio_state, hp.n_audio_layer
+    Wg = ops.EncoderWeightsF16(W.weights_dict(W.synth_model(hp, seed=0, encoder_only=True)), L, hp.n_audio_head,
+                               device=dev.index or 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    mel = torch.randn(hp.n_mels, B * 2 * n_ctx, generator=g, device=dev) * 0.5
+    out = torch.empty(B, n_ctx, ns, device=dev)
+    scratch = torch.empty(Wg.scratch_bytes(B), dtype=torch.uint8, device=dev)
+    t = time_graph(lambda: ops.encoder_forward(Wg, mel, B, out=out, scratch=scratch), steps, warmup) / steps
+    T = 2 * n_ctx
+    flops = B * (2 * T * ns * 3 * hp.n_mels + 2 * n_ctx * ns * 3 * ns
+                 + L * (2 * n_ctx * ns * 12 * ns + 4 * n_ctx * n_ctx * ns))
+    del Wg, mel, out, scratch
+    torch.cuda.empty_cache()
+    return [{"workload": f"configs[2] Whisper small.en whole encoder (convolutions, {L} blocks, ln_post), {B} "
+                         "windows: f16 tcgen05 GEMMs + bf16 attention",
+             "metric": "whisper_small_en_encoder_windows_per_s", "value": B / t, "unit": "windows/s",
+             "ms_per_step": t * 1e3,
+             "roofline": {"bound": "tensor", "achieved": flops / t / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
+                          "frac": flops / t / 1e12 / tc_peak, "peak_source": f"{peak_kind} bf16 (burst); f16 "
+                          "runs at the bf16 rate", "traffic": None, "flops_per_step": flops}}]
+
+
 def secondary_q8(dev, hbm_peak, steps=20, warmup=3):
     """Q8 projections of one decode step at one GPU (the "next" row around the attention):
     every Qwen2.5-1.5B linear of all 28 layers for one sequence (q, k, v, o, gate, up, down:
@@ -693,7 +726,8 @@ def run_ours(args, rank, world, local):
     cpu = None
     if world == 1 and not args.no_secondary:
         secondary = (secondary_decode(dev, hbm_peak) + secondary_prefill(dev, tc_peak, peak_kind) +
-                     secondary_q8(dev, hbm_peak) + secondary_step(dev, hbm_peak))
+                     secondary_encoder(dev, tc_peak, peak_kind) + secondary_q8(dev, hbm_peak) +
+                     secondary_step(dev, hbm_peak))
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_windows_per_s(min_seconds=args.cpu_seconds)
 

@@ -395,6 +395,68 @@ ZWG_API size_t zwg_dec_scratch_bytes(const zwg_dec_state* st, size_t n);
 ZWG_API int zwg_dec_forward_q8(zwg_dec_state* st, const zwg_dec_weights* w, const int32_t* tokens, size_t n_past,
                                size_t n, float* x, float* logits, void* scratch, size_t scratch_bytes, void* stream);
 
+/* ---- Whisper encoder on the device (src/encoder.zig:118-179) ----------------------------
+ * f16 weights as in the model file (exact in f16); every product on tcgen05 tensor cores with
+ * f16 operands (activations rounded to f16) and f32 accumulation; attention on the bf16
+ * kernel of zwg_enc_attn_bf16; LayerNorm, biases, GELU, residual adds and the positional
+ * embedding in f32. Weight matrices are f16 [n_out][n_in] row-major (the file's layout);
+ * vectors f32; all device pointers, 16-byte aligned. */
+typedef struct zwg_enc_layer_weights {
+    const float* attn_ln_w;
+    const float* attn_ln_b;
+    const uint16_t* w_qkv;      /* [3 n_state][n_state]: query, key and value rows stacked */
+    const float* b_qkv;         /* [3 n_state]: query bias, zeros (the key has none), value bias */
+    const uint16_t* w_o;        /* [n_state][n_state] */
+    const float* b_o;
+    const float* mlp_ln_w;
+    const float* mlp_ln_b;
+    const uint16_t* w_mlp0;     /* [4 n_state][n_state] */
+    const float* b_mlp0;
+    const uint16_t* w_mlp2;     /* [n_state][4 n_state] */
+    const float* b_mlp2;
+} zwg_enc_layer_weights;
+
+/* The encoder's weights (Encoder, src/encoder.zig:12-40). The convolution weights are
+ * stored tap-major: row n of conv1_w is [3][n_mels] (taps k = 0, 1, 2 of every mel channel,
+ * the file's [n_mels][3] transposed), row n of conv2_w is [3][n_state]. pos [n_ctx][n_state];
+ * `layers` a HOST array of n_layer entries. n_state a multiple of 128 (at most 1024) with
+ * n_head = n_state / 64; n_mels a multiple of 8. */
+typedef struct zwg_enc_weights {
+    size_t n_mels, n_ctx, n_state, n_head, n_layer;
+    const uint16_t* conv1_w;    /* [n_state][3 n_mels] */
+    const float* conv1_b;
+    const uint16_t* conv2_w;    /* [n_state][3 n_state] */
+    const float* conv2_b;
+    const float* pos;
+    const zwg_enc_layer_weights* layers;
+    const float* ln_post_w;
+    const float* ln_post_b;
+} zwg_enc_weights;
+
+/* Scratch bytes zwg_enc_forward_f16 needs for n_windows windows. */
+ZWG_API size_t zwg_enc_scratch_bytes(const zwg_enc_weights* w, size_t n_windows);
+
+/* Encoder.forward (src/encoder.zig:118-179) for n_windows windows of 2 n_ctx mel frames:
+ * mel [n_mels][n_len] f32 (device), window i starting at frame offsets[i] (device int32
+ * array; NULL: i * 2 n_ctx); out [n_windows][n_ctx][n_state] f32 (device), the encoder
+ * output after ln_post. Launches only; the stream orders it. */
+ZWG_API int zwg_enc_forward_f16(const zwg_enc_weights* w, const float* mel, size_t n_len, const int32_t* offsets,
+                                size_t n_windows, float* out, void* scratch, size_t scratch_bytes, void* stream);
+
+/* One f16 GEMM on the tensor cores, the encoder's building block (ops.linear, src/ops.zig:
+ * 243-306, with f16 weights): for b < n_batch, m < M, n < N,
+ *   v = sum_k a[b*a_bs + m*lda + k] * w[n*ldw + k] + bias[n]; gelu: v = gelu_tanh(v);
+ *   addend: v += addend[m*ld_add + n]; accumulate: v += out[...];
+ *   out[b*out_bs + m*ld_out + n] = v as out_type (ZWG_GEMM_F32 / F16 / BF16).
+ * a, w f16; bias, addend f32 or NULL. N a multiple of 32, K, lda, ldw, a_bs multiples of 8;
+ * rows of `a` may overlap (lda < K), which the encoder's convolutions use. */
+#define ZWG_GEMM_F32 0
+#define ZWG_GEMM_F16 1
+#define ZWG_GEMM_BF16 2
+ZWG_API int zwg_gemm_f16(const uint16_t* a, size_t lda, size_t a_bs, const uint16_t* w, size_t ldw, size_t M, size_t N,
+                         size_t K, size_t n_batch, const float* bias, int gelu, const float* addend, size_t ld_add,
+                         int accumulate, void* out, int out_type, size_t ld_out, size_t out_bs, void* stream);
+
 /* Self-test of the timeout path every kernel relies on: launches one bounded device-side
  * wait on a barrier nothing ever completes (a few seconds), then synchronizes. Returns
  * ZWG_TIMEOUT when the wait ran out, was reported through the error word and left the

@@ -89,6 +89,26 @@ class DecWeightsC(ctypes.Structure):
     ]
 
 
+class EncLayerWeightsC(ctypes.Structure):
+    """zwg_enc_layer_weights (encoder.Block, src/encoder.zig:12-30): f16 matrices, f32 vectors."""
+
+    _fields_ = [
+        ("attn_ln_w", c_ptr), ("attn_ln_b", c_ptr), ("w_qkv", c_ptr), ("b_qkv", c_ptr), ("w_o", c_ptr),
+        ("b_o", c_ptr), ("mlp_ln_w", c_ptr), ("mlp_ln_b", c_ptr), ("w_mlp0", c_ptr), ("b_mlp0", c_ptr),
+        ("w_mlp2", c_ptr), ("b_mlp2", c_ptr),
+    ]
+
+
+class EncWeightsC(ctypes.Structure):
+    """zwg_enc_weights (encoder.Encoder's weights, src/encoder.zig:32-40)."""
+
+    _fields_ = [
+        ("n_mels", c_size), ("n_ctx", c_size), ("n_state", c_size), ("n_head", c_size), ("n_layer", c_size),
+        ("conv1_w", c_ptr), ("conv1_b", c_ptr), ("conv2_w", c_ptr), ("conv2_b", c_ptr), ("pos", c_ptr),
+        ("layers", ctypes.POINTER(EncLayerWeightsC)), ("ln_post_w", c_ptr), ("ln_post_b", c_ptr),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/zwgpu.h declares
 SIGNATURES = {
     "zwg_version": (ctypes.c_int, []),
@@ -146,6 +166,12 @@ SIGNATURES = {
     "zwg_linear_q8_gelu": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr, c_size, c_ptr, c_ptr]),
     "zwg_dec_set_audio_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(DecWeightsC), c_size, c_ptr, c_ptr]),
     "zwg_dec_scratch_bytes": (c_size, [c_ptr, c_size]),
+    "zwg_enc_scratch_bytes": (c_size, [ctypes.POINTER(EncWeightsC), c_size]),
+    "zwg_enc_forward_f16": (ctypes.c_int, [ctypes.POINTER(EncWeightsC), c_ptr, c_size, c_ptr, c_size, c_ptr, c_ptr,
+                                           c_size, c_ptr]),
+    "zwg_gemm_f16": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_size, c_size, c_size, c_size, c_size, c_ptr,
+                                    ctypes.c_int, c_ptr, c_size, ctypes.c_int, c_ptr, ctypes.c_int, c_size, c_size,
+                                    c_ptr]),
     "zwg_dec_forward_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(DecWeightsC), c_ptr, c_size, c_size, c_ptr, c_ptr,
                                           c_ptr, c_size, c_ptr]),
 }

@@ -37,6 +37,7 @@
 // start later see the error word and exit at once.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <mutex>
@@ -126,9 +127,11 @@ __device__ __forceinline__ void decode_item(int item, int n_pairs, int n_head, i
     win = item / (n_pairs * n_head);
 }
 
+// OUT_F16: the output is f16 (the operand of the output projection) instead of f32.
+template <bool OUT_F16>
 __global__ void __launch_bounds__(THREADS, 1)
     enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, float* __restrict__ out, int n_ctx, int n_head,
+                       const __grid_constant__ CUtensorMap tm_v, void* __restrict__ out, int n_ctx, int n_head,
                        int n_items, int* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -371,18 +374,34 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const float inv = l > 0.f ? 1.0f / l : 0.f;
             const int grow = pair * 2 * BM + t * BM + row;
-            float* orow = out + ((size_t)win * n_ctx + grow) * (size_t)(n_head * D) + head * D;
+            const size_t oidx = ((size_t)win * n_ctx + grow) * (size_t)(n_head * D) + head * D;
 #pragma unroll
             for (int cc = 0; cc < D / 32; cc++) {
                 uint32_t o[32];
                 tmem_ld32(o_addr + cc * 32, o);
                 tmem_ld_wait();
                 if (grow < n_ctx) {
+                    if (OUT_F16) {
+                        uint4* orow = reinterpret_cast<uint4*>(static_cast<__half*>(out) + oidx + cc * 32);
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 v4 = make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                                                __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-                        *reinterpret_cast<float4*>(orow + cc * 32 + i) = v4;
+                        for (int i = 0; i < 32; i += 8) {
+                            uint32_t h[4];
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                __half2 p2 = __floats2half2_rn(__uint_as_float(o[i + 2 * u]) * inv,
+                                                               __uint_as_float(o[i + 2 * u + 1]) * inv);
+                                h[u] = *reinterpret_cast<uint32_t*>(&p2);
+                            }
+                            orow[i / 8] = make_uint4(h[0], h[1], h[2], h[3]);
+                        }
+                    } else {
+                        float* orow = static_cast<float*>(out) + oidx + cc * 32;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            float4 v4 = make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                                    __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+                            *reinterpret_cast<float4*>(orow + i) = v4;
+                        }
                     }
                 }
             }
@@ -403,13 +422,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---- host side -----------------------------------------------------------------------------
 
-// 3-d map over a bf16 [n_batch][n_ctx][n_head*64] tensor with [1][128][64] boxes.
-static bool make_map(CUtensorMap* map, const void* base, int n_batch, int n_ctx, int n_head) {
+// 3-d map over a bf16 [n_batch][n_ctx][n_head*64] tensor whose rows are ld elements apart,
+// with [1][128][64] boxes.
+static bool make_map(CUtensorMap* map, const void* base, int n_batch, int n_ctx, int n_head, size_t ld) {
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return false;
     const cuuint64_t row = (cuuint64_t)n_head * 64;
     cuuint64_t dims[3] = {row, (cuuint64_t)n_ctx, (cuuint64_t)n_batch};
-    cuuint64_t strides[2] = {row * 2, row * 2 * (cuuint64_t)n_ctx};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)ld * 2 * (cuuint64_t)n_ctx};
     cuuint32_t box[3] = {64, 128, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
@@ -420,22 +440,24 @@ static bool make_map(CUtensorMap* map, const void* base, int n_batch, int n_ctx,
 
 int enc_tc_launch(const EncTcParams& p, cudaStream_t st) {
     using namespace enc_tc;
+    const size_t ld = p.ld_qkv ? p.ld_qkv : (size_t)p.n_head * 64;
+    if (ld < (size_t)p.n_head * 64 || ld % 8) return -1;
     CUtensorMap mq, mk, mv;
-    if (!make_map(&mq, p.q, p.n_batch, p.n_ctx, p.n_head) || !make_map(&mk, p.k, p.n_batch, p.n_ctx, p.n_head) ||
-        !make_map(&mv, p.v, p.n_batch, p.n_ctx, p.n_head))
+    if (!make_map(&mq, p.q, p.n_batch, p.n_ctx, p.n_head, ld) || !make_map(&mk, p.k, p.n_batch, p.n_ctx, p.n_head, ld) ||
+        !make_map(&mv, p.v, p.n_batch, p.n_ctx, p.n_head, ld))
         return -1;
     // the shared-memory opt-in is a per-device function attribute
     static std::mutex mu;
-    static bool attr_set[64] = {};
+    static bool attr_set[64][2] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    auto kern = p.out_f16 ? enc_attn_tc_kernel<true> : enc_attn_tc_kernel<false>;
     {
         std::lock_guard<std::mutex> lk(mu);
-        if (!attr_set[dev]) {
-            if (cudaFuncSetAttribute(enc_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)SMEM_BYTES) != cudaSuccess)
+        if (!attr_set[dev][p.out_f16 ? 1 : 0]) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
                 return -1;
-            attr_set[dev] = true;
+            attr_set[dev][p.out_f16 ? 1 : 0] = true;
         }
     }
     static int sm_count[64] = {};
@@ -444,8 +466,7 @@ int enc_tc_launch(const EncTcParams& p, cudaStream_t st) {
     const long long n_items = (long long)p.n_batch * p.n_head * ((n_tiles + 1) / 2);
     if (n_items > (1ll << 30)) return -1;
     const int grid = (int)std::min<long long>(n_items, sm_count[dev] > 0 ? sm_count[dev] : 148);
-    enc_attn_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mk, mv, p.out, p.n_ctx, p.n_head, (int)n_items,
-                                                          p.err);
+    kern<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mk, mv, p.out, p.n_ctx, p.n_head, (int)n_items, p.err);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

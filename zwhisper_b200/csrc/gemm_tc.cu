@@ -1,0 +1,329 @@
+// The Whisper encoder's dense products as f16 GEMMs on the 5th-generation tensor cores
+// (sm_100a): the conv front-end (src/encoder.zig:125-150, each kernel-3 convolution as one
+// product over three consecutive input rows), the q/k/v and output projections and the MLP
+// (src/encoder.zig:152-176; ops.linear, src/ops.zig:243-306).
+//
+//   D[b][m][n] = epilogue( sum_k A[b][m][k] * W[n][k] )
+//
+// A: f16 activations [batch][M][K] (row m of batch b at A + b * a_bs + m * lda); W: f16
+// weights [N][K] row-major, the layout of the model file's linear weights; both K-major,
+// read by TMA in [rows][64] boxes with the 128-byte swizzle. The reference widens its f16
+// weights to f32 and multiplies in f32; here the weights enter the tensor cores exactly and
+// the activations are rounded to f16 (11 significant bits), with f32 accumulation.
+//
+// Persistent kernel, one CTA per SM, tiles of 128 x 256 dealt round-robin (n fastest, so CTAs
+// running together share their A rows through L2):
+//   warp 0     TMA producer: A [128][64] and W [256][64] boxes into a 4-stage ring.
+//   warp 1     allocates 512 TMEM columns (two accumulators of 256); lane 0 issues
+//              tcgen05.mma kind::f16 (M 128, N 256, K 16; both operands from shared memory)
+//              into the accumulator of the tile, alternating between the two, so the
+//              epilogue of one tile overlaps the products of the next.
+//   warps 2-5  epilogue, one thread per row (TMEM lane = row): 32 columns at a time from
+//              TMEM, + bias, optional tanh GELU, optional addend (the positional embedding),
+//              optional accumulation into the f32 output (the residual stream), stored as
+//              f32, f16 or bf16. Rows past M (per batch) and columns past N are not stored.
+// Every mbarrier wait is bounded; on a timeout the error word is set and the CTA tears down
+// after draining the copies and products it issued.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+#include "tmap.cuh"
+
+namespace zwg {
+
+using namespace sm100;
+
+namespace gemm_tc {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;        // 64 f16 = one 128-byte swizzled row
+constexpr int NS = 4;         // pipeline stages
+constexpr int THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr uint32_t A_BYTES = BM * BK * 2;
+constexpr uint32_t B_BYTES = BN * BK * 2;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+
+struct Smem {
+    uint8_t a[NS][A_BYTES];  // 1024-byte aligned stages
+    uint8_t b[NS][B_BYTES];
+    uint64_t full[NS], empty[NS];
+    uint64_t acc_full[2], acc_empty[2];
+    uint64_t mma_done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+
+struct Geo {
+    int M, N, K, n_batch;
+    int m_tiles, n_tiles, k_steps;
+    long long total;
+};
+
+__device__ __forceinline__ void tile_of(long long t, const Geo& g, int& b, int& m0, int& n0) {
+    const long long mt = t / g.n_tiles;
+    n0 = (int)(t - mt * g.n_tiles) * BN;
+    b = (int)(mt / g.m_tiles);
+    m0 = (int)(mt - (long long)b * g.m_tiles) * BM;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float u = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(u)));
+}
+
+template <int OUT, bool GELU, bool ACC>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w, Geo geo,
+                    GemmEpilogue e, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) sm.abort_flag = err ? *(volatile int*)err : 0;
+    __syncthreads();
+    if (sm.abort_flag) return;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; s++) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&sm.acc_full[b], 1);
+            mbar_init(&sm.acc_empty[b], 128);
+        }
+        mbar_init(&sm.mma_done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&sm.tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            prefetch_tmap(&tm_a);
+            prefetch_tmap(&tm_w);
+            uint32_t g = 0;
+            bool ok = true;
+            for (long long t = blockIdx.x; ok && t < geo.total; t += gridDim.x) {
+                int b, m0, n0;
+                tile_of(t, geo, b, m0, n0);
+                for (int ks = 0; ks < geo.k_steps; ks++, g++) {
+                    const uint32_t s = g % NS;
+                    if (g >= NS && !(ok = mbar_wait(&sm.empty[s], ((g / NS) - 1) & 1, err))) break;
+                    mbar_arrive_expect_tx(&sm.full[s], A_BYTES + B_BYTES);
+                    tma_load_3d(&tm_a, &sm.full[s], sm.a[s], ks * BK, m0, b);
+                    tma_load_3d(&tm_w, &sm.full[s], sm.b[s], ks * BK, n0, 0);
+                }
+            }
+            // no copy may be in flight when the CTA exits: wait for the last load of each stage
+            for (uint32_t s = 0; s < NS && s < g; s++) mbar_wait_drain(&sm.full[s], ((g - 1 - s) / NS) & 1);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(BM, BN, false, false, false);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true, issued = false;
+            for (long long t = blockIdx.x; ok && t < geo.total; t += gridDim.x, it++) {
+                const int buf = it & 1;
+                if (it >= 2 && !(ok = mbar_wait(&sm.acc_empty[buf], ((it >> 1) - 1) & 1, err))) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * BN;
+                for (int ks = 0; ks < geo.k_steps; ks++, g++) {
+                    const uint32_t s = g % NS;
+                    if (!(ok = mbar_wait(&sm.full[s], (g / NS) & 1, err))) break;
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sm.a[s]), b_addr = smem_u32(sm.b[s]);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; kk++) {
+                        const uint64_t ad = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+                        mma_f16_ss(d, ad, bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    issued = true;
+                    mma_commit(&sm.empty[s]);
+                }
+                if (ok) mma_commit(&sm.acc_full[buf]);
+            }
+            // every product this thread issued has completed before the CTA tears down
+            if (issued) {
+                mma_commit(&sm.mma_done);
+                mbar_wait_drain(&sm.mma_done, 0);
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int quarter = warp & 3;               // TMEM lanes this warp may access
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        int it = 0;
+        for (long long t = blockIdx.x; t < geo.total; t += gridDim.x, it++) {
+            const int buf = it & 1;
+            if (!mbar_wait_warp(&sm.acc_full[buf], (it >> 1) & 1, err)) break;
+            tc_fence_after();
+            int b, m0, n0;
+            tile_of(t, geo, b, m0, n0);
+            const int m = m0 + row;
+            const bool valid = m < geo.M;
+            const size_t orow = (size_t)b * e.out_bs + (size_t)(valid ? m : 0) * e.ld_out;
+            for (int c = 0; c < BN / 32; c++) {
+                const int n = n0 + c * 32;
+                if (n >= geo.N) break;  // uniform over the CTA
+                uint32_t r[32];
+                tmem_ld32(tmem + lane_addr + buf * BN + c * 32, r);
+                tmem_ld_wait();
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (e.bias) bb = __ldg(reinterpret_cast<const float4*>(e.bias + n + i));
+                    v[i] = __fadd_rn(__uint_as_float(r[i]), bb.x);
+                    v[i + 1] = __fadd_rn(__uint_as_float(r[i + 1]), bb.y);
+                    v[i + 2] = __fadd_rn(__uint_as_float(r[i + 2]), bb.z);
+                    v[i + 3] = __fadd_rn(__uint_as_float(r[i + 3]), bb.w);
+                }
+                if (GELU) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = gelu_tanh(v[i]);
+                }
+                if (!valid) continue;
+                if (e.addend) {
+                    const float* ad = e.addend + (size_t)m * e.ld_add + n;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 a4 = __ldg(reinterpret_cast<const float4*>(ad + i));
+                        v[i] = __fadd_rn(v[i], a4.x);
+                        v[i + 1] = __fadd_rn(v[i + 1], a4.y);
+                        v[i + 2] = __fadd_rn(v[i + 2], a4.z);
+                        v[i + 3] = __fadd_rn(v[i + 3], a4.w);
+                    }
+                }
+                if (OUT == GEMM_OUT_F32) {
+                    float* o = static_cast<float*>(e.out) + orow + n;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 w4 = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                        if (ACC) {
+                            const float4 x4 = *reinterpret_cast<const float4*>(o + i);
+                            w4 = make_float4(__fadd_rn(x4.x, w4.x), __fadd_rn(x4.y, w4.y), __fadd_rn(x4.z, w4.z),
+                                             __fadd_rn(x4.w, w4.w));
+                        }
+                        *reinterpret_cast<float4*>(o + i) = w4;
+                    }
+                } else {
+                    uint32_t h[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        if (OUT == GEMM_OUT_F16) {
+                            __half2 p = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                            h[i] = *reinterpret_cast<uint32_t*>(&p);
+                        } else {
+                            __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                            h[i] = *reinterpret_cast<uint32_t*>(&p);
+                        }
+                    }
+                    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + orow + n);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) o[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+                }
+            }
+            // the accumulator is in registers or stored: the next tile may overwrite it
+            tc_fence_before();
+            mbar_arrive(&sm.acc_empty[buf]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// 3-d map over f16 [dim2][dim1][dim0] with row stride ld and plane stride ps (elements) and
+// [1][rows][64] boxes in the 128-byte swizzle; reads outside the extents fill zeros.
+static bool make_map(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint64_t ld,
+                     uint64_t ps, uint32_t rows) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {dim0, dim1, dim2};
+    cuuint64_t strides[2] = {ld * 2, ps * 2};
+    cuuint32_t box[3] = {64, rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace gemm_tc
+
+bool gemm_f16_supported(const GemmParams& p) {
+    const uintptr_t base = (uintptr_t)p.a | (uintptr_t)p.w;
+    if (base & 15) return false;
+    if (!p.e.out || ((uintptr_t)p.e.out & 15)) return false;
+    if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.n_batch <= 0) return false;
+    if (p.N % 32 || p.K % 8 || p.lda % 8 || p.a_bs % 8 || p.ldw % 8) return false;
+    if (p.ldw < (size_t)p.K) return false;  // rows of a may overlap (the convolutions' views)
+    // 16-byte aligned output rows and chunks; f32 accumulation only into f32 outputs
+    const size_t esz = p.out_type == GEMM_OUT_F32 ? 4 : 2;
+    if ((p.e.ld_out * esz) % 16 || (p.e.out_bs * esz) % 16) return false;
+    if (p.accumulate && p.out_type != GEMM_OUT_F32) return false;
+    if (p.e.bias && ((uintptr_t)p.e.bias & 15)) return false;
+    if (p.e.addend && (((uintptr_t)p.e.addend & 15) || p.e.ld_add % 4)) return false;
+    if (p.out_type < GEMM_OUT_F32 || p.out_type > GEMM_OUT_BF16) return false;
+    return true;
+}
+
+int gemm_f16_launch(const GemmParams& p, int sm_count, int* err, cudaStream_t st) {
+    using namespace gemm_tc;
+    if (!gemm_f16_supported(p)) return -1;
+    CUtensorMap ma, mw;
+    if (!make_map(&ma, p.a, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.n_batch, p.lda, p.a_bs ? p.a_bs : p.lda * p.M,
+                  BM) ||
+        !make_map(&mw, p.w, (uint64_t)p.K, (uint64_t)p.N, 1, p.ldw, p.ldw * (uint64_t)p.N, BN))
+        return -1;
+    Geo g;
+    g.M = p.M;
+    g.N = p.N;
+    g.K = p.K;
+    g.n_batch = p.n_batch;
+    g.m_tiles = (p.M + BM - 1) / BM;
+    g.n_tiles = (p.N + BN - 1) / BN;
+    g.k_steps = (p.K + BK - 1) / BK;
+    g.total = (long long)g.m_tiles * g.n_batch * g.n_tiles;
+    const int grid = (int)std::min<long long>(g.total, std::max(1, sm_count));
+    auto go = [&](auto kern) -> int {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
+            return -1;
+        kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mw, g, p.e, err);
+        return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+    };
+    if (p.out_type == GEMM_OUT_F32) {
+        if (p.accumulate) return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F32, true, true>) : go(gemm_f16_kernel<GEMM_OUT_F32, false, true>);
+        return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F32, true, false>) : go(gemm_f16_kernel<GEMM_OUT_F32, false, false>);
+    }
+    if (p.out_type == GEMM_OUT_F16)
+        return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F16, true, false>) : go(gemm_f16_kernel<GEMM_OUT_F16, false, false>);
+    return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_BF16, true, false>) : go(gemm_f16_kernel<GEMM_OUT_BF16, false, false>);
+}
+
+}  // namespace zwg

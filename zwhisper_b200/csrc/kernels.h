@@ -73,8 +73,49 @@ struct EncTcParams {
     float* out;
     int n_batch, n_ctx, n_head;
     int* err;  // device error word
+    // Row stride of q, k and v in elements (0: n_head * 64, dense rows); a fused q|k|v
+    // projection output passes 3 * n_state.
+    size_t ld_qkv;
+    // Non-zero: out is f16 [n_batch][n_ctx][n_head * 64] (the next projection's operand)
+    // instead of f32.
+    int out_f16;
 };
 int enc_tc_launch(const EncTcParams& p, cudaStream_t st);
+
+// ---- f16 GEMM on tcgen05 (gemm_tc.cu): the encoder's projections and convolutions --------
+enum { GEMM_OUT_F32 = 0, GEMM_OUT_F16 = 1, GEMM_OUT_BF16 = 2 };
+struct GemmEpilogue {
+    const float* bias;    // [N], or nullptr
+    const float* addend;  // [M][ld_add] f32 added after the activation (the same for every
+                          // batch: the positional embedding), or nullptr
+    size_t ld_add;
+    void* out;            // [batch][M][N] at ld_out per row, out_bs per batch (elements)
+    size_t ld_out, out_bs;
+};
+struct GemmParams {
+    const uint16_t* a;    // f16 [batch][M][K]: row m of batch b at a + b * a_bs + m * lda
+    size_t lda, a_bs;     // a_bs 0: lda * M
+    const uint16_t* w;    // f16 [N][K], row stride ldw
+    size_t ldw;
+    int M, N, K, n_batch;
+    int out_type;         // GEMM_OUT_*
+    bool gelu;            // tanh GELU after the bias
+    bool accumulate;      // out (f32) += result
+    GemmEpilogue e;
+};
+bool gemm_f16_supported(const GemmParams& p);
+int gemm_f16_launch(const GemmParams& p, int sm_count, int* err, cudaStream_t st);
+
+// ---- encoder helpers (enc_aux.cu) -----------------------------------------------------------
+// LayerNorm of n_rows rows of n f32 (n a multiple of 128, at most 1024), one warp per row;
+// out f16 (out_f16) or f32, which may be x itself.
+int layer_norm_rows_launch(const float* x, size_t n_rows, int n, const float* w, const float* b, float eps, void* out,
+                           bool out_f16, cudaStream_t st);
+// Mel frames of each window as f16 rows: rows[b][1 + t][c] = mel[c][off_b + t] for t < n_frames
+// (zero past n_len), rows[b][0] and rows[b][n_frames + 1] zero; off_b = offsets[b], or
+// b * n_frames when offsets is null.
+int mel_rows_launch(const float* mel, int n_mels, size_t n_len, const int* offsets, int n_batch, int n_frames,
+                    uint16_t* rows, cudaStream_t st);
 
 // Prefill over a transposed key cache on tcgen05 tensor cores, kind::tf32
 // (attn_prefill_tc.cu): d 64 or 128, group <= 128, TMA-aligned buffers and strides.

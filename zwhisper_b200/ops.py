@@ -808,3 +808,128 @@ class DecoderWeightsQ8:
             self._c = _lib.DecWeightsC(self.n_vocab, m(self.te), self.pe.data_ptr(), self.ln_w.data_ptr(),
                                        self.ln_b.data_ptr(), ctypes.cast(arr, ctypes.POINTER(_lib.DecLayerWeightsC)))
         return self._c
+
+
+# ---- Whisper encoder on the device (src/encoder.zig:118-179) -------------------------------
+
+_GEMM_OUT = {"f32": 0, "f16": 1, "bf16": 2}
+
+
+def gemm_f16(a, w, bias=None, gelu: bool = False, addend=None, accumulate: bool = False, out=None,
+             out_dtype: str = "f32", M: int = None, K: int = None, lda: int = None, a_bs: int = None):
+    """One f16 GEMM on the tensor cores (zwg_gemm_f16): out[b][m][n] = act(a[b][m] . w[n] +
+    bias[n]) (+ addend[m][n]) (+ out when accumulate). a f16 [B][M][K] (or a strided view of
+    rows given by M, K, lda, a_bs over a flat f16 buffer), w f16 [N][K]; out [B][M][N]."""
+    torch = _torch()
+    if a.dtype != torch.float16 or w.dtype != torch.float16:
+        raise ValueError("a and w must be f16")
+    N, Kw = w.shape
+    if M is None:
+        if a.dim() == 2:
+            a = a.unsqueeze(0)
+        B, M, K = a.shape
+        lda, a_bs = K, M * K
+    else:
+        B = a.numel() // a_bs if a_bs else 1
+        K = Kw if K is None else K
+    dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[out_dtype]
+    if out is None:
+        out = torch.zeros(B, M, N, dtype=dt, device=a.device)
+    _lib.ensure_init(a.device.index or 0)
+    lib = _lib.load()
+    rc = lib.zwg_gemm_f16(a.data_ptr(), lda, a_bs or 0, w.data_ptr(), Kw, M, N, K, B,
+                          bias.data_ptr() if bias is not None else 0, 1 if gelu else 0,
+                          addend.data_ptr() if addend is not None else 0, N if addend is not None else 0,
+                          1 if accumulate else 0, out.data_ptr(), _GEMM_OUT[out_dtype], N, M * N, _stream_of(a))
+    _lib.check(rc)
+    return out
+
+
+class EncoderWeightsF16:
+    """The Whisper encoder's weights on the device (encoder.Encoder, src/encoder.zig:12-40)
+    and the zwg_enc_weights struct that points at them. `tensors` maps the model file's names
+    (encoder.conv1.weight [n_state][n_mels][3], encoder.positional_embedding,
+    encoder.blocks.{i}.attn.query.weight, ...) to numpy or torch arrays. Matrices stay f16 (the
+    file's values, exact); the convolution weights are stored tap-major ([n_out][3][n_in]) and
+    the query/key/value rows stacked into one [3 n_state][n_state] matrix with the key's
+    missing bias as zeros."""
+
+    def __init__(self, tensors, n_layer: int, n_head: int, device: int = 0):
+        torch = _torch()
+        dev = torch.device("cuda", device)
+        _lib.ensure_init(device)
+
+        def t(name):
+            a = tensors[name]
+            if not isinstance(a, torch.Tensor):
+                a = torch.from_numpy(np.ascontiguousarray(a))
+            return a.to(device=dev)
+
+        def f32(name):
+            return t(name).to(torch.float32).contiguous()
+
+        def f16(name):
+            return t(name).to(torch.float16).contiguous()
+
+        c1 = f16("encoder.conv1.weight")  # [n_state][n_mels][3]
+        c2 = f16("encoder.conv2.weight")  # [n_state][n_state][3]
+        self.n_state, self.n_mels = c1.shape[0], c1.shape[1]
+        self.n_head, self.n_layer = n_head, n_layer
+        self.conv1_w = c1.permute(0, 2, 1).contiguous().view(self.n_state, -1)
+        self.conv2_w = c2.permute(0, 2, 1).contiguous().view(self.n_state, -1)
+        self.conv1_b, self.conv2_b = f32("encoder.conv1.bias"), f32("encoder.conv2.bias")
+        self.pos = f32("encoder.positional_embedding")
+        self.n_ctx = self.pos.shape[0]
+        self.ln_post_w, self.ln_post_b = f32("encoder.ln_post.weight"), f32("encoder.ln_post.bias")
+        self.layers = []
+        for i in range(n_layer):
+            p = f"encoder.blocks.{i}."
+            zeros = torch.zeros(self.n_state, dtype=torch.float32, device=dev)
+            self.layers.append({
+                "attn_ln_w": f32(p + "attn_ln.weight"), "attn_ln_b": f32(p + "attn_ln.bias"),
+                "w_qkv": torch.cat([f16(p + "attn.query.weight"), f16(p + "attn.key.weight"),
+                                    f16(p + "attn.value.weight")]).contiguous(),
+                "b_qkv": torch.cat([f32(p + "attn.query.bias"), zeros, f32(p + "attn.value.bias")]).contiguous(),
+                "w_o": f16(p + "attn.out.weight"), "b_o": f32(p + "attn.out.bias"),
+                "mlp_ln_w": f32(p + "mlp_ln.weight"), "mlp_ln_b": f32(p + "mlp_ln.bias"),
+                "w_mlp0": f16(p + "mlp.0.weight"), "b_mlp0": f32(p + "mlp.0.bias"),
+                "w_mlp2": f16(p + "mlp.2.weight"), "b_mlp2": f32(p + "mlp.2.bias"),
+            })
+        self._c = None
+
+    FIELDS = ("attn_ln_w", "attn_ln_b", "w_qkv", "b_qkv", "w_o", "b_o", "mlp_ln_w", "mlp_ln_b", "w_mlp0", "b_mlp0",
+              "w_mlp2", "b_mlp2")
+
+    def c_struct(self) -> _lib.EncWeightsC:
+        if self._c is None:
+            arr = (_lib.EncLayerWeightsC * len(self.layers))(*[
+                _lib.EncLayerWeightsC(*[L[f].data_ptr() for f in self.FIELDS]) for L in self.layers])
+            self._arr = arr  # keeps the host array alive as long as the struct
+            self._c = _lib.EncWeightsC(self.n_mels, self.n_ctx, self.n_state, self.n_head, self.n_layer,
+                                       self.conv1_w.data_ptr(), self.conv1_b.data_ptr(), self.conv2_w.data_ptr(),
+                                       self.conv2_b.data_ptr(), self.pos.data_ptr(),
+                                       ctypes.cast(arr, ctypes.POINTER(_lib.EncLayerWeightsC)),
+                                       self.ln_post_w.data_ptr(), self.ln_post_b.data_ptr())
+        return self._c
+
+    def scratch_bytes(self, n_windows: int) -> int:
+        return int(_lib.load().zwg_enc_scratch_bytes(ctypes.byref(self.c_struct()), n_windows))
+
+
+def encoder_forward(weights: EncoderWeightsF16, mel, n_windows: int, offsets=None, out=None, scratch=None):
+    """Encoder.forward (src/encoder.zig:118-179) for n_windows windows of the device mel
+    [n_mels][n_len] f32 (zwg_enc_forward_f16): window i starts at frame offsets[i] (a CUDA int32
+    tensor) or i * 2 n_ctx. Returns out [n_windows][n_ctx][n_state] f32."""
+    torch = _torch()
+    _dev_ptr(mel, torch.float32, "mel")
+    n_len = mel.shape[1]
+    if out is None:
+        out = torch.empty(n_windows, weights.n_ctx, weights.n_state, dtype=torch.float32, device=mel.device)
+    need = weights.scratch_bytes(n_windows)
+    if scratch is None:
+        scratch = torch.empty(max(need, 256), dtype=torch.uint8, device=mel.device)
+    off = _dev_ptr(offsets, torch.int32, "offsets") if offsets is not None else 0
+    rc = _lib.load().zwg_enc_forward_f16(ctypes.byref(weights.c_struct()), mel.data_ptr(), n_len, off, n_windows,
+                                         out.data_ptr(), scratch.data_ptr(), scratch.numel(), _stream_of(mel))
+    _lib.check(rc)
+    return out
