@@ -433,6 +433,17 @@ typedef struct zwg_enc_weights {
     const float* ln_post_b;
 } zwg_enc_weights;
 
+/* mel.logMel (src/mel.zig:103-157) on the device: samples [n_samples] f32 (16 kHz), filters
+ * [n_mel][201] f32 (the model file's mel filters), out [n_mel][zwg_mel_frames(n_samples)]
+ * f32: 200 samples reflected at the front, 30 s of zeros appended, 400-sample Hann frames
+ * every 160 samples, DFT power, mel sums in f64, log10 with a 1e-10 floor, clamp to max - 8,
+ * (x + 4) / 4. The DFT sums run in f32 in another order than the reference's radix-2 FFT, so
+ * values agree to f32 rounding. scratch: zwg_mel_scratch_bytes() bytes of device memory. */
+ZWG_API size_t zwg_mel_frames(size_t n_samples);
+ZWG_API size_t zwg_mel_scratch_bytes(void);
+ZWG_API int zwg_log_mel(const float* samples, size_t n_samples, const float* filters, size_t n_mel, float* out,
+                        void* scratch, size_t scratch_bytes, void* stream);
+
 /* Scratch bytes zwg_enc_forward_f16 needs for n_windows windows. */
 ZWG_API size_t zwg_enc_scratch_bytes(const zwg_enc_weights* w, size_t n_windows);
 

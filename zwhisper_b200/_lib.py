@@ -167,6 +167,9 @@ SIGNATURES = {
     "zwg_dec_set_audio_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(DecWeightsC), c_size, c_ptr, c_ptr]),
     "zwg_dec_scratch_bytes": (c_size, [c_ptr, c_size]),
     "zwg_enc_scratch_bytes": (c_size, [ctypes.POINTER(EncWeightsC), c_size]),
+    "zwg_mel_frames": (c_size, [c_size]),
+    "zwg_mel_scratch_bytes": (c_size, []),
+    "zwg_log_mel": (ctypes.c_int, [c_ptr, c_size, c_ptr, c_size, c_ptr, c_ptr, c_size, c_ptr]),
     "zwg_enc_forward_f16": (ctypes.c_int, [ctypes.POINTER(EncWeightsC), c_ptr, c_size, c_ptr, c_size, c_ptr, c_ptr,
                                            c_size, c_ptr]),
     "zwg_gemm_f16": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_size, c_size, c_size, c_size, c_size, c_ptr,

@@ -109,6 +109,24 @@ int run_gemm(Ctx* c, const zwg::GemmParams& p, const char* what, cudaStream_t st
 
 extern "C" {
 
+size_t zwg_mel_frames(size_t n_samples) { return zwg::mel_frames(n_samples); }
+
+size_t zwg_mel_scratch_bytes(void) { return zwg::mel_scratch_bytes(); }
+
+int zwg_log_mel(const float* samples, size_t n_samples, const float* filters, size_t n_mel, float* out, void* scratch,
+                size_t scratch_bytes, void* stream) {
+    Ctx* c = cur();
+    if (!c) return ZWG_ERROR;
+    if (!samples || !filters || !out || !scratch) return fail("log_mel: null pointer");
+    if (n_samples == 0 || n_samples > (size_t)1 << 40) return fail("log_mel: bad sample count %zu", n_samples);
+    if (n_mel == 0 || n_mel > 1024) return fail("log_mel: bad n_mel %zu", n_mel);
+    if (scratch_bytes < zwg::mel_scratch_bytes() || !al16(scratch))
+        return fail("log_mel: scratch must be 16-byte aligned and at least %zu bytes", zwg::mel_scratch_bytes());
+    if (zwg::log_mel_launch(samples, n_samples, filters, (int)n_mel, out, scratch, c->sm_count, (cudaStream_t)stream))
+        return cuda_fail("log_mel launch", cudaGetLastError());
+    return ZWG_OK;
+}
+
 size_t zwg_enc_scratch_bytes(const zwg_enc_weights* w, size_t n_windows) {
     if (!w || !w->n_state || !w->n_ctx) return 0;
     size_t r[4];

@@ -11,19 +11,27 @@
 // weights to f32 and multiplies in f32; here the weights enter the tensor cores exactly and
 // the activations are rounded to f16 (11 significant bits), with f32 accumulation.
 //
-// Persistent kernel, one CTA per SM, tiles of 128 x 256 dealt round-robin (n fastest, so CTAs
-// running together share their A rows through L2):
-//   warp 0     TMA producer: A [128][64] and W [256][64] boxes into a 4-stage ring.
-//   warp 1     allocates 512 TMEM columns (two accumulators of 256); lane 0 issues
-//              tcgen05.mma kind::f16 (M 128, N 256, K 16; both operands from shared memory)
+// Persistent kernel over CTA pairs (clusters of 2, tcgen05 cta_group::2), one CTA per SM:
+// a pair computes a 256 x 256 tile, each CTA holding 128 rows of A and 128 rows of W in its
+// shared memory (32 KB a stage, 6 stages), so a CTA pulls half the W bytes a single-CTA
+// 128 x 256 tile would for the same products. Tiles are dealt round-robin over the pairs (n
+// fastest, so pairs running together share their A rows through L2).
+//   warp 0     TMA producer in both CTAs: its A and W boxes of each 64-wide k step, counted
+//              on the first CTA's full barrier (cta_group::2 loads, no multicast).
+//   warp 1     allocates 512 TMEM columns in both CTAs (two accumulators of 256); lane 0 of
+//              the first CTA issues tcgen05.mma.cta_group::2 kind::f16 (M 256, N 256, K 16)
 //              into the accumulator of the tile, alternating between the two, so the
-//              epilogue of one tile overlaps the products of the next.
-//   warps 2-5  epilogue, one thread per row (TMEM lane = row): 32 columns at a time from
-//              TMEM, + bias, optional tanh GELU, optional addend (the positional embedding),
-//              optional accumulation into the f32 output (the residual stream), stored as
-//              f32, f16 or bf16. Rows past M (per batch) and columns past N are not stored.
-// Every mbarrier wait is bounded; on a timeout the error word is set and the CTA tears down
-// after draining the copies and products it issued.
+//              epilogue of one tile overlaps the products of the next; its commits arrive
+//              in both CTAs.
+//   warps 2-9  epilogue in both CTAs, one thread per row of the CTA's 128 (TMEM lane = row)
+//              and half of the columns: 32 columns at a time from TMEM, + bias, optional
+//              tanh GELU, optional addend (the positional embedding) or accumulation into
+//              the f32 output (the residual stream), loaded a chunk ahead; stored as f32, f16
+//              or bf16. Rows past M (per batch) and columns past N are not stored. Each warp
+//              then releases the accumulator on the first CTA's barrier.
+// Every mbarrier wait is bounded; on a timeout the error word is set and the CTA goes to
+// the teardown: both CTAs meet at a cluster barrier (every path reaches it) after the first
+// CTA has drained its products and copies, then free their TMEM.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -42,14 +50,16 @@ using namespace sm100;
 
 namespace gemm_tc {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 64;        // 64 f16 = one 128-byte swizzled row
-constexpr int NS = 4;         // pipeline stages
-constexpr int THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int BM = 128;        // rows per CTA (M = 256 per pair)
+constexpr int BN = 256;        // columns per pair tile (each CTA loads 128 rows of W)
+constexpr int BK = 64;         // 64 f16 = one 128-byte swizzled row
+constexpr int NS = 6;          // pipeline stages
+constexpr int THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr uint32_t A_BYTES = BM * BK * 2;
-constexpr uint32_t B_BYTES = BN * BK * 2;
+constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
+constexpr uint32_t STAGE_TX = 2 * (A_BYTES + B_BYTES);  // both CTAs' loads, on the first CTA's barrier
 constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t EPI_WARPS = 8;
 
 struct Smem {
     uint8_t a[NS][A_BYTES];  // 1024-byte aligned stages
@@ -64,34 +74,38 @@ constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
 
 struct Geo {
     int M, N, K, n_batch;
-    int m_tiles, n_tiles, k_steps;
+    int m_pairs, n_tiles, k_steps;
     long long total;
 };
 
+// Tile t of the pair grid: batch b, first row of the pair's 256, first column.
 __device__ __forceinline__ void tile_of(long long t, const Geo& g, int& b, int& m0, int& n0) {
     const long long mt = t / g.n_tiles;
     n0 = (int)(t - mt * g.n_tiles) * BN;
-    b = (int)(mt / g.m_tiles);
-    m0 = (int)(mt - (long long)b * g.m_tiles) * BM;
+    b = (int)(mt / g.m_pairs);
+    m0 = (int)(mt - (long long)b * g.m_pairs) * (2 * BM);
 }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
+// ggml's tanh GELU (src/ops.zig:312-327), 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715
+// x^3), evaluated through the identity 1 + tanh(u) = 2 / (1 + exp(-2u)): x / (1 + exp(-2u)),
+// one exponential and one fast division (a few ulp of f32; the result is then rounded to the
+// f16 or bf16 operand of the next product, or added into the f32 stream). Large |u| gives x
+// or 0 exactly.
+__device__ __forceinline__ float gelu_fast(float x) {
     const float u = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x)));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(u)));
+    return __fdividef(x, __fadd_rn(1.0f, __expf(-2.0f * u)));
 }
 
 template <int OUT, bool GELU, bool ACC>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w, Geo geo,
                     GemmEpilogue e, int* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) sm.abort_flag = err ? *(volatile int*)err : 0;
-    __syncthreads();
-    if (sm.abort_flag) return;
+    const uint32_t rank = cluster_ctarank();      // 0: the pair's first CTA (issues the MMAs)
+    const long long pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; s++) {
@@ -100,49 +114,56 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&sm.acc_full[b], 1);
-            mbar_init(&sm.acc_empty[b], 128);
+            mbar_init(&sm.acc_empty[b], 2 * EPI_WARPS);
         }
         mbar_init(&sm.mma_done, 1);
         fence_mbar_init();
+        sm.abort_flag = err ? *(volatile int*)err : 0;
     }
     if (warp == 1) {
-        tmem_alloc(&sm.tmem_base, TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc_pair(&sm.tmem_base, TMEM_COLS);
+        tmem_relinquish_pair();
     }
+    // both CTAs' barriers are initialised and their TMEM allocated before any cross-CTA use
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    const bool run = sm.abort_flag == 0;
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- TMA producer
-        if (lane == 0) {
+        // ---------------------------------------------------------------- TMA producers
+        if (lane == 0 && run) {
             prefetch_tmap(&tm_a);
             prefetch_tmap(&tm_w);
             uint32_t g = 0;
             bool ok = true;
-            for (long long t = blockIdx.x; ok && t < geo.total; t += gridDim.x) {
+            for (long long t = pair; ok && t < geo.total; t += n_pairs) {
                 int b, m0, n0;
                 tile_of(t, geo, b, m0, n0);
                 for (int ks = 0; ks < geo.k_steps; ks++, g++) {
                     const uint32_t s = g % NS;
                     if (g >= NS && !(ok = mbar_wait(&sm.empty[s], ((g / NS) - 1) & 1, err))) break;
-                    mbar_arrive_expect_tx(&sm.full[s], A_BYTES + B_BYTES);
-                    tma_load_3d(&tm_a, &sm.full[s], sm.a[s], ks * BK, m0, b);
-                    tma_load_3d(&tm_w, &sm.full[s], sm.b[s], ks * BK, n0, 0);
+                    const uint32_t fb = mapa_shared(smem_u32(&sm.full[s]), 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], STAGE_TX);
+                    tma_load_3d_pair(&tm_a, fb, sm.a[s], ks * BK, m0 + (int)rank * BM, b);
+                    tma_load_3d_pair(&tm_w, fb, sm.b[s], ks * BK, n0 + (int)rank * (BN / 2), 0);
                 }
             }
-            // no copy may be in flight when the CTA exits: wait for the last load of each stage
-            for (uint32_t s = 0; s < NS && s < g; s++) mbar_wait_drain(&sm.full[s], ((g - 1 - s) / NS) & 1);
+            // every load of both CTAs lands on the first CTA's full barriers: it waits for the
+            // last phase of each stage before the teardown
+            if (rank == 0)
+                for (uint32_t s = 0; s < NS && s < g; s++) mbar_wait_drain(&sm.full[s], ((g - 1 - s) / NS) & 1);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16(BM, BN, false, false, false);
+        if (lane == 0 && rank == 0 && run) {
+            constexpr uint32_t idesc = idesc_f16(2 * BM, BN, false, false, false);
             uint32_t g = 0;
             int it = 0;
-            bool ok = true, issued = false;
-            for (long long t = blockIdx.x; ok && t < geo.total; t += gridDim.x, it++) {
+            bool ok = true;
+            for (long long t = pair; ok && t < geo.total; t += n_pairs, it++) {
                 const int buf = it & 1;
                 if (it >= 2 && !(ok = mbar_wait(&sm.acc_empty[buf], ((it >> 1) - 1) & 1, err))) break;
                 tc_fence_after();
@@ -156,39 +177,56 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int kk = 0; kk < BK / 16; kk++) {
                         const uint64_t ad = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
                         const uint64_t bd = smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-                        mma_f16_ss(d, ad, bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+                        mma_f16_ss_pair(d, ad, bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
                     }
-                    issued = true;
-                    mma_commit(&sm.empty[s]);
+                    mma_commit_pair(&sm.empty[s]);
                 }
-                if (ok) mma_commit(&sm.acc_full[buf]);
+                if (ok) mma_commit_pair(&sm.acc_full[buf]);
             }
-            // every product this thread issued has completed before the CTA tears down
-            if (issued) {
-                mma_commit(&sm.mma_done);
-                mbar_wait_drain(&sm.mma_done, 0);
-            }
+            // every product has completed (and read both CTAs' shared memory) before the
+            // teardown
+            mma_commit_pair(&sm.mma_done);
+            mbar_wait_drain(&sm.mma_done, 0);
         }
-    } else {
+    } else if (run) {
         // ---------------------------------------------------------------- epilogue
+        // warps 2-9: two warps per TMEM lane quarter, each taking one half of the columns
         const int quarter = warp & 3;               // TMEM lanes this warp may access
+        const int half = (warp - 2) >> 2;           // column half of the tile
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        constexpr int CH = BN / 64;                 // 32-column chunks per half
         int it = 0;
-        for (long long t = blockIdx.x; t < geo.total; t += gridDim.x, it++) {
+        for (long long t = pair; t < geo.total; t += n_pairs, it++) {
             const int buf = it & 1;
-            if (!mbar_wait_warp(&sm.acc_full[buf], (it >> 1) & 1, err)) break;
-            tc_fence_after();
             int b, m0, n0;
             tile_of(t, geo, b, m0, n0);
-            const int m = m0 + row;
+            const int m = m0 + (int)rank * BM + row;
             const bool valid = m < geo.M;
             const size_t orow = (size_t)b * e.out_bs + (size_t)(valid ? m : 0) * e.ld_out;
-            for (int c = 0; c < BN / 32; c++) {
-                const int n = n0 + c * 32;
-                if (n >= geo.N) break;  // uniform over the CTA
+            const int nb = n0 + half * (BN / 2);
+            // the f32 values added after the activation (the residual stream or the addend)
+            // are loaded one chunk ahead, the first before the accumulator is ready
+            const float* src = ACC ? static_cast<const float*>(e.out) + orow
+                                   : (e.addend ? e.addend + (size_t)(valid ? m : 0) * e.ld_add : nullptr);
+            const bool has_src = valid && src != nullptr;
+            float4 cur[8], nxt[8];
+            if (has_src && nb < geo.N) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) cur[i] = *reinterpret_cast<const float4*>(src + nb + 4 * i);
+            }
+            if (!mbar_wait_warp(&sm.acc_full[buf], (it >> 1) & 1, err)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < CH; c++) {
+                const int n = nb + c * 32;
+                if (n >= geo.N) break;  // uniform over the warp
+                if (has_src && c + 1 < CH && n + 32 < geo.N) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) nxt[i] = *reinterpret_cast<const float4*>(src + n + 32 + 4 * i);
+                }
                 uint32_t r[32];
-                tmem_ld32(tmem + lane_addr + buf * BN + c * 32, r);
+                tmem_ld32(tmem + lane_addr + buf * BN + half * (BN / 2) + c * 32, r);
                 tmem_ld_wait();
                 float v[32];
 #pragma unroll
@@ -202,60 +240,57 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 if (GELU) {
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = gelu_tanh(v[i]);
+                    for (int i = 0; i < 32; i++) v[i] = gelu_fast(v[i]);
                 }
-                if (!valid) continue;
-                if (e.addend) {
-                    const float* ad = e.addend + (size_t)m * e.ld_add + n;
+                if (valid) {
+                    if (has_src) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        const float4 a4 = __ldg(reinterpret_cast<const float4*>(ad + i));
-                        v[i] = __fadd_rn(v[i], a4.x);
-                        v[i + 1] = __fadd_rn(v[i + 1], a4.y);
-                        v[i + 2] = __fadd_rn(v[i + 2], a4.z);
-                        v[i + 3] = __fadd_rn(v[i + 3], a4.w);
-                    }
-                }
-                if (OUT == GEMM_OUT_F32) {
-                    float* o = static_cast<float*>(e.out) + orow + n;
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 w4 = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                        if (ACC) {
-                            const float4 x4 = *reinterpret_cast<const float4*>(o + i);
-                            w4 = make_float4(__fadd_rn(x4.x, w4.x), __fadd_rn(x4.y, w4.y), __fadd_rn(x4.z, w4.z),
-                                             __fadd_rn(x4.w, w4.w));
-                        }
-                        *reinterpret_cast<float4*>(o + i) = w4;
-                    }
-                } else {
-                    uint32_t h[16];
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        if (OUT == GEMM_OUT_F16) {
-                            __half2 p = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-                            h[i] = *reinterpret_cast<uint32_t*>(&p);
-                        } else {
-                            __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-                            h[i] = *reinterpret_cast<uint32_t*>(&p);
+                        for (int i = 0; i < 8; i++) {
+                            v[4 * i] = __fadd_rn(v[4 * i], cur[i].x);
+                            v[4 * i + 1] = __fadd_rn(v[4 * i + 1], cur[i].y);
+                            v[4 * i + 2] = __fadd_rn(v[4 * i + 2], cur[i].z);
+                            v[4 * i + 3] = __fadd_rn(v[4 * i + 3], cur[i].w);
                         }
                     }
-                    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + orow + n);
+                    if (OUT == GEMM_OUT_F32) {
+                        float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + orow + n);
 #pragma unroll
-                    for (int i = 0; i < 4; i++) o[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+                        for (int i = 0; i < 8; i++) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    } else {
+                        uint32_t h[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            if (OUT == GEMM_OUT_F16) {
+                                __half2 p2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                                h[i] = *reinterpret_cast<uint32_t*>(&p2);
+                            } else {
+                                __nv_bfloat162 p2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                                h[i] = *reinterpret_cast<uint32_t*>(&p2);
+                            }
+                        }
+                        uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + orow + n);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) o[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+                    }
                 }
+#pragma unroll
+                for (int i = 0; i < 8; i++) cur[i] = nxt[i];
             }
             // the accumulator is in registers or stored: the next tile may overwrite it
             tc_fence_before();
-            mbar_arrive(&sm.acc_empty[buf]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&sm.acc_empty[buf]), 0));
         }
     }
 
+    // teardown: the first CTA's products and copies are drained; neither CTA leaves while the
+    // other may still touch its shared memory or TMEM
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc_pair(tmem, TMEM_COLS);
     }
 }
 
@@ -286,7 +321,7 @@ bool gemm_f16_supported(const GemmParams& p) {
     // 16-byte aligned output rows and chunks; f32 accumulation only into f32 outputs
     const size_t esz = p.out_type == GEMM_OUT_F32 ? 4 : 2;
     if ((p.e.ld_out * esz) % 16 || (p.e.out_bs * esz) % 16) return false;
-    if (p.accumulate && p.out_type != GEMM_OUT_F32) return false;
+    if (p.accumulate && (p.out_type != GEMM_OUT_F32 || p.e.addend)) return false;
     if (p.e.bias && ((uintptr_t)p.e.bias & 15)) return false;
     if (p.e.addend && (((uintptr_t)p.e.addend & 15) || p.e.ld_add % 4)) return false;
     if (p.out_type < GEMM_OUT_F32 || p.out_type > GEMM_OUT_BF16) return false;
@@ -299,21 +334,30 @@ int gemm_f16_launch(const GemmParams& p, int sm_count, int* err, cudaStream_t st
     CUtensorMap ma, mw;
     if (!make_map(&ma, p.a, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.n_batch, p.lda, p.a_bs ? p.a_bs : p.lda * p.M,
                   BM) ||
-        !make_map(&mw, p.w, (uint64_t)p.K, (uint64_t)p.N, 1, p.ldw, p.ldw * (uint64_t)p.N, BN))
+        !make_map(&mw, p.w, (uint64_t)p.K, (uint64_t)p.N, 1, p.ldw, p.ldw * (uint64_t)p.N, BN / 2))
         return -1;
     Geo g;
     g.M = p.M;
     g.N = p.N;
     g.K = p.K;
     g.n_batch = p.n_batch;
-    g.m_tiles = (p.M + BM - 1) / BM;
+    g.m_pairs = (p.M + 2 * BM - 1) / (2 * BM);
     g.n_tiles = (p.N + BN - 1) / BN;
     g.k_steps = (p.K + BK - 1) / BK;
-    g.total = (long long)g.m_tiles * g.n_batch * g.n_tiles;
-    const int grid = (int)std::min<long long>(g.total, std::max(1, sm_count));
+    g.total = (long long)g.m_pairs * g.n_batch * g.n_tiles;
     auto go = [&](auto kern) -> int {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
             return -1;
+        // as many pairs as can be resident at once (the SMs of a cluster must share a GPC)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (unsigned)std::max(1, sm_count / 2));
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = SMEM_BYTES;
+        int max_pairs = 0;
+        if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs < 1)
+            max_pairs = std::max(1, sm_count / 2);
+        cudaGetLastError();
+        const int grid = 2 * (int)std::min<long long>(g.total, max_pairs);
         kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mw, g, p.e, err);
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
     };

@@ -114,6 +114,13 @@ int layer_norm_rows_launch(const float* x, size_t n_rows, int n, const float* w,
 // Mel frames of each window as f16 rows: rows[b][1 + t][c] = mel[c][off_b + t] for t < n_frames
 // (zero past n_len), rows[b][0] and rows[b][n_frames + 1] zero; off_b = offsets[b], or
 // b * n_frames when offsets is null.
+// ---- log-mel spectrogram (mel.cu) ----------------------------------------------------------
+// Frames of the spectrogram of n samples (the reference's n_len, 30 s of zero pad included).
+size_t mel_frames(size_t n_samples);
+size_t mel_scratch_bytes();
+// out [n_mel][mel_frames(n)] from samples [n] and filters [n_mel][201] (device pointers).
+int log_mel_launch(const float* samples, size_t n, const float* filters, int n_mel, float* out, void* scratch,
+                   int sm_count, cudaStream_t st);
 int mel_rows_launch(const float* mel, int n_mels, size_t n_len, const int* offsets, int n_batch, int n_frames,
                     uint16_t* rows, cudaStream_t st);
 

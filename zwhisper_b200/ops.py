@@ -933,3 +933,22 @@ def encoder_forward(weights: EncoderWeightsF16, mel, n_windows: int, offsets=Non
                                          out.data_ptr(), scratch.data_ptr(), scratch.numel(), _stream_of(mel))
     _lib.check(rc)
     return out
+
+
+def log_mel(samples, filters, out=None):
+    """mel.logMel (src/mel.zig:103-157) on the device (zwg_log_mel): samples [n] f32 CUDA
+    tensor at 16 kHz, filters [n_mel][201] f32; returns [n_mel][n_len] f32."""
+    torch = _torch()
+    _dev_ptr(samples, torch.float32, "samples")
+    _dev_ptr(filters, torch.float32, "filters")
+    lib = _lib.load()
+    _lib.ensure_init(samples.device.index or 0)
+    n = samples.numel()
+    n_mel = filters.shape[0]
+    n_len = int(lib.zwg_mel_frames(n))
+    if out is None:
+        out = torch.empty(n_mel, n_len, dtype=torch.float32, device=samples.device)
+    scratch = torch.empty(int(lib.zwg_mel_scratch_bytes()), dtype=torch.uint8, device=samples.device)
+    _lib.check(lib.zwg_log_mel(samples.data_ptr(), n, filters.data_ptr(), n_mel, out.data_ptr(), scratch.data_ptr(),
+                               scratch.numel(), _stream_of(samples)))
+    return out
