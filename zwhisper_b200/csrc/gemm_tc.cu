@@ -53,17 +53,18 @@ namespace gemm_tc {
 constexpr int BM = 128;        // rows per CTA (M = 256 per pair)
 constexpr int BN = 256;        // columns per pair tile (each CTA loads 128 rows of W)
 constexpr int BK = 64;         // 64 f16 = one 128-byte swizzled row
-constexpr int NS = 6;          // pipeline stages
+constexpr int NS = 5;          // pipeline stages
 constexpr int THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr uint32_t A_BYTES = BM * BK * 2;
 constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
 constexpr uint32_t STAGE_TX = 2 * (A_BYTES + B_BYTES);  // both CTAs' loads, on the first CTA's barrier
 constexpr uint32_t TMEM_COLS = 2 * BN;
-constexpr uint32_t EPI_WARPS = 8;
+constexpr int EPI_WARPS = 8;
 
 struct Smem {
     uint8_t a[NS][A_BYTES];  // 1024-byte aligned stages
     uint8_t b[NS][B_BYTES];
+    float stage[EPI_WARPS][32][33];  // per epilogue warp: a 32 x 32 chunk, rows to columns
     uint64_t full[NS], empty[NS];
     uint64_t acc_full[2], acc_empty[2];
     uint64_t mma_done;
@@ -87,16 +88,23 @@ __device__ __forceinline__ void tile_of(long long t, const Geo& g, int& b, int& 
 }
 
 // ggml's tanh GELU (src/ops.zig:312-327), 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715
-// x^3), evaluated through the identity 1 + tanh(u) = 2 / (1 + exp(-2u)): x / (1 + exp(-2u)),
-// one exponential and one fast division (a few ulp of f32; the result is then rounded to the
-// f16 or bf16 operand of the next product, or added into the f32 stream). Large |u| gives x
-// or 0 exactly.
+// x^3), evaluated through the identity 1 + tanh(u) = 2 / (1 + exp(-2u)) as x / (1 + 2^t) with
+// t = -2 log2(e) u = x (K1 + K2 x^2): one base-2 exponential and one reciprocal on the MUFU,
+// three other operations. The error is a few ulp of f32 relative to the result (for
+// negative x too, where the result is small), far below the f16 or bf16 rounding of the next
+// product's operand. Large |x| gives x or -0 exactly.
 __device__ __forceinline__ float gelu_fast(float x) {
-    const float u = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x)));
-    return __fdividef(x, __fadd_rn(1.0f, __expf(-2.0f * u)));
+    constexpr float K1 = -2.0 * 1.4426950408889634 * 0.7978845608028654;  // -2 log2(e) sqrt(2/pi)
+    constexpr float K2 = K1 * 0.044715;
+    const float t = x * fmaf(K2, x * x, K1);
+    return __fdividef(x, 1.0f + exp2_approx(t));
 }
 
-template <int OUT, bool GELU, bool ACC>
+// SRC: what is added after the activation: SRC_NONE, SRC_ACC (the f32 output itself, the
+// residual stream) or SRC_ADDEND (e.addend, the positional embedding).
+enum { SRC_NONE = 0, SRC_ACC = 1, SRC_ADDEND = 2 };
+
+template <int OUT, bool GELU, int SRC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w, Geo geo,
                     GemmEpilogue e, int* err) {
@@ -193,27 +201,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         // warps 2-9: two warps per TMEM lane quarter, each taking one half of the columns
         const int quarter = warp & 3;               // TMEM lanes this warp may access
         const int half = (warp - 2) >> 2;           // column half of the tile
-        const int row = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         constexpr int CH = BN / 64;                 // 32-column chunks per half
+        // a chunk leaves TMEM one row per lane and goes out through shared memory as four
+        // rows per instruction, eight lanes per row, so global reads and writes are whole
+        // 128-byte lines
+        float (*stg)[33] = sm.stage[warp - 2];
+        const int rsub = lane >> 3, q = 4 * (lane & 7);
+        constexpr bool has_src = SRC != SRC_NONE;
         int it = 0;
         for (long long t = pair; t < geo.total; t += n_pairs, it++) {
             const int buf = it & 1;
             int b, m0, n0;
             tile_of(t, geo, b, m0, n0);
-            const int m = m0 + (int)rank * BM + row;
-            const bool valid = m < geo.M;
-            const size_t orow = (size_t)b * e.out_bs + (size_t)(valid ? m : 0) * e.ld_out;
+            const int mw = m0 + (int)rank * BM + quarter * 32;  // first row of this warp's 32
             const int nb = n0 + half * (BN / 2);
             // the f32 values added after the activation (the residual stream or the addend)
             // are loaded one chunk ahead, the first before the accumulator is ready
-            const float* src = ACC ? static_cast<const float*>(e.out) + orow
-                                   : (e.addend ? e.addend + (size_t)(valid ? m : 0) * e.ld_add : nullptr);
-            const bool has_src = valid && src != nullptr;
+            auto src_row = [&](int m) -> const float* {
+                return SRC == SRC_ACC ? static_cast<const float*>(e.out) + (size_t)b * e.out_bs + (size_t)m * e.ld_out
+                                      : e.addend + (size_t)m * e.ld_add;
+            };
             float4 cur[8], nxt[8];
             if (has_src && nb < geo.N) {
 #pragma unroll
-                for (int i = 0; i < 8; i++) cur[i] = *reinterpret_cast<const float4*>(src + nb + 4 * i);
+                for (int i = 0; i < 8; i++) {
+                    const int m = mw + i * 4 + rsub;
+                    if (m < geo.M) cur[i] = *reinterpret_cast<const float4*>(src_row(m) + nb + q);
+                }
             }
             if (!mbar_wait_warp(&sm.acc_full[buf], (it >> 1) & 1, err)) break;
             tc_fence_after();
@@ -223,56 +238,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 if (n >= geo.N) break;  // uniform over the warp
                 if (has_src && c + 1 < CH && n + 32 < geo.N) {
 #pragma unroll
-                    for (int i = 0; i < 8; i++) nxt[i] = *reinterpret_cast<const float4*>(src + n + 32 + 4 * i);
+                    for (int i = 0; i < 8; i++) {
+                        const int m = mw + i * 4 + rsub;
+                        if (m < geo.M) nxt[i] = *reinterpret_cast<const float4*>(src_row(m) + n + 32 + q);
+                    }
                 }
                 uint32_t r[32];
                 tmem_ld32(tmem + lane_addr + buf * BN + half * (BN / 2) + c * 32, r);
                 tmem_ld_wait();
-                float v[32];
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
                     float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (e.bias) bb = __ldg(reinterpret_cast<const float4*>(e.bias + n + i));
-                    v[i] = __fadd_rn(__uint_as_float(r[i]), bb.x);
-                    v[i + 1] = __fadd_rn(__uint_as_float(r[i + 1]), bb.y);
-                    v[i + 2] = __fadd_rn(__uint_as_float(r[i + 2]), bb.z);
-                    v[i + 3] = __fadd_rn(__uint_as_float(r[i + 3]), bb.w);
+                    float v0 = __fadd_rn(__uint_as_float(r[i]), bb.x);
+                    float v1 = __fadd_rn(__uint_as_float(r[i + 1]), bb.y);
+                    float v2 = __fadd_rn(__uint_as_float(r[i + 2]), bb.z);
+                    float v3 = __fadd_rn(__uint_as_float(r[i + 3]), bb.w);
+                    if (GELU) {
+                        v0 = gelu_fast(v0);
+                        v1 = gelu_fast(v1);
+                        v2 = gelu_fast(v2);
+                        v3 = gelu_fast(v3);
+                    }
+                    stg[lane][i] = v0;
+                    stg[lane][i + 1] = v1;
+                    stg[lane][i + 2] = v2;
+                    stg[lane][i + 3] = v3;
                 }
-                if (GELU) {
+                __syncwarp();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = gelu_fast(v[i]);
-                }
-                if (valid) {
-                    if (has_src) {
-#pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            v[4 * i] = __fadd_rn(v[4 * i], cur[i].x);
-                            v[4 * i + 1] = __fadd_rn(v[4 * i + 1], cur[i].y);
-                            v[4 * i + 2] = __fadd_rn(v[4 * i + 2], cur[i].z);
-                            v[4 * i + 3] = __fadd_rn(v[4 * i + 3], cur[i].w);
+                for (int i = 0; i < 8; i++) {
+                    const int rr = i * 4 + rsub;
+                    const int m = mw + rr;
+                    if (m < geo.M) {
+                        float4 x = make_float4(stg[rr][q], stg[rr][q + 1], stg[rr][q + 2], stg[rr][q + 3]);
+                        if (has_src)
+                            x = make_float4(__fadd_rn(x.x, cur[i].x), __fadd_rn(x.y, cur[i].y), __fadd_rn(x.z, cur[i].z),
+                                            __fadd_rn(x.w, cur[i].w));
+                        const size_t o = (size_t)b * e.out_bs + (size_t)m * e.ld_out + n + q;
+                        if (OUT == GEMM_OUT_F32) {
+                            *reinterpret_cast<float4*>(static_cast<float*>(e.out) + o) = x;
+                        } else if (OUT == GEMM_OUT_F16) {
+                            __half2 h0 = __floats2half2_rn(x.x, x.y), h1 = __floats2half2_rn(x.z, x.w);
+                            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(e.out) + o) =
+                                make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+                        } else {
+                            __nv_bfloat162 h0 = __floats2bfloat162_rn(x.x, x.y), h1 = __floats2bfloat162_rn(x.z, x.w);
+                            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(e.out) + o) =
+                                make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
                         }
                     }
-                    if (OUT == GEMM_OUT_F32) {
-                        float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + orow + n);
-#pragma unroll
-                        for (int i = 0; i < 8; i++) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                    } else {
-                        uint32_t h[16];
-#pragma unroll
-                        for (int i = 0; i < 16; i++) {
-                            if (OUT == GEMM_OUT_F16) {
-                                __half2 p2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-                                h[i] = *reinterpret_cast<uint32_t*>(&p2);
-                            } else {
-                                __nv_bfloat162 p2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-                                h[i] = *reinterpret_cast<uint32_t*>(&p2);
-                            }
-                        }
-                        uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + orow + n);
-#pragma unroll
-                        for (int i = 0; i < 4; i++) o[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
-                    }
                 }
+                __syncwarp();
 #pragma unroll
                 for (int i = 0; i < 8; i++) cur[i] = nxt[i];
             }
@@ -322,6 +339,7 @@ bool gemm_f16_supported(const GemmParams& p) {
     const size_t esz = p.out_type == GEMM_OUT_F32 ? 4 : 2;
     if ((p.e.ld_out * esz) % 16 || (p.e.out_bs * esz) % 16) return false;
     if (p.accumulate && (p.out_type != GEMM_OUT_F32 || p.e.addend)) return false;
+    if (p.e.addend && p.out_type != GEMM_OUT_F32) return false;
     if (p.e.bias && ((uintptr_t)p.e.bias & 15)) return false;
     if (p.e.addend && (((uintptr_t)p.e.addend & 15) || p.e.ld_add % 4)) return false;
     if (p.out_type < GEMM_OUT_F32 || p.out_type > GEMM_OUT_BF16) return false;
@@ -362,12 +380,17 @@ int gemm_f16_launch(const GemmParams& p, int sm_count, int* err, cudaStream_t st
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
     };
     if (p.out_type == GEMM_OUT_F32) {
-        if (p.accumulate) return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F32, true, true>) : go(gemm_f16_kernel<GEMM_OUT_F32, false, true>);
-        return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F32, true, false>) : go(gemm_f16_kernel<GEMM_OUT_F32, false, false>);
+        if (p.accumulate)
+            return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F32, true, SRC_ACC>) : go(gemm_f16_kernel<GEMM_OUT_F32, false, SRC_ACC>);
+        if (p.e.addend)
+            return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F32, true, SRC_ADDEND>)
+                          : go(gemm_f16_kernel<GEMM_OUT_F32, false, SRC_ADDEND>);
+        return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F32, true, SRC_NONE>) : go(gemm_f16_kernel<GEMM_OUT_F32, false, SRC_NONE>);
     }
+    // 16-bit outputs take no addend (gemm_f16_supported)
     if (p.out_type == GEMM_OUT_F16)
-        return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F16, true, false>) : go(gemm_f16_kernel<GEMM_OUT_F16, false, false>);
-    return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_BF16, true, false>) : go(gemm_f16_kernel<GEMM_OUT_BF16, false, false>);
+        return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_F16, true, SRC_NONE>) : go(gemm_f16_kernel<GEMM_OUT_F16, false, SRC_NONE>);
+    return p.gelu ? go(gemm_f16_kernel<GEMM_OUT_BF16, true, SRC_NONE>) : go(gemm_f16_kernel<GEMM_OUT_BF16, false, SRC_NONE>);
 }
 
 }  // namespace zwg
