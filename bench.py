@@ -855,6 +855,30 @@ def run_kernel_case(args):
             st.qkv_q8(0, h, W, 2255, q_out=qo)
             ops.linear_q8_silu_mul(h.view(1, -1), L["w_gate"], L["w_up"], out=gate)
         work = f"{(1536 + 512) * 1536 * 1.125 / 1e6:.1f} + {2 * 8960 * 1536 * 1.125 / 1e6:.1f} MB of Q8 weights"
+    elif args.kernel_case == "gemm_mlp2":
+        # the MLP down-projection of 16 small.en windows into the f32 residual stream
+        B, M, N, K = 16, 1500, 768, 3072
+        a = torch.randn(B, M, K, generator=g, device=dev).half()
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).half()
+        bias = torch.zeros(N, device=dev)
+        out = torch.zeros(B, M, N, device=dev)
+
+        def fn():
+            ops.gemm_f16(a, w, bias=bias, accumulate=True, out=out)
+        work = f"{2 * B * M * N * K / 1e9:.1f} GFLOP per launch"
+    elif args.kernel_case == "encoder_small_en":
+        from oracle import whisper as Wh
+        hp = Wh.SMALL_EN
+        B = 4
+        Wg = ops.EncoderWeightsF16(Wh.weights_dict(Wh.synth_model(hp, seed=0, encoder_only=True)), hp.n_audio_layer,
+                                   hp.n_audio_head)
+        mel = torch.randn(hp.n_mels, B * 3000, generator=g, device=dev) * 0.5
+        out = torch.empty(B, hp.n_audio_ctx, hp.n_audio_state, device=dev)
+        scratch = torch.empty(Wg.scratch_bytes(B), dtype=torch.uint8, device=dev)
+
+        def fn():
+            ops.encoder_forward(Wg, mel, B, out=out, scratch=scratch)
+        work = f"the whole small.en encoder for {B} windows"
     elif args.kernel_case == "prefill_qwen":
         B, H, Hkv, d, n_ctx, n_past, n_q = 64, 12, 2, 128, 2048, 1792, 208
         q = torch.randn(B, n_q, H * d, generator=g, device=dev)
@@ -900,7 +924,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64",
                                              "decode_tc_qwen_b1", "decode_whisper", "prefill_qwen",
-                                             "q8_logits", "step_qwen15", "step_whisper_base", "pair_qwen15"],
+                                             "q8_logits", "step_qwen15", "step_whisper_base", "pair_qwen15",
+                                             "gemm_mlp2", "encoder_small_en"],
                     default=None)
     args = ap.parse_args()
     if args.kernel_case:
