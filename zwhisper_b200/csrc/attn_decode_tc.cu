@@ -42,6 +42,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "chain.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -117,6 +118,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
     const int t_first = (int)(((long long)piece * a.n_t) / a.pieces);
     const int n_t = (int)(((long long)(piece + 1) * a.n_t) / a.pieces) - t_first;
 
+    // launched as a programmatic dependent of the kernel before it (the q/k/v projection of
+    // a decode step): the next kernel may start as soon as every CTA got here
+    chain_release();
     if (threadIdx.x == 0) {
         sm.abort_flag = err ? *(volatile int*)err : 0;
         sm.last = 0;
@@ -144,6 +148,22 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
         tmem_alloc(&sm.tmem_base, C::TMEM_COLS);
         tmem_relinquish();
     }
+    // While the previous kernel finishes: the first K^T and V tiles of this piece into L2 (a
+    // prefetch reads nothing into the CTA, so data the previous kernel is still writing is
+    // read only after the wait below, from the coherent L2). Then every thread waits for the
+    // previous kernel before any read of q, K, V or the workspace and any write.
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        const int n_pre = n_t < NST + 1 ? n_t : NST + 1;
+        for (int j = 0; j < n_pre; j++) {
+            const int key0 = (t_first + j) * BN;
+            tma_prefetch_3d(&tm_k, key0, kh * D, b);
+            tma_prefetch_3d(&tm_k, key0 + 32, kh * D, b);
+            for (int c = 0; c < D / 32; c++) tma_prefetch_3d(&tm_v, kh * D + c * 32, key0, b);
+        }
+    }
+    chain_wait();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -525,7 +545,9 @@ int launch_d(const DecodeParams& p, size_t n_batch, int sm_count, cudaStream_t s
             attr_set[dev] = true;
         }
     }
-    decode_tc_kernel<D><<<a.n_items, THREADS, smem_bytes<D>(), st>>>(mk, mv, a);
+    if (launch_chained_smem(decode_tc_kernel<D>, dim3(a.n_items), dim3(THREADS), smem_bytes<D>(), st, mk, mv, a) !=
+        cudaSuccess)
+        return -1;
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -33,6 +33,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "chain.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -152,6 +153,9 @@ __global__ void __launch_bounds__(Cfg<D, RMAX>::THREADS, 1)
     const long long t_begin = range_begin(blockIdx.x, geo, gridDim.x);
     const long long t_end = range_begin(blockIdx.x + 1, geo, gridDim.x);
 
+    // launched as a programmatic dependent of the kernel before it (the q/k/v projection of
+    // a decode step): the next kernel may start as soon as every CTA got here
+    chain_release();
     if (threadIdx.x == 0) sm.abort_flag = err ? *(volatile int*)err : 0;
     __syncthreads();
     if (sm.abort_flag || t_begin >= t_end) return;
@@ -166,6 +170,25 @@ __global__ void __launch_bounds__(Cfg<D, RMAX>::THREADS, 1)
         }
         fence_mbar_init();
     }
+    // While the previous kernel finishes: this CTA's first K and V tiles into L2 (a prefetch
+    // reads nothing into the CTA, so data the previous kernel is still writing is read only
+    // after the wait, from the coherent L2). Then every thread waits for the previous kernel
+    // before any read of q, K, V or the workspace and any write.
+    if (warp == C::NW && lane == 0) {
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        const long long x_end = std::min<long long>(t_end, t_begin + C::NS);
+        for (long long x = t_begin; x < x_end; x++) {
+            const int seg = (int)(x / geo.n_t);
+            const int hk = seg % (int)p.n_head_kv;
+            const int b = seg / (int)p.n_head_kv;
+            const int t0 = (int)(x - (long long)seg * geo.n_t) * TK;
+            if (KT) tma_prefetch_3d(&tm_k, t0, hk * D, b);
+            else tma_prefetch_3d(&tm_k, hk * D, t0, b);
+            tma_prefetch_3d(&tm_v, hk * D, t0, b);
+        }
+    }
+    chain_wait();
     __syncthreads();
 
     if (warp == C::NW) {
@@ -653,7 +676,8 @@ static int launch_d(const DecodeParams& p, size_t n_batch, int rmax, int grid, i
     auto go = [&](auto kern, size_t smem, int threads) -> int {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return -1;
-        kern<<<grid, threads, smem, st>>>(mk, mv, p, geo, counters, err);
+        if (launch_chained_smem(kern, dim3(grid), dim3(threads), smem, st, mk, mv, p, geo, counters, err) != cudaSuccess)
+            return -1;
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
     };
     switch (rmax) {

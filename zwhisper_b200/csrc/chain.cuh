@@ -26,11 +26,12 @@ __device__ __forceinline__ int chain_wait() {
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_chained(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+cudaError_t launch_chained_smem(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -38,6 +39,11 @@ cudaError_t launch_chained(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaSt
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_chained(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    return launch_chained_smem(kern, grid, block, 0, st, args...);
 }
 
 }  // namespace zwg

@@ -94,6 +94,14 @@ ZWG_DEV void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst, int c
         : "memory");
 }
 
+// Prefetch one tile of a tensor map into L2 (no shared memory, no barrier): a hint that
+// reads nothing into the CTA, so it may run before the data's producer has finished.
+ZWG_DEV void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(map), "r"(c0), "r"(c1),
+                 "r"(c2)
+                 : "memory");
+}
+
 ZWG_DEV void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
