@@ -56,9 +56,32 @@ def check_linear(torch, ops, m, n, k, bias, seed):
 @pytest.mark.parametrize("m", [1, 2, 3, 8, 13, 37])
 @pytest.mark.parametrize("n,k", [(1, 32), (7, 64), (512, 512), (1536, 1536), (101, 8960)])
 def test_linear_matches_oracle(env, m, n, k):
-    """m >= 16 runs every full chunk of 8 x rows in one launch (grid.y) and the rest in another."""
+    """Up to 15 rows run in chunks of 8 rows of x; 16 or more (37 here) the register-tiled
+    product."""
     torch, ops = env
     check_linear(torch, ops, m, n, k, bias=(m % 2 == 1), seed=m * 100 + n + k)
+
+
+@pytest.mark.parametrize("m,n,k", [(32, 4096, 512), (64, 1536, 8960), (64, 2048, 1536), (16, 100, 96)])
+def test_linear_many_rows(env, m, n, k):
+    """16 or more rows run the register-tiled product; small tile counts split k over a
+    cluster of CTAs and reduce through distributed shared memory (512 x 4096 at 32 rows: 8
+    splits; 100 columns: a partial tile)."""
+    torch, ops = env
+    check_linear(torch, ops, m, n, k, bias=(n % 2 == 0), seed=m + n + k)
+
+
+def test_linear_many_rows_deterministic(env):
+    """The split-K reduction sums the partial tiles in a fixed order: repeated calls are
+    bit-identical."""
+    torch, ops = env
+    rng = np.random.default_rng(9)
+    dev = torch.device("cuda:0")
+    x = torch.from_numpy(rng.standard_normal((32, 512), dtype=np.float32)).to(dev)
+    qo, so = q8.quantize((rng.standard_normal((512, 512), dtype=np.float32) * 0.02).astype(np.float32))
+    tq, ts = torch.from_numpy(qo).to(dev), torch.from_numpy(so).to(dev)
+    outs = [ops.linear_q8(x, tq, ts, None).cpu() for _ in range(3)]
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
 
 
 def test_linear_set_audio_shape(env):

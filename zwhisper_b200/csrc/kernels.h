@@ -140,6 +140,10 @@ int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const
 // Paired-row Q8 products with a fused epilogue (q8.cu): PAIR_ROPE = the q/k/v projections
 // with bias, RoPE and the K^T / V cache append; PAIR_SILU = silu(x . Wg^T) * (x . Wu^T).
 enum { PAIR_ROPE = 0, PAIR_SILU = 1 };
+// The register-tiled Q8 product for many rows of x (q8_gemm.cu), same arguments and modes as
+// q8_linear_launch; k a multiple of 32, x and wq 16-byte aligned.
+int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
+                   int mode, float* out, int sm_count, cudaStream_t st);
 struct PairParams {
     const float* x;  // [m][k], row t of the call is sequence t / n_tok, token t % n_tok
     int m, k;

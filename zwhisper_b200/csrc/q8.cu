@@ -511,18 +511,9 @@ int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const
     if (m == 0 || n == 0) return 0;
     const int sms = sm_count_current();
     const int ik = (int)k, in = (int)n;
-    size_t m0 = 0;
-    if (m >= 16) {
-        // all full chunks of 8 rows in one launch (grid.y = chunk)
-        const size_t full = m / 8;
-        if (full >= 65536) return -1;
-        const q8::Plan pl = q8::plan(8, n, 0, sms);
-        const size_t rows_per_cta = (size_t)(q8::WARPS / pl.ks) * pl.rw;
-        const dim3 grid((unsigned)((n + rows_per_cta - 1) / rows_per_cta), (unsigned)full);
-        if (q8::linear_chunk<8>(pl, grid, st, x, 8, ik, wq, ws, bias, in, mode, out) != cudaSuccess) return -1;
-        m0 = full * 8;
-    }
-    for (; m0 < m; m0 += 8) {
+    // many rows of x: the register-tiled product, the weights read once per 32 rows
+    if (m >= 16) return q8_gemm_launch(x, m, k, wq, ws, bias, n, mode, out, sms, st);
+    for (size_t m0 = 0; m0 < m; m0 += 8) {
         const int mc = (int)std::min<size_t>(8, m - m0);
         const float* xc = x + m0 * k;
         float* oc = out + m0 * n;
