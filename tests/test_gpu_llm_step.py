@@ -87,7 +87,7 @@ def test_linear_q8_add(env, m, n, k):
     assert (err <= 2e-6 * (bound(x, w) + np.abs(resid)) + 1e-30).all()
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 13])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 13, 16, 64])
 @pytest.mark.parametrize("n,k", [(101, 256), (1000, 1536), (33, 896)])
 def test_linear_q8_silu_mul(env, m, n, k):
     torch, ops = env

@@ -144,6 +144,10 @@ enum { PAIR_ROPE = 0, PAIR_SILU = 1 };
 // q8_linear_launch; k a multiple of 32, x and wq 16-byte aligned.
 int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
                    int mode, float* out, int sm_count, cudaStream_t st);
+// out[m][n_ff] = silu(x . Wg^T + bg) * (x . Wu^T + bu) on the same tiles (biases may be null).
+int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, const float* sg, const float* bg,
+                        const int8_t* wu, const float* su, const float* bu, size_t n_ff, float* out, int sm_count,
+                        cudaStream_t st);
 struct PairParams {
     const float* x;  // [m][k], row t of the call is sequence t / n_tok, token t % n_tok
     int m, k;

@@ -18,6 +18,11 @@
 // the epilogue. The kernel has no spin waits: only block and cluster barriers, which every
 // thread reaches.
 //
+// The SiLU pair (the gate and up projections and ops.siluMul of an LLM layer, src/llm.zig:
+// 206-208, src/ops.zig:435-440) runs on the same tiles: a tile's 64 columns are 32 gate rows
+// and the same 32 up rows, a thread owns two of each, and the epilogue writes
+// gate / (1 + exp(-gate)) * up.
+//
 // Launched as a programmatic dependent (chain.cuh): the weight rows of the CTA's k range are
 // prefetched into L2 before the wait for the kernel that wrote x.
 #include <cuda_runtime.h>
@@ -63,6 +68,17 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+__device__ __forceinline__ void finish_pair(float* out, const float* bias_g, const float* bias_u, int n, int row,
+                                            int col, float g, float u) {
+    if (bias_g) g = __fadd_rn(g, __ldg(bias_g + col));
+    if (bias_u) u = __fadd_rn(u, __ldg(bias_u + col));
+    out[(size_t)row * n + col] = silu_mul(g, u);
+}
+
 template <int MODE>
 __device__ __forceinline__ void finish(float* out, const float* bias, int n, int row, int col, float v) {
     if (bias) v = __fadd_rn(v, __ldg(bias + col));
@@ -72,20 +88,39 @@ __device__ __forceinline__ void finish(float* out, const float* bias, int n, int
     *o = v;
 }
 
-template <int MODE>
+// The second matrix of the SiLU pair, and its bias.
+struct Second {
+    const int8_t* wq;
+    const float* ws;
+    const float* bias;
+};
+
+// Column of the tile held by output j (0..3) of thread tx: four consecutive columns, or for
+// the SiLU pair two gate columns and the same two up columns.
+template <bool PAIR>
+__device__ __forceinline__ int tile_col(int tx, int j) {
+    return PAIR ? (j < 2 ? tx * 2 + j : BN / 2 + tx * 2 + (j - 2)) : tx * 4 + j;
+}
+
+// MODE: LIN_STORE / LIN_ADD / LIN_GELU; PAIR: the SiLU pair (out [m][n], n = n_ff).
+template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m, int k, const int8_t* __restrict__ wq,
                                                           const float* __restrict__ ws, const float* __restrict__ bias,
-                                                          int n, float* out, int ks) {
+                                                          int n, float* out, int ks, Second sec) {
     __shared__ __align__(16) Smem sm;
     const int t = threadIdx.x, ty = t >> 4, tx = t & 15;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, kz = blockIdx.z;
+    // a tile's first output column: 64 columns, or 32 gate / up pairs
+    const int n0 = blockIdx.x * (PAIR ? BN / 2 : BN), m0 = blockIdx.y * BM, kz = blockIdx.z;
     const int nb = k / BK;
     const int b_beg = (int)((long long)kz * nb / ks), b_end = (int)((long long)(kz + 1) * nb / ks);
     // loader roles: x rows (t >> 3) and (t >> 3) + 16, four k at (t & 7) * 4; weight row t >> 1,
     // sixteen k at (t & 1) * 16
     const int xrow = t >> 3, xk = (t & 7) * 4, wj = t >> 1, wh = t & 1;
-    const bool wrow_ok = n0 + wj < n;
-    const int8_t* wrow = wq + (size_t)(wrow_ok ? n0 + wj : 0) * k;
+    const bool up = PAIR && wj >= BN / 2;          // this loader's row comes from the up matrix
+    const int wn = PAIR ? n0 + (up ? wj - BN / 2 : wj) : n0 + wj;
+    const bool wrow_ok = wn < n;
+    const int8_t* wrow = (up ? sec.wq : wq) + (size_t)(wrow_ok ? wn : 0) * k;
+    const float* wsc = (up ? sec.ws : ws) + (size_t)(wrow_ok ? wn : 0) * nb;
     // the weights are constants: their rows of this k range go to L2 before the wait
     if (wrow_ok)
         for (int off = b_beg * BK + wh * 128; off < b_end * BK; off += 256)
@@ -106,7 +141,7 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         qr = wrow_ok ? __ldg(reinterpret_cast<const uint4*>(wrow + kb * BK + wh * 16)) : make_uint4(0, 0, 0, 0);
-        if (wh == 0) sr = wrow_ok ? __ldg(ws + (size_t)(n0 + wj) * nb + kb) : 0.f;
+        if (wh == 0) sr = wrow_ok ? __ldg(wsc + kb) : 0.f;
     };
     auto store = [&](int buf) {
 #pragma unroll
@@ -147,15 +182,24 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
 #pragma unroll 8
         for (int kk = 0; kk < BK; kk++) {
             const float4 a = *reinterpret_cast<const float4*>(&sm.xs[buf][kk][ty * 4]);
-            const float4 b = *reinterpret_cast<const float4*>(&sm.wq[buf][kk][tx * 4]);
-            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+            float bv[4];
+            if (PAIR) {
+                const float2 b0 = *reinterpret_cast<const float2*>(&sm.wq[buf][kk][tx * 2]);
+                const float2 b1 = *reinterpret_cast<const float2*>(&sm.wq[buf][kk][BN / 2 + tx * 2]);
+                bv[0] = b0.x, bv[1] = b0.y, bv[2] = b1.x, bv[3] = b1.y;
+            } else {
+                const float4 b = *reinterpret_cast<const float4*>(&sm.wq[buf][kk][tx * 4]);
+                bv[0] = b.x, bv[1] = b.y, bv[2] = b.z, bv[3] = b.w;
+            }
+            const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) p[i][j] = fmaf(av[i], bv[j], p[i][j]);
         }
-        const float4 s = *reinterpret_cast<const float4*>(&sm.sc[buf][tx * 4]);
-        const float sv[4] = {s.x, s.y, s.z, s.w};
+        float sv[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) sv[j] = sm.sc[buf][tile_col<PAIR>(tx, j)];
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
@@ -169,10 +213,18 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
         for (int i = 0; i < 4; i++) {
             const int row = m0 + ty * 4 + i;
             if (row >= m) continue;
+            if (PAIR) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int col = n0 + tx * 4 + j;
-                if (col < n) finish<MODE>(out, bias, n, row, col, acc[i][j]);
+                for (int j = 0; j < 2; j++) {
+                    const int col = n0 + tx * 2 + j;
+                    if (col < n) finish_pair(out, bias, sec.bias, n, row, col, acc[i][j], acc[i][2 + j]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int col = n0 + tx * 4 + j;
+                    if (col < n) finish<MODE>(out, bias, n, row, col, acc[i][j]);
+                }
             }
         }
         return;
@@ -181,15 +233,22 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) sm.red[ty * 4 + i][tx * 4 + j] = acc[i][j];
+        for (int j = 0; j < 4; j++) sm.red[ty * 4 + i][tile_col<PAIR>(tx, j)] = acc[i][j];
     cluster_sync_all();
     const int rows = BM / ks, r0 = kz * rows;
-    for (int e = t; e < rows * BN; e += THREADS) {
-        const int rr = r0 + e / BN, cc = e % BN;
+    constexpr int OUTS = PAIR ? BN / 2 : BN;  // outputs per tile row
+    for (int e = t; e < rows * OUTS; e += THREADS) {
+        const int rr = r0 + e / OUTS, cc = e % OUTS;
         const int row = m0 + rr, col = n0 + cc;
-        float v = 0.f;
-        for (int q = 0; q < ks; q++) v = __fadd_rn(v, ld_cluster(cluster_addr(&sm.red[rr][cc], (uint32_t)q)));
-        if (row < m && col < n) finish<MODE>(out, bias, n, row, col, v);
+        float v = 0.f, u = 0.f;
+        for (int q = 0; q < ks; q++) {
+            v = __fadd_rn(v, ld_cluster(cluster_addr(&sm.red[rr][cc], (uint32_t)q)));
+            if (PAIR) u = __fadd_rn(u, ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)));
+        }
+        if (row < m && col < n) {
+            if (PAIR) finish_pair(out, bias, sec.bias, n, row, col, v, u);
+            else finish<MODE>(out, bias, n, row, col, v);
+        }
     }
     // no CTA leaves while another may still read its partial tile
     cluster_sync_all();
@@ -197,15 +256,17 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
 
 }  // namespace q8g
 
-// out[m][n] (+)= x[m][k] . W^T for m >= 1 (meant for m >= 16), k a multiple of 32; mode as
-// q8_linear_launch. Returns -1 on a bad argument or a launch failure.
-int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
-                   int mode, float* out, int sm_count, cudaStream_t st) {
+namespace {
+
+int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
+           int mode, bool pair, q8g::Second sec, float* out, int sm_count, cudaStream_t st) {
     using namespace q8g;
     if (m == 0 || n == 0) return 0;
-    if (k == 0 || k % BK || ((uintptr_t)x & 15) || ((uintptr_t)wq & 15)) return -1;
+    if (k == 0 || k % BK || ((uintptr_t)x & 15) || ((uintptr_t)wq & 15) || (pair && ((uintptr_t)sec.wq & 15)))
+        return -1;
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return -1;
-    const size_t tiles_n = (n + BN - 1) / BN, tiles_m = (m + BM - 1) / BM;
+    const size_t per_tile = pair ? BN / 2 : BN;
+    const size_t tiles_n = (n + per_tile - 1) / per_tile, tiles_m = (m + BM - 1) / BM;
     if (tiles_m > 65535 || tiles_n > 0x7fffffff) return -1;
     const size_t nb = k / BK;
     // k splits (powers of two, at most 8, at least two k blocks each) while the tiles alone
@@ -228,10 +289,29 @@ int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const f
     cfg.numAttrs = 2;
     cudaError_t e;
     const int im = (int)m, ik = (int)k, in = (int)n;
-    if (mode == LIN_ADD) e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_ADD>, x, im, ik, wq, ws, bias, in, out, ks);
-    else if (mode == LIN_GELU) e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_GELU>, x, im, ik, wq, ws, bias, in, out, ks);
-    else e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_STORE>, x, im, ik, wq, ws, bias, in, out, ks);
+    if (pair) e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_STORE, true>, x, im, ik, wq, ws, bias, in, out, ks, sec);
+    else if (mode == LIN_ADD)
+        e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_ADD, false>, x, im, ik, wq, ws, bias, in, out, ks, sec);
+    else if (mode == LIN_GELU)
+        e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_GELU, false>, x, im, ik, wq, ws, bias, in, out, ks, sec);
+    else e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_STORE, false>, x, im, ik, wq, ws, bias, in, out, ks, sec);
     return e == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace
+
+// out[m][n] (+)= x[m][k] . W^T (meant for m >= 16), k a multiple of 32; mode as
+// q8_linear_launch. Returns -1 on a bad argument or a launch failure.
+int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
+                   int mode, float* out, int sm_count, cudaStream_t st) {
+    return launch(x, m, k, wq, ws, bias, n, mode, false, q8g::Second{nullptr, nullptr, nullptr}, out, sm_count, st);
+}
+
+// out[m][n_ff] = silu(x . Wg^T + bg) * (x . Wu^T + bu), the SiLU pair of q8_pair_launch.
+int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, const float* sg, const float* bg,
+                        const int8_t* wu, const float* su, const float* bu, size_t n_ff, float* out, int sm_count,
+                        cudaStream_t st) {
+    return launch(x, m, k, wg, sg, bg, n_ff, LIN_STORE, true, q8g::Second{wu, su, bu}, out, sm_count, st);
 }
 
 }  // namespace zwg
