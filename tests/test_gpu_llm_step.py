@@ -88,7 +88,7 @@ def test_linear_q8_add(env, m, n, k):
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 8, 13, 16, 64])
-@pytest.mark.parametrize("n,k", [(101, 256), (1000, 1536), (33, 896)])
+@pytest.mark.parametrize("n,k", [(101, 256), (1000, 1536), (33, 896), (4096, 512)])
 def test_linear_q8_silu_mul(env, m, n, k):
     torch, ops = env
     rng = np.random.default_rng(10 * m + n + k)

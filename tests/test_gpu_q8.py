@@ -62,11 +62,13 @@ def test_linear_matches_oracle(env, m, n, k):
     check_linear(torch, ops, m, n, k, bias=(m % 2 == 1), seed=m * 100 + n + k)
 
 
-@pytest.mark.parametrize("m,n,k", [(32, 4096, 512), (64, 1536, 8960), (64, 2048, 1536), (16, 100, 96)])
+@pytest.mark.parametrize("m,n,k", [(32, 4096, 512), (64, 1536, 8960), (64, 2048, 1536), (16, 100, 96),
+                                   (32, 8192, 512), (64, 8960, 1536), (200, 2048, 256)])
 def test_linear_many_rows(env, m, n, k):
-    """16 or more rows run the register-tiled product; small tile counts split k over a
-    cluster of CTAs and reduce through distributed shared memory (512 x 4096 at 32 rows: 8
-    splits; 100 columns: a partial tile)."""
+    """16 or more rows run the register-tiled product: shapes with at least 64 tiles of 32 or
+    64 rows x 128 columns on those (8192 or 8960 columns, 200 rows with a partial row tile),
+    the others on 32 x 64 tiles with k split over a cluster of CTAs and reduced through
+    distributed shared memory (100 columns: a partial tile)."""
     torch, ops = env
     check_linear(torch, ops, m, n, k, bias=(n % 2 == 0), seed=m + n + k)
 

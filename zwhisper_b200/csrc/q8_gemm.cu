@@ -1,15 +1,14 @@
 // Q8 products for 16 or more rows of activations (ops.linear with Q8 weights, src/ops.zig:
-// 280-306 -> gemm.ntBlockQ, src/gemm.zig:268-351): out[i][j] = sum over the k/32 blocks of
-// scale[j][b] * (sum over the block of x[i][k] * q[j][k]), + bias[j], then the epilogue of
-// q8_linear_kernel (store, add into out, or tanh GELU).
+// 280-306 -> gemm.ntBlockQ, src/gemm.zig:268-351): out[i][j] = sum over k of x[i][k] * w[j][k]
+// with w = q * scale (the dequantized weight of Q8.row, src/gemm.zig:256-263), + bias[j], then
+// the epilogue of q8_linear_kernel (store, add into out, or tanh GELU).
 //
 // At 16-64 rows (a decoder step over 32 windows, an LLM step over 64 sequences, the 1500 rows
 // of setAudio) the weight bytes are read once per tile instead of once per 8 rows, and the
-// work is f32 FMA: a register-tiled product, CTA tile 32 rows x 64 columns, 128 threads with
-// 4 x 4 outputs each. Per 32-wide k block the CTA stages x (k-major) and the int8 weights as
-// exact small floats (k-major) in shared memory, double-buffered through registers; each
-// thread forms the block's 4 x 4 dots and adds them times the block's scales, as the
-// reference does per block.
+// work is f32 FMA: a register-tiled product, CTA tile 32 or 64 rows x 128 columns, 8 x 8
+// outputs per thread (shapes with fewer than 64 such tiles take 32 x 64 tiles, below). Per 32-wide k block the CTA stages x (k-major) and the dequantized
+// weights (k-major) in shared memory, double-buffered through registers; a thread's k step
+// is four 16-byte shared loads for 64 FMAs.
 //
 // Split-K without a workspace: when the tiles alone would leave SMs idle, a cluster of ks
 // CTAs (1 x 1 x ks) takes one tile, each CTA a contiguous range of k blocks; the CTAs then
@@ -19,8 +18,8 @@
 // thread reaches.
 //
 // The SiLU pair (the gate and up projections and ops.siluMul of an LLM layer, src/llm.zig:
-// 206-208, src/ops.zig:435-440) runs on the same tiles: a tile's 64 columns are 32 gate rows
-// and the same 32 up rows, a thread owns two of each, and the epilogue writes
+// 206-208, src/ops.zig:435-440) runs on the same tiles: a tile's 128 columns are 64 gate rows
+// and the same 64 up rows, a thread owns four of each, and the epilogue writes
 // gate / (1 + exp(-gate)) * up.
 //
 // Launched as a programmatic dependent (chain.cuh): the weight rows of the CTA's k range are
@@ -38,13 +37,17 @@ namespace zwg {
 
 namespace q8g {
 
-constexpr int BM = 32, BN = 64, BK = 32, THREADS = 128, MAX_KS = 8;
+constexpr int BN = 128, BK = 32, MAX_KS = 8;
 
+template <int BM>
 struct Smem {
-    float xs[2][BK][BM];  // x block, k-major
-    float wq[2][BK][BN];  // int8 weights of the block as floats, k-major
-    float sc[2][BN];      // the block's scale of each column
-    float red[BM][BN];    // this CTA's partial tile (split-K)
+    union {
+        struct {
+            float xs[2][BK][BM];  // x block, k-major
+            float ws[2][BK][BN];  // dequantized weights of the block, k-major
+        } s;
+        float red[BM][BN];        // this CTA's partial tile (split-K), after the k loop
+    };
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -95,8 +98,187 @@ struct Second {
     const float* bias;
 };
 
-// Column of the tile held by output j (0..3) of thread tx: four consecutive columns, or for
-// the SiLU pair two gate columns and the same two up columns.
+// Tile column of output j (0..7) of thread tx: columns tx*4..+3 of each 64-column half (for
+// the SiLU pair the gate and the up half).
+__device__ __forceinline__ int tile_col(int tx, int j) { return (j < 4 ? 0 : BN / 2) + tx * 4 + (j & 3); }
+
+// MODE: LIN_STORE / LIN_ADD / LIN_GELU; PAIR: the SiLU pair (out [m][n], n = n_ff); BM: rows
+// of x per tile (32 or 64), threads = BM / 8 * 16.
+template <int MODE, bool PAIR, int BM>
+__global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, int k, const int8_t* __restrict__ wq,
+                                                        const float* __restrict__ ws, const float* __restrict__ bias,
+                                                        int n, float* out, int ks, Second sec) {
+    constexpr int THREADS = BM * 2;
+    constexpr int XL = BM * BK / 4 / THREADS;    // x float4 per thread per block (4)
+    constexpr int WL = BN * BK / 16 / THREADS;   // weight 16-byte pieces per thread per block
+    __shared__ __align__(16) Smem<BM> sm;
+    const int t = threadIdx.x, ty = t >> 4, tx = t & 15;
+    // a tile's first output column: 128 columns, or 64 gate / up pairs
+    const int n0 = blockIdx.x * (PAIR ? BN / 2 : BN), m0 = blockIdx.y * BM, kz = blockIdx.z;
+    const int nb = k / BK;
+    const int b_beg = (int)((long long)kz * nb / ks), b_end = (int)((long long)(kz + 1) * nb / ks);
+    // weight loader rows: piece t + i * THREADS is row (.) >> 1, sixteen k at ((.) & 1) * 16
+    const int8_t* wrow[WL];
+    const float* wsc[WL];
+    bool wok[WL];
+#pragma unroll
+    for (int i = 0; i < WL; i++) {
+        const int wj = (t + i * THREADS) >> 1;
+        const bool up = PAIR && wj >= BN / 2;      // this row comes from the up matrix
+        const int wn = n0 + (up ? wj - BN / 2 : wj);
+        wok[i] = wn < n;
+        wrow[i] = (up ? sec.wq : wq) + (size_t)(wok[i] ? wn : 0) * k;
+        wsc[i] = (up ? sec.ws : ws) + (size_t)(wok[i] ? wn : 0) * nb;
+        // the weights are constants: their rows of this k range go to L2 before the wait
+        if (wok[i] && ((t + i * THREADS) & 1) == 0)
+            for (int off = b_beg * BK; off < b_end * BK; off += 128)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(wrow[i] + off));
+    }
+    chain_release();
+    const int z = chain_wait();
+    x += z;
+    out += z;
+
+    float4 xr[XL];
+    uint4 qr[WL];
+    float sr[WL];
+    auto load = [&](int kb) {
+#pragma unroll
+        for (int i = 0; i < XL; i++) {
+            const int idx = t + i * THREADS, row = m0 + (idx >> 3), kq = (idx & 7) * 4;
+            xr[i] = row < m ? *reinterpret_cast<const float4*>(x + (size_t)row * k + kb * BK + kq)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < WL; i++) {
+            const int h = (t + i * THREADS) & 1;
+            qr[i] = wok[i] ? __ldg(reinterpret_cast<const uint4*>(wrow[i] + kb * BK + h * 16)) : make_uint4(0, 0, 0, 0);
+            sr[i] = wok[i] ? __ldg(wsc[i] + kb) : 0.f;
+        }
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < XL; i++) {
+            const int idx = t + i * THREADS, row = idx >> 3, kq = (idx & 7) * 4;
+            sm.s.xs[buf][kq][row] = xr[i].x;
+            sm.s.xs[buf][kq + 1][row] = xr[i].y;
+            sm.s.xs[buf][kq + 2][row] = xr[i].z;
+            sm.s.xs[buf][kq + 3][row] = xr[i].w;
+        }
+#pragma unroll
+        for (int i = 0; i < WL; i++) {
+            const int idx = t + i * THREADS, wj = idx >> 1, h = idx & 1;
+            const uint32_t words[4] = {qr[i].x, qr[i].y, qr[i].z, qr[i].w};
+#pragma unroll
+            for (int wdx = 0; wdx < 4; wdx++)
+#pragma unroll
+                for (int byte = 0; byte < 4; byte++)
+                    sm.s.ws[buf][h * 16 + wdx * 4 + byte][wj] =
+                        __fmul_rn((float)(int8_t)(words[wdx] >> (8 * byte)), sr[i]);
+        }
+    };
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+    if (b_beg < b_end) {
+        load(b_beg);
+        store(0);
+    }
+    __syncthreads();
+    for (int kb = b_beg; kb < b_end; kb++) {
+        const int buf = (kb - b_beg) & 1;
+        if (kb + 1 < b_end) load(kb + 1);
+#pragma unroll 4
+        for (int kk = 0; kk < BK; kk++) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&sm.s.xs[buf][kk][ty * 8]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&sm.s.xs[buf][kk][ty * 8 + 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&sm.s.ws[buf][kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&sm.s.ws[buf][kk][BN / 2 + tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (kb + 1 < b_end) store(buf ^ 1);
+        __syncthreads();
+    }
+
+    if (ks == 1) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int row = m0 + ty * 8 + i;
+            if (row >= m) continue;
+            if (PAIR) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int col = n0 + tx * 4 + j;
+                    if (col < n) finish_pair(out, bias, sec.bias, n, row, col, acc[i][j], acc[i][4 + j]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int col = n0 + tile_col(tx, j);
+                    if (col < n) finish<MODE>(out, bias, n, row, col, acc[i][j]);
+                }
+            }
+        }
+        return;
+    }
+    // split-K: partial tiles in shared memory (over the staging buffers, all reads of which
+    // ended at the loop's last barrier), each CTA reduces BM / ks rows over the cluster
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) sm.red[ty * 8 + i][tile_col(tx, j)] = acc[i][j];
+    cluster_sync_all();
+    const int rows = BM / ks, r0 = kz * rows;
+    constexpr int OUTS = PAIR ? BN / 2 : BN;  // outputs per tile row
+    for (int e = t; e < rows * OUTS; e += THREADS) {
+        const int rr = r0 + e / OUTS, cc = e % OUTS;
+        const int row = m0 + rr, col = n0 + cc;
+        float v = 0.f, u = 0.f;
+        for (int q = 0; q < ks; q++) {
+            v = __fadd_rn(v, ld_cluster(cluster_addr(&sm.red[rr][cc], (uint32_t)q)));
+            if (PAIR) u = __fadd_rn(u, ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)));
+        }
+        if (row < m && col < n) {
+            if (PAIR) finish_pair(out, bias, sec.bias, n, row, col, v, u);
+            else finish<MODE>(out, bias, n, row, col, v);
+        }
+    }
+    // no CTA leaves while another may still read its partial tile
+    cluster_sync_all();
+}
+
+}  // namespace q8g
+
+// The small-tile kernel for shapes that give few 64 x 128 tiles (a decoder step's 512 x 512
+// projections, an LLM layer's output and down projections at 64 rows): tiles of 32 x 64, 4 x
+// 4 outputs per thread, the block's dots formed unscaled and added times the block's scales,
+// and more k splits.
+namespace q8s {
+
+constexpr int BM = 32, BN = 64, BK = 32, THREADS = 128, MAX_KS = 8;
+
+struct Smem {
+    float xs[2][BK][BM];  // x block, k-major
+    float wq[2][BK][BN];  // int8 weights of the block as floats, k-major
+    float sc[2][BN];      // the block's scale of each column
+    float red[BM][BN];    // this CTA's partial tile (split-K)
+};
+
+using q8g::cluster_addr;
+using q8g::cluster_sync_all;
+using q8g::finish;
+using q8g::finish_pair;
+using q8g::ld_cluster;
+using q8g::Second;
+
 template <bool PAIR>
 __device__ __forceinline__ int tile_col(int tx, int j) {
     return PAIR ? (j < 2 ? tx * 2 + j : BN / 2 + tx * 2 + (j - 2)) : tx * 4 + j;
@@ -254,28 +436,39 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
     cluster_sync_all();
 }
 
-}  // namespace q8g
+}  // namespace q8s
 
 namespace {
 
+// k splits (powers of two, at most 8, at least two k blocks each) while the tiles alone
+// would give fewer than two CTAs per SM
+int k_splits(size_t tiles, size_t nb, int sm_count) {
+    int ks = 1;
+    while (ks < q8g::MAX_KS && tiles * ks < 2 * (size_t)std::max(1, sm_count) && nb / (2 * ks) >= 2) ks *= 2;
+    return ks;
+}
+
 int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
            int mode, bool pair, q8g::Second sec, float* out, int sm_count, cudaStream_t st) {
-    using namespace q8g;
     if (m == 0 || n == 0) return 0;
-    if (k == 0 || k % BK || ((uintptr_t)x & 15) || ((uintptr_t)wq & 15) || (pair && ((uintptr_t)sec.wq & 15)))
+    if (k == 0 || k % q8g::BK || ((uintptr_t)x & 15) || ((uintptr_t)wq & 15) || (pair && ((uintptr_t)sec.wq & 15)))
         return -1;
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return -1;
-    const size_t per_tile = pair ? BN / 2 : BN;
-    const size_t tiles_n = (n + per_tile - 1) / per_tile, tiles_m = (m + BM - 1) / BM;
+    const size_t nb = k / q8g::BK;
+    // the large tiles (32 or 64 rows x 128 columns) when the shape gives at least 64 of them
+    // (measured on B200: the logits, an LLM layer's gate/up pair), else the small ones
+    const int bm = m <= 32 ? 32 : 64;
+    const size_t big_n = (n + (pair ? q8g::BN / 2 : q8g::BN) - 1) / (pair ? q8g::BN / 2 : q8g::BN);
+    const size_t big_m = (m + bm - 1) / bm;
+    const bool big = big_n * big_m >= 64;
+    const size_t small_n = (n + (pair ? q8s::BN / 2 : q8s::BN) - 1) / (pair ? q8s::BN / 2 : q8s::BN);
+    const size_t small_m = (m + q8s::BM - 1) / q8s::BM;
+    const size_t tiles_n = big ? big_n : small_n, tiles_m = big ? big_m : small_m;
     if (tiles_m > 65535 || tiles_n > 0x7fffffff) return -1;
-    const size_t nb = k / BK;
-    // k splits (powers of two, at most 8, at least two k blocks each) while the tiles alone
-    // would give fewer than two CTAs per SM
-    int ks = 1;
-    while (ks < MAX_KS && tiles_n * tiles_m * ks < 2 * (size_t)std::max(1, sm_count) && nb / (2 * ks) >= 2) ks *= 2;
+    const int ks = k_splits(tiles_n * tiles_m, nb, sm_count);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)tiles_n, (unsigned)tiles_m, (unsigned)ks);
-    cfg.blockDim = dim3(THREADS);
+    cfg.blockDim = dim3((unsigned)(big ? 2 * bm : q8s::THREADS));
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -287,15 +480,27 @@ int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws
     attr[1].val.clusterDim.z = (unsigned)ks;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e;
     const int im = (int)m, ik = (int)k, in = (int)n;
-    if (pair) e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_STORE, true>, x, im, ik, wq, ws, bias, in, out, ks, sec);
-    else if (mode == LIN_ADD)
-        e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_ADD, false>, x, im, ik, wq, ws, bias, in, out, ks, sec);
-    else if (mode == LIN_GELU)
-        e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_GELU, false>, x, im, ik, wq, ws, bias, in, out, ks, sec);
-    else e = cudaLaunchKernelEx(&cfg, q8_gemm_kernel<LIN_STORE, false>, x, im, ik, wq, ws, bias, in, out, ks, sec);
-    return e == cudaSuccess ? 0 : -1;
+    auto go = [&](auto kern) {
+        return cudaLaunchKernelEx(&cfg, kern, x, im, ik, wq, ws, bias, in, out, ks, sec) == cudaSuccess ? 0 : -1;
+    };
+    using q8g::q8_gemm_kernel;
+    if (!big) {
+        if (pair) return go(q8s::q8_gemm_kernel<LIN_STORE, true>);
+        if (mode == LIN_ADD) return go(q8s::q8_gemm_kernel<LIN_ADD, false>);
+        if (mode == LIN_GELU) return go(q8s::q8_gemm_kernel<LIN_GELU, false>);
+        return go(q8s::q8_gemm_kernel<LIN_STORE, false>);
+    }
+    if (bm == 32) {
+        if (pair) return go(q8_gemm_kernel<LIN_STORE, true, 32>);
+        if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, false, 32>);
+        if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, false, 32>);
+        return go(q8_gemm_kernel<LIN_STORE, false, 32>);
+    }
+    if (pair) return go(q8_gemm_kernel<LIN_STORE, true, 64>);
+    if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, false, 64>);
+    if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, false, 64>);
+    return go(q8_gemm_kernel<LIN_STORE, false, 64>);
 }
 
 }  // namespace
