@@ -855,6 +855,18 @@ def run_kernel_case(args):
             st.qkv_q8(0, h, W, 2255, q_out=qo)
             ops.linear_q8_silu_mul(h.view(1, -1), L["w_gate"], L["w_up"], out=gate)
         work = f"{(1536 + 512) * 1536 * 1.125 / 1e6:.1f} + {2 * 8960 * 1536 * 1.125 / 1e6:.1f} MB of Q8 weights"
+    elif args.kernel_case == "q8_gateup64":
+        # the gate/up SiLU pair of a Qwen2.5-1.5B layer for 64 sequences (the tiled Q8 product)
+        m, n_ff, k = 64, 8960, 1536
+        xg = torch.randn(m, k, generator=g, device=dev)
+        qg = torch.randint(-127, 128, (n_ff, k), generator=g, device=dev, dtype=torch.int8)
+        qu = torch.randint(-127, 128, (n_ff, k), generator=g, device=dev, dtype=torch.int8)
+        sc = torch.rand(n_ff, k // 32, generator=g, device=dev) * 1e-3
+        og = torch.empty(m, n_ff, device=dev)
+
+        def fn():
+            ops.linear_q8_silu_mul(xg, (qg, sc), (qu, sc), out=og)
+        work = f"{2 * 2 * m * n_ff * k / 1e9:.2f} GFLOP, {2 * n_ff * k * 1.125 / 1e6:.1f} MB of Q8 weights per launch"
     elif args.kernel_case == "gemm_mlp2":
         # the MLP down-projection of 16 small.en windows into the f32 residual stream
         B, M, N, K = 16, 1500, 768, 3072
@@ -925,7 +937,7 @@ def main():
     ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64",
                                              "decode_tc_qwen_b1", "decode_whisper", "prefill_qwen",
                                              "q8_logits", "step_qwen15", "step_whisper_base", "pair_qwen15",
-                                             "gemm_mlp2", "encoder_small_en"],
+                                             "gemm_mlp2", "encoder_small_en", "q8_gateup64"],
                     default=None)
     args = ap.parse_args()
     if args.kernel_case:

@@ -174,6 +174,17 @@ def test_qkv_q8_d128_many_rows(env):
     run_qkv(torch, ops, B=1, H=6, Hkv=2, d=128, n_ctx=32, chunks=[9, 1], seed=3, bias=False)
 
 
+def test_qkv_q8_many_rows_tiled(env):
+    """16 or more rows per call run the pair on the tiled Q8 product: 16 sequences of one
+    token (32 x 64 tiles), then chunks of 60 and 64 tokens whose 64 x 128 tiles span two heads
+    (d 64) or one head (d 128); the next single-token call runs the 8-row path on the same
+    caches."""
+    torch, ops = env
+    run_qkv(torch, ops, B=16, H=4, Hkv=2, d=64, n_ctx=32, chunks=[1, 1], seed=4)
+    run_qkv(torch, ops, B=8, H=14, Hkv=2, d=64, n_ctx=128, chunks=[60, 1], seed=5)
+    run_qkv(torch, ops, B=4, H=14, Hkv=2, d=128, n_ctx=128, chunks=[64, 1], seed=6, bias=False)
+
+
 def device_model(ops, m):
     return ops.LlmWeightsQ8(m["layers"], m["embd"], None if m["output"] is m["embd"] else m["output"],
                             m["output_norm"], m["cfg"]["eps"])

@@ -148,6 +148,9 @@ int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const f
 int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, const float* sg, const float* bg,
                         const int8_t* wu, const float* su, const float* bu, size_t n_ff, float* out, int sm_count,
                         cudaStream_t st);
+struct PairParams;
+// The RoPE pair of q8_pair_launch on the same tiles.
+int q8_gemm_rope_launch(const PairParams& p, int sm_count, cudaStream_t st);
 struct PairParams {
     const float* x;  // [m][k], row t of the call is sequence t / n_tok, token t % n_tok
     int m, k;

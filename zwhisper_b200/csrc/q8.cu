@@ -533,7 +533,8 @@ int q8_linear_launch(const float* x, size_t m, size_t k, const int8_t* wq, const
 int q8_pair_launch(const PairParams& p0, int epi, cudaStream_t st) {
     if (p0.m == 0 || p0.n_pairs == 0) return 0;
     const int sms = sm_count_current();
-    // many rows of x: the SiLU pair on the register-tiled product
+    // many rows of x: the pairs on the register-tiled product
+    if (epi == PAIR_ROPE && p0.m >= 16) return q8_gemm_rope_launch(p0, sms, st);
     if (epi == PAIR_SILU && p0.m >= 16)
         return q8_gemm_silu_launch(p0.x, (size_t)p0.m, (size_t)p0.k, p0.wq[0], p0.ws[0], p0.bias[0], p0.wq[1], p0.ws[1],
                                    p0.bias[1], (size_t)p0.n_pairs, p0.out + (size_t)p0.m0 * p0.n_pairs, sms, st);

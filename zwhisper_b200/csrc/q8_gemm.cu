@@ -91,23 +91,103 @@ __device__ __forceinline__ void finish(float* out, const float* bias, int n, int
     *o = v;
 }
 
-// The second matrix of the SiLU pair, and its bias.
-struct Second {
-    const int8_t* wq;
-    const float* ws;
-    const float* bias;
-};
+// Pair modes: two output rows that one epilogue needs together share a thread.
+//   PE_SILU: row j of the gate matrix (the args' wq / ws / bias) and of pp.wq[1] (up).
+//   PE_ROPE: rows i and i + d/2 of one head of wq, wk or wv (pp.wq[0..2]); the epilogue of
+//            q8_pair_kernel's PAIR_ROPE (bias, rotation, q out, K^T scatter, V copy).
+enum { PE_NONE = 0, PE_SILU = 1, PE_ROPE = 2 };
+
+// Matrix (0 q, 1 k, 2 v) and row of pair pc's first (second: + d/2) row in PE_ROPE.
+__device__ __forceinline__ void rope_row(const PairParams& p, int pc, bool second, int& sec, int& row) {
+    const int half = p.d >> 1;
+    const int hh = pc / half, i0 = pc - hh * half;
+    sec = hh < p.n_head ? 0 : hh < p.n_head + p.n_head_kv ? 1 : 2;
+    const int head = sec == 0 ? hh : sec == 1 ? hh - p.n_head : hh - p.n_head - p.n_head_kv;
+    row = head * p.d + i0 + (second ? half : 0);
+}
+
+// Loader row wj of a tile of TBN columns starting at output n0: the matrix, its scales, the
+// row, and whether the row exists (outputs past n are not stored).
+template <int PE, int TBN>
+__device__ __forceinline__ void tile_row(int wj, int n0, int n, const int8_t* wq, const float* ws,
+                                         const PairParams& pp, const int8_t*& base, const float*& sbase, int& row,
+                                         bool& ok) {
+    if (PE == PE_NONE) {
+        row = n0 + wj;
+        ok = row < n;
+        base = wq;
+        sbase = ws;
+        return;
+    }
+    const bool second = wj >= TBN / 2;
+    const int pc = n0 + (second ? wj - TBN / 2 : wj);
+    ok = pc < n;
+    if (PE == PE_SILU) {
+        row = pc;
+        base = second ? pp.wq[1] : wq;
+        sbase = second ? pp.ws[1] : ws;
+    } else {
+        int sec;
+        rope_row(pp, ok ? pc : 0, second, sec, row);
+        base = pp.wq[sec];
+        sbase = pp.ws[sec];
+    }
+}
+
+// PAIR_ROPE's epilogue for x row r of the call and pair pc (q8_pair_kernel, q8.cu).
+__device__ __forceinline__ void finish_rope(const PairParams& p, int r, int pc, float va, float vb) {
+    int sec, ra;
+    rope_row(p, pc, false, sec, ra);
+    const int half = p.d >> 1, i = ra % p.d;
+    const float* bias = p.bias[sec];
+    if (bias) {
+        va = __fadd_rn(va, __ldg(bias + ra));
+        vb = __fadd_rn(vb, __ldg(bias + ra + half));
+    }
+    const int tok = p.m0 + r;
+    const int seq = tok / p.n_tok, t = tok - seq * p.n_tok;
+    const size_t pos = (size_t)p.n_past + t;
+    const size_t kvw = (size_t)p.n_head_kv * p.d;
+    if (sec == 2) {
+        float* cv = p.cache_v + (size_t)seq * p.cache_bs + pos * kvw + ra;
+        cv[0] = va;
+        cv[half] = vb;
+        return;
+    }
+    // separately rounded products and sums, as the reference's rope
+    const float c = p.cos_tab[pos * half + i], s = p.sin_tab[pos * half + i];
+    const float lo = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+    const float hi = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
+    if (sec == 0) {
+        float* qo = p.q_out + (size_t)tok * p.n_head * p.d + ra;
+        qo[0] = lo;
+        qo[half] = hi;
+    } else {
+        float* kt = p.cache_kt + (size_t)seq * p.cache_bs;
+        kt[(size_t)ra * p.n_ctx + pos] = lo;
+        kt[(size_t)(ra + half) * p.n_ctx + pos] = hi;
+    }
+}
+
+// The epilogue of one output pair.
+template <int PE>
+__device__ __forceinline__ void finish_two(float* out, const float* bias, const PairParams& pp, int n, int row, int col,
+                                           float a, float b) {
+    if (PE == PE_SILU) finish_pair(out, bias, pp.bias[1], n, row, col, a, b);
+    else finish_rope(pp, row, col, a, b);
+}
 
 // Tile column of output j (0..7) of thread tx: columns tx*4..+3 of each 64-column half (for
 // the SiLU pair the gate and the up half).
 __device__ __forceinline__ int tile_col(int tx, int j) { return (j < 4 ? 0 : BN / 2) + tx * 4 + (j & 3); }
 
-// MODE: LIN_STORE / LIN_ADD / LIN_GELU; PAIR: the SiLU pair (out [m][n], n = n_ff); BM: rows
-// of x per tile (32 or 64), threads = BM / 8 * 16.
-template <int MODE, bool PAIR, int BM>
+// MODE: LIN_STORE / LIN_ADD / LIN_GELU (PE_NONE); PE: a pair mode (n = the number of pairs);
+// BM: rows of x per tile (32 or 64), threads = BM / 8 * 16.
+template <int MODE, int PE, int BM>
 __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, int k, const int8_t* __restrict__ wq,
                                                         const float* __restrict__ ws, const float* __restrict__ bias,
-                                                        int n, float* out, int ks, Second sec) {
+                                                        int n, float* out, int ks, PairParams pp) {
+    constexpr bool PAIR = PE != PE_NONE;
     constexpr int THREADS = BM * 2;
     constexpr int XL = BM * BK / 4 / THREADS;    // x float4 per thread per block (4)
     constexpr int WL = BN * BK / 16 / THREADS;   // weight 16-byte pieces per thread per block
@@ -124,11 +204,12 @@ __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, 
 #pragma unroll
     for (int i = 0; i < WL; i++) {
         const int wj = (t + i * THREADS) >> 1;
-        const bool up = PAIR && wj >= BN / 2;      // this row comes from the up matrix
-        const int wn = n0 + (up ? wj - BN / 2 : wj);
-        wok[i] = wn < n;
-        wrow[i] = (up ? sec.wq : wq) + (size_t)(wok[i] ? wn : 0) * k;
-        wsc[i] = (up ? sec.ws : ws) + (size_t)(wok[i] ? wn : 0) * nb;
+        const int8_t* base;
+        const float* sbase;
+        int wn;
+        tile_row<PE, BN>(wj, n0, n, wq, ws, pp, base, sbase, wn, wok[i]);
+        wrow[i] = base + (size_t)(wok[i] ? wn : 0) * k;
+        wsc[i] = sbase + (size_t)(wok[i] ? wn : 0) * nb;
         // the weights are constants: their rows of this k range go to L2 before the wait
         if (wok[i] && ((t + i * THREADS) & 1) == 0)
             for (int off = b_beg * BK; off < b_end * BK; off += 128)
@@ -217,7 +298,7 @@ __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, 
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int col = n0 + tx * 4 + j;
-                    if (col < n) finish_pair(out, bias, sec.bias, n, row, col, acc[i][j], acc[i][4 + j]);
+                    if (col < n) finish_two<PE>(out, bias, pp, n, row, col, acc[i][j], acc[i][4 + j]);
                 }
             } else {
 #pragma unroll
@@ -247,7 +328,7 @@ __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, 
             if (PAIR) u = __fadd_rn(u, ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)));
         }
         if (row < m && col < n) {
-            if (PAIR) finish_pair(out, bias, sec.bias, n, row, col, v, u);
+            if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
             else finish<MODE>(out, bias, n, row, col, v);
         }
     }
@@ -275,20 +356,22 @@ struct Smem {
 using q8g::cluster_addr;
 using q8g::cluster_sync_all;
 using q8g::finish;
-using q8g::finish_pair;
+using q8g::finish_two;
 using q8g::ld_cluster;
-using q8g::Second;
+using q8g::PE_NONE;
+using q8g::tile_row;
 
 template <bool PAIR>
 __device__ __forceinline__ int tile_col(int tx, int j) {
     return PAIR ? (j < 2 ? tx * 2 + j : BN / 2 + tx * 2 + (j - 2)) : tx * 4 + j;
 }
 
-// MODE: LIN_STORE / LIN_ADD / LIN_GELU; PAIR: the SiLU pair (out [m][n], n = n_ff).
-template <int MODE, bool PAIR>
+// MODE: LIN_STORE / LIN_ADD / LIN_GELU (PE_NONE); PE: a pair mode.
+template <int MODE, int PE>
 __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m, int k, const int8_t* __restrict__ wq,
                                                           const float* __restrict__ ws, const float* __restrict__ bias,
-                                                          int n, float* out, int ks, Second sec) {
+                                                          int n, float* out, int ks, PairParams pp) {
+    constexpr bool PAIR = PE != PE_NONE;
     __shared__ __align__(16) Smem sm;
     const int t = threadIdx.x, ty = t >> 4, tx = t & 15;
     // a tile's first output column: 64 columns, or 32 gate / up pairs
@@ -298,11 +381,13 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
     // loader roles: x rows (t >> 3) and (t >> 3) + 16, four k at (t & 7) * 4; weight row t >> 1,
     // sixteen k at (t & 1) * 16
     const int xrow = t >> 3, xk = (t & 7) * 4, wj = t >> 1, wh = t & 1;
-    const bool up = PAIR && wj >= BN / 2;          // this loader's row comes from the up matrix
-    const int wn = PAIR ? n0 + (up ? wj - BN / 2 : wj) : n0 + wj;
-    const bool wrow_ok = wn < n;
-    const int8_t* wrow = (up ? sec.wq : wq) + (size_t)(wrow_ok ? wn : 0) * k;
-    const float* wsc = (up ? sec.ws : ws) + (size_t)(wrow_ok ? wn : 0) * nb;
+    const int8_t* base;
+    const float* sbase;
+    int wn;
+    bool wrow_ok;
+    tile_row<PE, BN>(wj, n0, n, wq, ws, pp, base, sbase, wn, wrow_ok);
+    const int8_t* wrow = base + (size_t)(wrow_ok ? wn : 0) * k;
+    const float* wsc = sbase + (size_t)(wrow_ok ? wn : 0) * nb;
     // the weights are constants: their rows of this k range go to L2 before the wait
     if (wrow_ok)
         for (int off = b_beg * BK + wh * 128; off < b_end * BK; off += 256)
@@ -399,7 +484,7 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
 #pragma unroll
                 for (int j = 0; j < 2; j++) {
                     const int col = n0 + tx * 2 + j;
-                    if (col < n) finish_pair(out, bias, sec.bias, n, row, col, acc[i][j], acc[i][2 + j]);
+                    if (col < n) finish_two<PE>(out, bias, pp, n, row, col, acc[i][j], acc[i][2 + j]);
                 }
             } else {
 #pragma unroll
@@ -428,7 +513,7 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
             if (PAIR) u = __fadd_rn(u, ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)));
         }
         if (row < m && col < n) {
-            if (PAIR) finish_pair(out, bias, sec.bias, n, row, col, v, u);
+            if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
             else finish<MODE>(out, bias, n, row, col, v);
         }
     }
@@ -449,10 +534,13 @@ int k_splits(size_t tiles, size_t nb, int sm_count) {
 }
 
 int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
-           int mode, bool pair, q8g::Second sec, float* out, int sm_count, cudaStream_t st) {
+           int mode, int pe, const PairParams& pp, float* out, int sm_count, cudaStream_t st) {
+    using namespace q8g;
+    const bool pair = pe != PE_NONE;
     if (m == 0 || n == 0) return 0;
-    if (k == 0 || k % q8g::BK || ((uintptr_t)x & 15) || ((uintptr_t)wq & 15) || (pair && ((uintptr_t)sec.wq & 15)))
-        return -1;
+    if (k == 0 || k % q8g::BK || ((uintptr_t)x & 15) || ((uintptr_t)wq & 15)) return -1;
+    for (int i = 0; i < (pe == PE_ROPE ? 3 : pe == PE_SILU ? 2 : 0); i++)
+        if (!pp.wq[i] || ((uintptr_t)pp.wq[i] & 15)) return -1;
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return -1;
     const size_t nb = k / q8g::BK;
     // the large tiles (32 or 64 rows x 128 columns) when the shape gives at least 64 of them
@@ -482,25 +570,28 @@ int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws
     cfg.numAttrs = 2;
     const int im = (int)m, ik = (int)k, in = (int)n;
     auto go = [&](auto kern) {
-        return cudaLaunchKernelEx(&cfg, kern, x, im, ik, wq, ws, bias, in, out, ks, sec) == cudaSuccess ? 0 : -1;
+        return cudaLaunchKernelEx(&cfg, kern, x, im, ik, wq, ws, bias, in, out, ks, pp) == cudaSuccess ? 0 : -1;
     };
     using q8g::q8_gemm_kernel;
     if (!big) {
-        if (pair) return go(q8s::q8_gemm_kernel<LIN_STORE, true>);
-        if (mode == LIN_ADD) return go(q8s::q8_gemm_kernel<LIN_ADD, false>);
-        if (mode == LIN_GELU) return go(q8s::q8_gemm_kernel<LIN_GELU, false>);
-        return go(q8s::q8_gemm_kernel<LIN_STORE, false>);
+        if (pe == PE_SILU) return go(q8s::q8_gemm_kernel<LIN_STORE, PE_SILU>);
+        if (pe == PE_ROPE) return go(q8s::q8_gemm_kernel<LIN_STORE, PE_ROPE>);
+        if (mode == LIN_ADD) return go(q8s::q8_gemm_kernel<LIN_ADD, PE_NONE>);
+        if (mode == LIN_GELU) return go(q8s::q8_gemm_kernel<LIN_GELU, PE_NONE>);
+        return go(q8s::q8_gemm_kernel<LIN_STORE, PE_NONE>);
     }
     if (bm == 32) {
-        if (pair) return go(q8_gemm_kernel<LIN_STORE, true, 32>);
-        if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, false, 32>);
-        if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, false, 32>);
-        return go(q8_gemm_kernel<LIN_STORE, false, 32>);
+        if (pe == PE_SILU) return go(q8_gemm_kernel<LIN_STORE, PE_SILU, 32>);
+        if (pe == PE_ROPE) return go(q8_gemm_kernel<LIN_STORE, PE_ROPE, 32>);
+        if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, PE_NONE, 32>);
+        if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, PE_NONE, 32>);
+        return go(q8_gemm_kernel<LIN_STORE, PE_NONE, 32>);
     }
-    if (pair) return go(q8_gemm_kernel<LIN_STORE, true, 64>);
-    if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, false, 64>);
-    if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, false, 64>);
-    return go(q8_gemm_kernel<LIN_STORE, false, 64>);
+    if (pe == PE_SILU) return go(q8_gemm_kernel<LIN_STORE, PE_SILU, 64>);
+    if (pe == PE_ROPE) return go(q8_gemm_kernel<LIN_STORE, PE_ROPE, 64>);
+    if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, PE_NONE, 64>);
+    if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, PE_NONE, 64>);
+    return go(q8_gemm_kernel<LIN_STORE, PE_NONE, 64>);
 }
 
 }  // namespace
@@ -509,14 +600,28 @@ int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws
 // q8_linear_launch. Returns -1 on a bad argument or a launch failure.
 int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
                    int mode, float* out, int sm_count, cudaStream_t st) {
-    return launch(x, m, k, wq, ws, bias, n, mode, false, q8g::Second{nullptr, nullptr, nullptr}, out, sm_count, st);
+    const PairParams none{};
+    return launch(x, m, k, wq, ws, bias, n, mode, q8g::PE_NONE, none, out, sm_count, st);
 }
 
 // out[m][n_ff] = silu(x . Wg^T + bg) * (x . Wu^T + bu), the SiLU pair of q8_pair_launch.
 int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, const float* sg, const float* bg,
                         const int8_t* wu, const float* su, const float* bu, size_t n_ff, float* out, int sm_count,
                         cudaStream_t st) {
-    return launch(x, m, k, wg, sg, bg, n_ff, LIN_STORE, true, q8g::Second{wu, su, bu}, out, sm_count, st);
+    PairParams pp{};
+    pp.wq[0] = wg;
+    pp.ws[0] = sg;
+    pp.bias[0] = bg;
+    pp.wq[1] = wu;
+    pp.ws[1] = su;
+    pp.bias[1] = bu;
+    return launch(x, m, k, wg, sg, bg, n_ff, LIN_STORE, q8g::PE_SILU, pp, out, sm_count, st);
+}
+
+// The RoPE pair of q8_pair_launch (q/k/v + bias + RoPE + K^T / V append) on the tiles.
+int q8_gemm_rope_launch(const PairParams& p, int sm_count, cudaStream_t st) {
+    return launch(p.x, (size_t)p.m, (size_t)p.k, p.wq[0], p.ws[0], nullptr, (size_t)p.n_pairs, LIN_STORE, q8g::PE_ROPE,
+                  p, nullptr, sm_count, st);
 }
 
 }  // namespace zwg
