@@ -103,3 +103,42 @@ def test_state_decode_after_reported_error(env):
         st.attn(0, q, 800, out=out)
         np.testing.assert_allclose(out.cpu().numpy().reshape(-1), want_for(st, kt, v, q, 801), atol=1e-4, rtol=0)
     st.close()
+
+
+def test_decoder_state_many_segments(env):
+    """32 windows x 8 heads = 256 segments, more than the SMs (whole segments per CTA, no
+    ticket): cross-attention over 1500 keys and self-attention over a growing cache through a
+    decoder state, each call against the oracle (src/decoder.zig:179-191), three cross calls
+    in a row."""
+    torch, _lib, ops = env
+    ops.set_math("f32")
+    B, ns, H, n_text, n_audio = 32, 512, 8, 64, 1500
+    st = ops.DecoderState(1, B, ns, H, n_text, n_audio)
+    g = torch.Generator(device="cuda:0")
+    g.manual_seed(21)
+    ck = torch.randn(B, n_audio, ns, generator=g, device="cuda:0")
+    cv = torch.randn(B, n_audio, ns, generator=g, device="cuda:0")
+    for w in range(B):
+        st.set_cross(0, w, ck[w], cv[w])
+    ckn, cvn = ck.cpu().numpy(), cv.cpu().numpy()
+    for _ in range(3):
+        q = torch.randn(B, 1, ns, generator=g, device="cuda:0")
+        out = st.cross_attn(0, q).cpu().numpy()
+        qn = q.cpu().numpy()
+        for b in (0, 13, 31):
+            want = A.attention(qn[b].reshape(-1), ckn[b].reshape(-1), cvn[b].reshape(-1), 1, n_audio, ns, H, False)
+            np.testing.assert_allclose(out[b].reshape(-1), want, atol=1e-4, rtol=0)
+    keys = np.zeros((B, n_text, ns), np.float32)
+    vals = np.zeros((B, n_text, ns), np.float32)
+    for n_past in range(0, 40, 13):
+        q = torch.randn(B, 1, ns, generator=g, device="cuda:0")
+        kn = torch.randn(B, 1, ns, generator=g, device="cuda:0")
+        vn = torch.randn(B, 1, ns, generator=g, device="cuda:0")
+        keys[:, n_past], vals[:, n_past] = kn.cpu().numpy()[:, 0], vn.cpu().numpy()[:, 0]
+        out = st.self_attn(0, q, kn, vn, n_past).cpu().numpy()
+        qn = q.cpu().numpy()
+        for b in (0, 31):
+            want = A.attention(qn[b].reshape(-1), keys[b, :n_past + 1].reshape(-1), vals[b, :n_past + 1].reshape(-1),
+                               1, n_past + 1, ns, H, True)
+            np.testing.assert_allclose(out[b].reshape(-1), want, atol=1e-4, rtol=0)
+    st.close()
