@@ -795,12 +795,14 @@ def run_kernel_case(args):
         def fn():
             ops.enc_attn_bf16(q, k, v, N_HEAD, out)
         work = f"{FLOP_PER_WINDOW_LAYER * B / 1e9:.1f} GFLOP per launch"
-    elif args.kernel_case in ("decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64", "decode_tc_qwen_b1"):
+    elif args.kernel_case in ("decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64", "decode_tc_qwen_b1",
+                              "decode_tc_qwen05"):
         B, H, Hkv, d, n_ctx, n_kv = {"decode_qwen": (16, 12, 2, 128, 2560, 2256),
                                      "decode_qwen05": (16, 14, 2, 64, 2560, 2128),
                                      "decode_qwen_b1": (1, 12, 2, 128, 2560, 2256),
                                      "decode_tc_qwen64": (64, 12, 2, 128, 2560, 2256),
-                                     "decode_tc_qwen_b1": (1, 12, 2, 128, 2560, 2256)}[args.kernel_case]
+                                     "decode_tc_qwen_b1": (1, 12, 2, 128, 2560, 2256),
+                                     "decode_tc_qwen05": (16, 14, 2, 64, 2560, 2128)}[args.kernel_case]
         if args.kernel_case.startswith("decode_tc"):
             ops.set_math("tf32")
         q = torch.randn(B, H * d, generator=g, device=dev)
@@ -937,7 +939,7 @@ def main():
     ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64",
                                              "decode_tc_qwen_b1", "decode_whisper", "prefill_qwen",
                                              "q8_logits", "step_qwen15", "step_whisper_base", "pair_qwen15",
-                                             "gemm_mlp2", "encoder_small_en", "q8_gateup64"],
+                                             "gemm_mlp2", "encoder_small_en", "q8_gateup64", "decode_tc_qwen05"],
                     default=None)
     args = ap.parse_args()
     if args.kernel_case:
