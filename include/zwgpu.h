@@ -178,7 +178,8 @@ ZWG_API int zwg_q8_quantize(const float* w, size_t n, size_t k, int8_t* q, float
 /* ops.linear with Q8 weights (src/ops.zig:280-306 -> gemm.ntBlockQ, src/gemm.zig:268-351):
  * out[m][n] = x[m][k] . W[n][k]^T + bias[n], W = q * scale per block of 32; bias may be NULL.
  * Device pointers; x [m][k] and out [m][n] f32 row-major, k a multiple of 32, x and q
- * 16-byte aligned. f32 arithmetic; the weight bytes are streamed once per 8 rows of x. */
+ * 16-byte aligned. f32 arithmetic; up to 15 rows of x stream the weight bytes once per 8
+ * rows, 16 or more run as a register-tiled product (the weights read once per tile). */
 ZWG_API int zwg_linear_q8(const float* x, size_t m, size_t k, const int8_t* q, const float* scales,
                           const float* bias, size_t n, float* out, void* stream);
 

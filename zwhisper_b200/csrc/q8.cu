@@ -12,7 +12,8 @@
 //   absmax)), -127, 127) with the reference's f32 operations and round-half-away, so the
 //   int8 values and scales are bit-identical to Q8.quantize.
 // q8_linear_kernel<MR, RW, KS, UNR>: the decode-shaped product (m <= 8 rows of x per launch;
-//   larger m in chunks of 8). The weight bytes are the traffic (1.125 B per weight with the
+//   9-15 rows in chunks of 8; 16 or more rows go to the register-tiled product of
+//   q8_gemm.cu, pairs included). The weight bytes are the traffic (1.125 B per weight with the
 //   scales), so the kernel streams them once: a warp owns RW weight rows over 1/KS of k
 //   (KS warps of a CTA share a row set and add their partial sums through shared memory in
 //   a fixed order), lane l reads 16 (8 for MR = 8) consecutive int8 of each row per step
@@ -22,8 +23,7 @@
 //   and scales it by the block's scale. Warp shuffles sum the lanes; the bias is added on
 //   the way out; the epilogue then stores, adds into `out` (the residual: ops.linear then
 //   ops.add, src/llm.zig:203-204, 209-210; src/decoder.zig:185-186) or applies GELU
-//   (ops.linear then ops.gelu, src/decoder.zig:197-198). One launch covers all full chunks of
-//   8 x rows (grid.y), the remainder a second.
+//   (ops.linear then ops.gelu, src/decoder.zig:197-198).
 // q8_pair_kernel<MR, RP, KS, UNR, EPI>: the same dot products for two matrices' rows at once, a warp
 //   owning RP pairs of rows whose outputs one epilogue combines:
 //   - PAIR_ROPE: rows i and i + d/2 of one head of the q, k or v projection
