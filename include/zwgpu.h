@@ -207,7 +207,9 @@ ZWG_API int zwg_cross_kv_set(zwg_dec_state* st, size_t layer, size_t window, con
                              const float* v, void* stream);
 /* One decoder step's attention for every window (src/decoder.zig:179-191), q and out
  * [n_batch][n][n_state]. ZWG_DEC_SELF: k_new, v_new [n_batch][n][n_state] are written at
- * rows n_past.. of the layer's cache, then causal attention over n_past + n keys.
+ * rows n_past.. of the layer's cache, then causal attention over n_past + n keys; with both
+ * NULL those rows are taken as already written (by a kernel of the caller's on the same
+ * stream, through zwg_dec_state_cache's pointers).
  * ZWG_DEC_CROSS: attention over the window's cross K/V (k_new, v_new, n_past unused). */
 #define ZWG_DEC_SELF 0
 #define ZWG_DEC_CROSS 1

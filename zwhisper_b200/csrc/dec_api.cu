@@ -167,10 +167,31 @@ int zwg_dec_forward_q8(zwg_dec_state* st, const zwg_dec_weights* w, const int32_
         const zwg_dec_layer_weights& L = w->layers[l];
         // masked self-attention over the cache (src/decoder.zig:180-186)
         if ((rc = ln(x, ns, M, ns, L.attn_ln_w, L.attn_ln_b, sc.h, ns, s))) return rc;
-        if ((rc = lin(sc.h, M, ns, L.q, L.q_b, ns, zwg::LIN_STORE, sc.q, s, "q launch"))) return rc;
-        if ((rc = lin(sc.h, M, ns, L.k, nullptr, ns, zwg::LIN_STORE, sc.k, s, "k launch"))) return rc;
-        if ((rc = lin(sc.h, M, ns, L.v, L.v_b, ns, zwg::LIN_STORE, sc.v, s, "v launch"))) return rc;
-        if ((rc = zwg_dec_step_attn(st, l, ZWG_DEC_SELF, sc.q, sc.k, sc.v, n_past, n, sc.attn, stream))) return rc;
+        if (M >= 16) {
+            // q, k and v in one tiled product whose epilogue appends k and v to the caches
+            zwg::PairParams p{};
+            p.x = sc.h;
+            p.m = (int)M;
+            p.k = (int)ns;
+            p.wq[0] = L.q.q; p.wq[1] = L.k.q; p.wq[2] = L.v.q;
+            p.ws[0] = L.q.scales; p.ws[1] = L.k.scales; p.ws[2] = L.v.scales;
+            p.bias[0] = L.q_b; p.bias[2] = L.v_b;
+            p.d = (int)ns;
+            p.n_tok = (int)n;
+            p.n_past = (int)n_past;
+            p.q_out = sc.q;
+            p.cache_kt = st->self_k[l];
+            p.cache_v = st->self_v[l];
+            p.cache_bs = st->n_text_ctx * ns;
+            if (zwg::q8_gemm_qkv_launch(p, c->sm_count, s)) return cuda_fail("qkv launch", cudaGetLastError());
+            rc = zwg_dec_step_attn(st, l, ZWG_DEC_SELF, sc.q, nullptr, nullptr, n_past, n, sc.attn, stream);
+        } else {
+            if ((rc = lin(sc.h, M, ns, L.q, L.q_b, ns, zwg::LIN_STORE, sc.q, s, "q launch"))) return rc;
+            if ((rc = lin(sc.h, M, ns, L.k, nullptr, ns, zwg::LIN_STORE, sc.k, s, "k launch"))) return rc;
+            if ((rc = lin(sc.h, M, ns, L.v, L.v_b, ns, zwg::LIN_STORE, sc.v, s, "v launch"))) return rc;
+            rc = zwg_dec_step_attn(st, l, ZWG_DEC_SELF, sc.q, sc.k, sc.v, n_past, n, sc.attn, stream);
+        }
+        if (rc) return rc;
         if ((rc = lin(sc.attn, M, ns, L.o, L.o_b, ns, zwg::LIN_ADD, x, s, "o launch"))) return rc;
         // cross-attention over the audio (src/decoder.zig:188-193)
         if ((rc = ln(x, ns, M, ns, L.cross_ln_w, L.cross_ln_b, sc.h, ns, s))) return rc;

@@ -151,6 +151,10 @@ int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, co
 struct PairParams;
 // The RoPE pair of q8_pair_launch on the same tiles.
 int q8_gemm_rope_launch(const PairParams& p, int sm_count, cudaStream_t st);
+// The Whisper decoder's q/k/v projections as one tiled product (16+ rows of x): q to
+// p.q_out, k and v appended to the decoder caches p.cache_kt / p.cache_v (window w at
+// w * p.cache_bs, row n_past + t of p.n_tok, p.d = n_state).
+int q8_gemm_qkv_launch(const PairParams& p, int sm_count, cudaStream_t st);
 struct PairParams {
     const float* x;  // [m][k], row t of the call is sequence t / n_tok, token t % n_tok
     int m, k;

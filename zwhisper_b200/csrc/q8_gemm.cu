@@ -95,7 +95,12 @@ __device__ __forceinline__ void finish(float* out, const float* bias, int n, int
 //   PE_SILU: row j of the gate matrix (the args' wq / ws / bias) and of pp.wq[1] (up).
 //   PE_ROPE: rows i and i + d/2 of one head of wq, wk or wv (pp.wq[0..2]); the epilogue of
 //            q8_pair_kernel's PAIR_ROPE (bias, rotation, q out, K^T scatter, V copy).
-enum { PE_NONE = 0, PE_SILU = 1, PE_ROPE = 2 };
+// And one column mode that is not a pair:
+//   PE_QKV:  the Whisper decoder's self-attention projections as one product over the 3 d
+//            columns of wq, wk and wv (pp.wq[0..2], d = pp.d rows each, biases pp.bias[]):
+//            q to pp.q_out, k and v appended to the decoder caches (pp.cache_kt / cache_v,
+//            window w at w * cache_bs, position n_past + t, row stride d).
+enum { PE_NONE = 0, PE_SILU = 1, PE_ROPE = 2, PE_QKV = 3 };
 
 // Matrix (0 q, 1 k, 2 v) and row of pair pc's first (second: + d/2) row in PE_ROPE.
 __device__ __forceinline__ void rope_row(const PairParams& p, int pc, bool second, int& sec, int& row) {
@@ -117,6 +122,15 @@ __device__ __forceinline__ void tile_row(int wj, int n0, int n, const int8_t* wq
         ok = row < n;
         base = wq;
         sbase = ws;
+        return;
+    }
+    if (PE == PE_QKV) {
+        const int vc = n0 + wj;
+        ok = vc < n;
+        const int sel = ok ? vc / pp.d : 0;
+        row = ok ? vc - sel * pp.d : 0;
+        base = pp.wq[sel];
+        sbase = pp.ws[sel];
         return;
     }
     const bool second = wj >= TBN / 2;
@@ -169,6 +183,27 @@ __device__ __forceinline__ void finish_rope(const PairParams& p, int r, int pc, 
     }
 }
 
+// PE_QKV's epilogue for x row r of the call (window r / n_tok, token r % n_tok) and column vc.
+__device__ __forceinline__ void finish_qkv(const PairParams& p, int r, int vc, float v) {
+    const int sel = vc / p.d, col = vc - sel * p.d;
+    if (p.bias[sel]) v = __fadd_rn(v, __ldg(p.bias[sel] + col));
+    if (sel == 0) {
+        p.q_out[(size_t)r * p.d + col] = v;
+        return;
+    }
+    const int seq = r / p.n_tok, t = r - seq * p.n_tok;
+    float* cache = sel == 1 ? p.cache_kt : p.cache_v;
+    cache[(size_t)seq * p.cache_bs + ((size_t)p.n_past + t) * p.d + col] = v;
+}
+
+// The epilogue of one output column (not a pair).
+template <int MODE, int PE>
+__device__ __forceinline__ void finish_one(float* out, const float* bias, const PairParams& pp, int n, int row, int col,
+                                           float v) {
+    if (PE == PE_QKV) finish_qkv(pp, row, col, v);
+    else finish<MODE>(out, bias, n, row, col, v);
+}
+
 // The epilogue of one output pair.
 template <int PE>
 __device__ __forceinline__ void finish_two(float* out, const float* bias, const PairParams& pp, int n, int row, int col,
@@ -187,7 +222,7 @@ template <int MODE, int PE, int BM>
 __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, int k, const int8_t* __restrict__ wq,
                                                         const float* __restrict__ ws, const float* __restrict__ bias,
                                                         int n, float* out, int ks, PairParams pp) {
-    constexpr bool PAIR = PE != PE_NONE;
+    constexpr bool PAIR = PE == PE_SILU || PE == PE_ROPE;
     constexpr int THREADS = BM * 2;
     constexpr int XL = BM * BK / 4 / THREADS;    // x float4 per thread per block (4)
     constexpr int WL = BN * BK / 16 / THREADS;   // weight 16-byte pieces per thread per block
@@ -304,7 +339,7 @@ __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, 
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     const int col = n0 + tile_col(tx, j);
-                    if (col < n) finish<MODE>(out, bias, n, row, col, acc[i][j]);
+                    if (col < n) finish_one<MODE, PE>(out, bias, pp, n, row, col, acc[i][j]);
                 }
             }
         }
@@ -329,7 +364,7 @@ __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, 
         }
         if (row < m && col < n) {
             if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
-            else finish<MODE>(out, bias, n, row, col, v);
+            else finish_one<MODE, PE>(out, bias, pp, n, row, col, v);
         }
     }
     // no CTA leaves while another may still read its partial tile
@@ -356,9 +391,12 @@ struct Smem {
 using q8g::cluster_addr;
 using q8g::cluster_sync_all;
 using q8g::finish;
+using q8g::finish_one;
 using q8g::finish_two;
 using q8g::ld_cluster;
 using q8g::PE_NONE;
+using q8g::PE_ROPE;
+using q8g::PE_SILU;
 using q8g::tile_row;
 
 template <bool PAIR>
@@ -371,7 +409,7 @@ template <int MODE, int PE>
 __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m, int k, const int8_t* __restrict__ wq,
                                                           const float* __restrict__ ws, const float* __restrict__ bias,
                                                           int n, float* out, int ks, PairParams pp) {
-    constexpr bool PAIR = PE != PE_NONE;
+    constexpr bool PAIR = PE == PE_SILU || PE == PE_ROPE;
     __shared__ __align__(16) Smem sm;
     const int t = threadIdx.x, ty = t >> 4, tx = t & 15;
     // a tile's first output column: 64 columns, or 32 gate / up pairs
@@ -490,7 +528,7 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int col = n0 + tx * 4 + j;
-                    if (col < n) finish<MODE>(out, bias, n, row, col, acc[i][j]);
+                    if (col < n) finish_one<MODE, PE>(out, bias, pp, n, row, col, acc[i][j]);
                 }
             }
         }
@@ -514,7 +552,7 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
         }
         if (row < m && col < n) {
             if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
-            else finish<MODE>(out, bias, n, row, col, v);
+            else finish_one<MODE, PE>(out, bias, pp, n, row, col, v);
         }
     }
     // no CTA leaves while another may still read its partial tile
@@ -536,10 +574,10 @@ int k_splits(size_t tiles, size_t nb, int sm_count) {
 int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
            int mode, int pe, const PairParams& pp, float* out, int sm_count, cudaStream_t st) {
     using namespace q8g;
-    const bool pair = pe != PE_NONE;
+    const bool pair = pe == PE_SILU || pe == PE_ROPE;
     if (m == 0 || n == 0) return 0;
     if (k == 0 || k % q8g::BK || ((uintptr_t)x & 15) || ((uintptr_t)wq & 15)) return -1;
-    for (int i = 0; i < (pe == PE_ROPE ? 3 : pe == PE_SILU ? 2 : 0); i++)
+    for (int i = 0; i < (pe == PE_ROPE || pe == PE_QKV ? 3 : pe == PE_SILU ? 2 : 0); i++)
         if (!pp.wq[i] || ((uintptr_t)pp.wq[i] & 15)) return -1;
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return -1;
     const size_t nb = k / q8g::BK;
@@ -576,6 +614,7 @@ int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws
     if (!big) {
         if (pe == PE_SILU) return go(q8s::q8_gemm_kernel<LIN_STORE, PE_SILU>);
         if (pe == PE_ROPE) return go(q8s::q8_gemm_kernel<LIN_STORE, PE_ROPE>);
+        if (pe == PE_QKV) return go(q8s::q8_gemm_kernel<LIN_STORE, PE_QKV>);
         if (mode == LIN_ADD) return go(q8s::q8_gemm_kernel<LIN_ADD, PE_NONE>);
         if (mode == LIN_GELU) return go(q8s::q8_gemm_kernel<LIN_GELU, PE_NONE>);
         return go(q8s::q8_gemm_kernel<LIN_STORE, PE_NONE>);
@@ -583,12 +622,14 @@ int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws
     if (bm == 32) {
         if (pe == PE_SILU) return go(q8_gemm_kernel<LIN_STORE, PE_SILU, 32>);
         if (pe == PE_ROPE) return go(q8_gemm_kernel<LIN_STORE, PE_ROPE, 32>);
+        if (pe == PE_QKV) return go(q8_gemm_kernel<LIN_STORE, PE_QKV, 32>);
         if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, PE_NONE, 32>);
         if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, PE_NONE, 32>);
         return go(q8_gemm_kernel<LIN_STORE, PE_NONE, 32>);
     }
     if (pe == PE_SILU) return go(q8_gemm_kernel<LIN_STORE, PE_SILU, 64>);
     if (pe == PE_ROPE) return go(q8_gemm_kernel<LIN_STORE, PE_ROPE, 64>);
+    if (pe == PE_QKV) return go(q8_gemm_kernel<LIN_STORE, PE_QKV, 64>);
     if (mode == LIN_ADD) return go(q8_gemm_kernel<LIN_ADD, PE_NONE, 64>);
     if (mode == LIN_GELU) return go(q8_gemm_kernel<LIN_GELU, PE_NONE, 64>);
     return go(q8_gemm_kernel<LIN_STORE, PE_NONE, 64>);
@@ -616,6 +657,13 @@ int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, co
     pp.ws[1] = su;
     pp.bias[1] = bu;
     return launch(x, m, k, wg, sg, bg, n_ff, LIN_STORE, q8g::PE_SILU, pp, out, sm_count, st);
+}
+
+// The Whisper decoder's q/k/v projections in one product (PE_QKV): p.x [m][p.k], p.wq/ws/bias
+// [3], p.d = n_state, q to p.q_out, k / v rows appended to p.cache_kt / p.cache_v.
+int q8_gemm_qkv_launch(const PairParams& p, int sm_count, cudaStream_t st) {
+    return launch(p.x, (size_t)p.m, (size_t)p.k, p.wq[0], p.ws[0], nullptr, (size_t)3 * p.d, LIN_STORE, q8g::PE_QKV,
+                  p, nullptr, sm_count, st);
 }
 
 // The RoPE pair of q8_pair_launch (q/k/v + bias + RoPE + K^T / V append) on the tiles.

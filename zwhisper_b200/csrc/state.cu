@@ -173,16 +173,19 @@ int zwg_dec_step_attn(zwg_dec_state* st, size_t layer, int kind, const float* q,
     zwg_batch b;
     const float *kp, *vp;
     if (kind == ZWG_DEC_SELF) {
-        if (!k_new || !v_new) return fail("dec_step_attn: null k_new/v_new");
+        if (!k_new != !v_new) return fail("dec_step_attn: k_new and v_new must both be given or both be null");
         if (n_past + n > st->n_text_ctx) return fail("dec_step_attn: context full (%zu + %zu > %zu)", n_past, n, st->n_text_ctx);
-        // the new rows land at n_past.. of every window's cache (src/decoder.zig:182-183)
-        const size_t row_bytes = n * ns * sizeof(float), pitch = st->n_text_ctx * ns * sizeof(float);
-        cudaError_t e = cudaMemcpy2DAsync(st->self_k[layer] + n_past * ns, pitch, k_new, row_bytes, row_bytes, nb,
-                                          cudaMemcpyDefault, s);
-        if (e == cudaSuccess)
-            e = cudaMemcpy2DAsync(st->self_v[layer] + n_past * ns, pitch, v_new, row_bytes, row_bytes, nb,
-                                  cudaMemcpyDefault, s);
-        if (e != cudaSuccess) return cuda_fail("dec_step_attn append", e);
+        // the new rows land at n_past.. of every window's cache (src/decoder.zig:182-183);
+        // both null: the caller's kernel has written them there already
+        if (k_new) {
+            const size_t row_bytes = n * ns * sizeof(float), pitch = st->n_text_ctx * ns * sizeof(float);
+            cudaError_t e = cudaMemcpy2DAsync(st->self_k[layer] + n_past * ns, pitch, k_new, row_bytes, row_bytes, nb,
+                                              cudaMemcpyDefault, s);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(st->self_v[layer] + n_past * ns, pitch, v_new, row_bytes, row_bytes, nb,
+                                      cudaMemcpyDefault, s);
+            if (e != cudaSuccess) return cuda_fail("dec_step_attn append", e);
+        }
         sh = mha(n, n_past + n, ns, st->n_head, true);
         b = zwg_batch{nb, n * ns, st->n_text_ctx * ns, st->n_text_ctx * ns, n * ns};
         kp = st->self_k[layer];
