@@ -55,6 +55,7 @@ namespace enc_tc {
 
 constexpr int BM = 128;        // query rows per tile
 constexpr int BN = 128;        // keys per tile
+static_assert(BN == 128, "a softmax row is one 128-column TMEM load and one 64-column store");
 constexpr int D = 64;          // head dim
 constexpr int NS = 3;          // K/V pipeline stages
 constexpr int THREADS = 384;   // 12 warps: control warpgroup + two softmax warpgroups
@@ -286,13 +287,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!(ok = mbar_wait_warp(&sm.s_full[t], gj & 1, err))) break;
                 tc_fence_after();
                 uint32_t sr[BN];
-#pragma unroll
-                for (int cc = 0; cc < BN / 32; cc++) {
-                    uint32_t tmp[32];
-                    tmem_ld32(s_addr + cc * 32, tmp);
-#pragma unroll
-                    for (int i = 0; i < 32; i++) sr[cc * 32 + i] = tmp[i];
-                }
+                tmem_ld128(s_addr, sr);  // the row's 128 scores, one load
                 tmem_ld_wait();
                 // the scores are in registers: the next S may be written over them
                 tc_fence_before();
@@ -358,13 +353,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         tmem_st32(o_addr + cc * 32, o);
                     }
                 }
-#pragma unroll
-                for (int cc = 0; cc < BN / 32; cc++) {
-                    uint32_t q16[16];
-#pragma unroll
-                    for (int i = 0; i < 16; i++) q16[i] = pk[cc * 16 + i];
-                    tmem_st16(p_addr + cc * 16, q16);
-                }
+tmem_st64(p_addr, pk);  // the row's 64 bf16 pairs, one store
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&sm.p_full[t]);
