@@ -5,10 +5,12 @@
 //
 // At 16-64 rows (a decoder step over 32 windows, an LLM step over 64 sequences, the 1500 rows
 // of setAudio) the weight bytes are read once per tile instead of once per 8 rows, and the
-// work is f32 FMA: a register-tiled product, CTA tile 32 or 64 rows x 128 columns, 8 x 8
-// outputs per thread (shapes with fewer than 64 such tiles take 32 x 64 tiles, below). Per 32-wide k block the CTA stages x (k-major) and the dequantized
-// weights (k-major) in shared memory, double-buffered through registers; a thread's k step
-// is four 16-byte shared loads for 64 FMAs.
+// work is f32 FMA: a register-tiled product. Shapes with at least 64 tiles of 32 or 64 rows
+// x 128 columns take those (q8g below: 8 x 8 outputs per thread, the dequantized weights
+// staged, four 16-byte shared loads per 64 FMAs); the others take 32 x 64 tiles (q8s: 4 x 4
+// outputs per thread, the block's dots formed unscaled and added times the block's scales).
+// Per 32-wide k block a CTA stages x and the weights k-major in shared memory,
+// double-buffered through registers.
 //
 // Split-K without a workspace: when the tiles alone would leave SMs idle, a cluster of ks
 // CTAs (1 x 1 x ks) takes one tile, each CTA a contiguous range of k blocks; the CTAs then
@@ -17,10 +19,11 @@
 // the epilogue. The kernel has no spin waits: only block and cluster barriers, which every
 // thread reaches.
 //
-// The SiLU pair (the gate and up projections and ops.siluMul of an LLM layer, src/llm.zig:
-// 206-208, src/ops.zig:435-440) runs on the same tiles: a tile's 128 columns are 64 gate rows
-// and the same 64 up rows, a thread owns four of each, and the epilogue writes
-// gate / (1 + exp(-gate)) * up.
+// Fused modes on the same tiles (the pair kernels of q8.cu for many rows, and one more): the
+// SiLU pair (gate and up, src/llm.zig:206-208) and the RoPE pair (q/k/v + bias + rotation +
+// cache append, src/llm.zig:179-190), a thread owning the same columns of both row sets; and
+// the Whisper decoder's q/k/v as one product whose epilogue appends k and v to the caches
+// (src/decoder.zig:180-183).
 //
 // Launched as a programmatic dependent (chain.cuh): the weight rows of the CTA's k range are
 // prefetched into L2 before the wait for the kernel that wrote x.
