@@ -37,6 +37,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -364,17 +365,33 @@ int gemm_f16_launch(const GemmParams& p, int sm_count, int* err, cudaStream_t st
     g.k_steps = (p.K + BK - 1) / BK;
     g.total = (long long)g.m_pairs * g.n_batch * g.n_tiles;
     auto go = [&](auto kern) -> int {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
-            return -1;
-        // as many pairs as can be resident at once (the SMs of a cluster must share a GPC)
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * (unsigned)std::max(1, sm_count / 2));
-        cfg.blockDim = dim3(THREADS);
-        cfg.dynamicSmemBytes = SMEM_BYTES;
+        // once per device and kernel: the shared-memory opt-in and the number of CTA pairs
+        // that can be resident at once (the SMs of a cluster must share a GPC)
+        static std::mutex mu;
+        static std::map<std::pair<int, const void*>, int> pairs_of;
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return -1;
         int max_pairs = 0;
-        if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs < 1)
-            max_pairs = std::max(1, sm_count / 2);
-        cudaGetLastError();
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kern));
+            const auto it = pairs_of.find(key);
+            if (it != pairs_of.end()) {
+                max_pairs = it->second;
+            } else {
+                if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) !=
+                    cudaSuccess)
+                    return -1;
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(2 * (unsigned)std::max(1, sm_count / 2));
+                cfg.blockDim = dim3(THREADS);
+                cfg.dynamicSmemBytes = SMEM_BYTES;
+                if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs < 1)
+                    max_pairs = std::max(1, sm_count / 2);
+                cudaGetLastError();
+                pairs_of[key] = max_pairs;
+            }
+        }
         const int grid = 2 * (int)std::min<long long>(g.total, max_pairs);
         kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mw, g, p.e, err);
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
