@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <set>
 
 #include "chain.cuh"
 #include "common.cuh"
@@ -674,8 +675,20 @@ static int launch_d(const DecodeParams& p, size_t n_batch, int rmax, int grid, i
     geo.mode = mode;
     geo.pieces = pieces;
     auto go = [&](auto kern, size_t smem, int threads) -> int {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return -1;
+        // the shared-memory opt-in, once per device and kernel
+        static std::mutex mu;
+        static std::set<std::pair<int, const void*>> opted;
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kern));
+            if (!opted.count(key)) {
+                if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+                    return -1;
+                opted.insert(key);
+            }
+        }
         if (launch_chained_smem(kern, dim3(grid), dim3(threads), smem, st, mk, mv, p, geo, counters, err) != cudaSuccess)
             return -1;
         return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
