@@ -29,3 +29,17 @@ def test_reference_arm_json_line():
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert d["config"]["workload"]
+
+
+def test_reference_arm_two_ranks_prints_once():
+    """Launched the way the driver launches N > 1 (torchrun, 127.0.0.1): rank 0 alone runs
+    and prints the reference line; the other rank exits 0 without work."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+           "127.0.0.1", "--master-port", "29561", "bench.py", "--impl", "reference", "--gpus", "2", "--steps", "1",
+           "--warmup", "3"]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout[-2000:]
+    assert json.loads(lines[0])["impl"] == "reference"
