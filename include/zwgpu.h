@@ -140,9 +140,10 @@ ZWG_API int zwg_attention_dev(const zwg_attn_shape* sh, const zwg_batch* b, cons
  * rules: decode shapes only (d in {32, 64, 128}, n_q * n_head / n_head_kv <= 8); a call
  * whose partials exceed 4 MiB returns ZWG_ERROR with a message and launches nothing;
  * every device that loads the library holds the 4 MiB until exit; the first call on a
- * device looks up the array's device address (make it before any stream capture); all
- * calls share the array, so calls that overlap on the GPU race: keep one device's calls
- * on one stream or ordered. Needs no zwg_init. */
+ * device looks up the array's device address (make it before any stream capture), and
+ * the first call after a device reset looks it up again; all calls share the array, so
+ * calls that overlap on the GPU race: keep one device's calls on one stream or ordered.
+ * Shapes are checked as zwg_attention_dev checks them. Needs no zwg_init. */
 ZWG_API int zwg_attention_dev_noalloc(const zwg_attn_shape* sh, const zwg_batch* b, const float* q,
                                       const float* k, const float* v, float* out, void* stream);
 

@@ -78,5 +78,6 @@ def test_device_roundings_explain_the_encoder_tolerance():
     want = W.encode(Wd, hp, mel, 0)
     got = encode_device_rounding(Wd, hp, mel)
     err = float(np.abs(got - want).max())
-    # measured 6.99e-4 here against the device's 7.3e-4; inside the GPU test's 5e-3 bound
-    assert 1e-4 < err < 5e-3, err
+    # measured 6.99e-4 here against the device's 7.3e-4 (tests/test_gpu_whisper_pipeline.py):
+    # the bound holds the restatement to within about 2x of that figure
+    assert 3e-4 < err < 1.5e-3, err

@@ -13,7 +13,10 @@
 // exits. Host code cannot use the array's name as a device address (on the host it names a
 // stand-in object), so the device address is looked up with cudaGetSymbolAddress once per
 // device, with that device current, on the first call made on that device. Make that first
-// call on each device before any stream capture begins.
+// call on each device before any stream capture begins. The address is remembered together
+// with the CUDA context it belongs to: after a device reset (cudaDeviceReset, or a reset of
+// the primary context by other code in the process) the module is loaded again and the
+// array may move, so the next call sees a new context and looks the address up again.
 //
 // All calls on a device share the one array, and the array keeps whatever the previous
 // call left in it. Nothing in it has to start at zero: each call writes every partial slot
@@ -22,9 +25,11 @@
 // them) use the same array and race; issue calls for one device on one stream, or order
 // them.
 #include "../../include/zwgpu.h"
+#include "api_internal.h"
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -36,23 +41,55 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
 namespace {
 
-std::mutex g_mu;
-float* g_scratch_ptr[64] = {};
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 
-// Device address of the array on the current device; looked up once per device.
-int scratch_for_current_device(float** out) {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return zwg::set_last_error_cuda("cudaGetDevice", e);
-    if (dev < 0 || dev >= 64) return zwg::set_last_error("device index out of range");
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_ptr[dev]) {
+// cuCtxGetCurrent through the runtime's driver entry point (no link against libcuda).
+CtxGetCurrentFn ctx_get_current_fn() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p) return zwg::set_last_error_cuda("cudaGetSymbolAddress(scratch)", e);
-        g_scratch_ptr[dev] = static_cast<float*>(p);
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (CtxGetCurrentFn)p;
+    });
+    return fn;
+}
+
+struct ScratchSlot {
+    CUcontext ctx = nullptr;
+    float* ptr = nullptr;
+};
+
+std::mutex g_mu;
+ScratchSlot g_slots[64];
+
+// Device address of the array in the current device's current context; looked up on the
+// first call in that context.
+int scratch_for_current_device(int dev, float** out) {
+    if (dev < 0 || dev >= 64) return zwg::set_last_error("device index out of range");
+    CtxGetCurrentFn get = ctx_get_current_fn();
+    if (!get) return zwg::set_last_error("cuCtxGetCurrent is not available from the driver");
+    CUcontext ctx = nullptr;
+    if (get(&ctx) != CUDA_SUCCESS) return zwg::set_last_error("cuCtxGetCurrent failed");
+    if (!ctx) {
+        // nothing has used the device on this thread yet: cudaSetDevice makes its primary
+        // context current (it allocates no memory)
+        cudaError_t e = cudaSetDevice(dev);
+        if (e != cudaSuccess) return zwg::set_last_error_cuda("cudaSetDevice", e);
+        if (get(&ctx) != CUDA_SUCCESS || !ctx) return zwg::set_last_error("no current CUDA context");
     }
-    *out = g_scratch_ptr[dev];
+    std::lock_guard<std::mutex> lk(g_mu);
+    ScratchSlot& slot = g_slots[dev];
+    if (slot.ctx != ctx || !slot.ptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) return zwg::set_last_error_cuda("cudaGetSymbolAddress(scratch)", e);
+        slot.ctx = ctx;
+        slot.ptr = static_cast<float*>(p);
+    }
+    *out = slot.ptr;
     return ZWG_OK;
 }
 
@@ -60,14 +97,10 @@ int scratch_for_current_device(float** out) {
 
 extern "C" int zwg_attention_dev_noalloc(const zwg_attn_shape* sh, const zwg_batch* b, const float* q,
                                          const float* k, const float* v, float* out, void* stream) {
-    if (!sh) return zwg::set_last_error("null shape");
-    if (sh->n_head == 0 || sh->n_head_kv == 0 || sh->n_head % sh->n_head_kv)
-        return zwg::set_last_error("n_head must be a positive multiple of n_head_kv");
-    if (sh->causal && sh->n_kv < sh->n_q) return zwg::set_last_error("causal attention needs n_kv >= n_q");
-    if (sh->kt_stride && sh->kt_stride < sh->n_kv) return zwg::set_last_error("kt_stride < n_kv");
-    if (sh->q_stride < sh->n_head * sh->d || sh->out_stride < sh->n_head * sh->d ||
-        sh->kv_stride < sh->n_head_kv * sh->d)
-        return zwg::set_last_error("row stride smaller than the heads it holds");
+    // the checks every attention entry point makes (the reference's asserts), then this
+    // entry point's own limits
+    int rc = zwg::capi::check_shape(sh);
+    if (rc) return rc;
     const size_t rows = sh->n_q * (sh->n_head / sh->n_head_kv);
     if (!zwg::decode_supported(sh->d, rows, sh->kt_stride))
         return zwg::set_last_error("zwg_attention_dev_noalloc takes decode shapes only: d in {32, 64, 128}, "
@@ -79,9 +112,11 @@ extern "C" int zwg_attention_dev_noalloc(const zwg_attn_shape* sh, const zwg_bat
     if (b && (b->q_batch_stride % 4 || b->k_batch_stride % 4 || b->v_batch_stride % 4))
         return zwg::set_last_error("batch strides must be multiples of 4");
 
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return zwg::set_last_error_cuda("cudaGetDevice", e);
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess || sms <= 0) return zwg::set_last_error_cuda("cudaDeviceGetAttribute(SM count)", e);
     int n_splits = 1, chunk = 0;
     zwg::decode_plan(nb, sh->n_head_kv, sh->n_kv, sh->kt_stride != 0, sms, &n_splits, &chunk);
     const size_t need = zwg::decode_workspace_floats(nb, sh->n_head_kv, rows, n_splits, sh->d);
@@ -89,7 +124,7 @@ extern "C" int zwg_attention_dev_noalloc(const zwg_attn_shape* sh, const zwg_bat
         return zwg::set_last_error("zwg_attention_dev_noalloc: this call needs more scratch than the built-in "
                                    "4 MiB array holds; split the batch or use zwg_attention_dev");
     float* scratch = nullptr;
-    int rc = scratch_for_current_device(&scratch);
+    rc = scratch_for_current_device(dev, &scratch);
     if (rc) return rc;
 
     zwg::DecodeParams p{};
@@ -99,7 +134,10 @@ extern "C" int zwg_attention_dev_noalloc(const zwg_attn_shape* sh, const zwg_bat
     p.kt_stride = sh->kt_stride; p.causal = sh->causal ? 1 : 0;
     p.n_splits = n_splits; p.chunk = chunk;
     if (b) { p.q_bs = b->q_batch_stride; p.k_bs = b->k_batch_stride; p.v_bs = b->v_batch_stride; p.out_bs = b->out_batch_stride; }
-    if (zwg::decode_f32_launch(p, nb, (cudaStream_t)stream))
-        return zwg::set_last_error_cuda("decode kernel launch", cudaGetLastError());
+    if (zwg::decode_f32_launch(p, nb, (cudaStream_t)stream)) {
+        e = cudaGetLastError();
+        if (e == cudaSuccess) return zwg::set_last_error("zwg_attention_dev_noalloc: no decode kernel for this shape");
+        return zwg::set_last_error_cuda("decode kernel launch", e);
+    }
     return ZWG_OK;
 }
