@@ -399,6 +399,89 @@ ZWG_API size_t zwg_dec_scratch_bytes(const zwg_dec_state* st, size_t n);
 ZWG_API int zwg_dec_forward_q8(zwg_dec_state* st, const zwg_dec_weights* w, const int32_t* tokens, size_t n_past,
                                size_t n, float* x, float* logits, void* scratch, size_t scratch_bytes, void* stream);
 
+/* ---- Whisper's greedy decoding rules on the device (src/transcribe.zig:176-193, 248-580) ---
+ * The transcription driver's per-token sampling (Engine.sample) and the bookkeeping of its
+ * window loop, so a window's tokens stay on the device between decoder steps. */
+
+/* Special token ids and options of Engine.sample: the ids of src/model.zig:37-47 (`space`
+ * is the id of the token " ", src/transcribe.zig:116), n_audio_ctx (30 s = 2 * n_audio_ctx
+ * mel frames), max_initial_ts in seconds (<= 0 turns the rule off, Options.max_initial_ts),
+ * hotword_bias (Engine.hotword_bias) and the hotword forms as DEVICE arrays: the forms'
+ * token ids concatenated in `hotwords`, form f at [hotword_offsets[f], hotword_offsets[f+1])
+ * (n_hotwords + 1 offsets; each hotword's two forms, with and without a leading space, in
+ * the reference's order). */
+typedef struct zwg_whisper_rules {
+    int32_t eot, sot, translate, transcribe, solm, prev, nosp, not_, beg, space;
+    int32_t n_audio_ctx;
+    float max_initial_ts;
+    float hotword_bias;
+    const int32_t* hotwords;
+    const int32_t* hotword_offsets;
+    int32_t n_hotwords;
+} zwg_whisper_rules;
+
+/* The reference's defaults for English-only models: the ids above, n_audio_ctx 1500,
+ * max_initial_ts 1 s, hotword bias 5, no hotwords. */
+ZWG_API int zwg_whisper_rules_default(zwg_whisper_rules* r);
+
+/* Engine.sample (src/transcribe.zig:491-580) for n_batch rows of logits [n_batch][n_vocab]
+ * (device f32, modified in place as the reference modifies Engine.logits): row b's window
+ * has sampled tokens[b * tokens_stride + 0 .. n_tokens[b]) so far (device int32; n_tokens
+ * NULL: none, the first token), has_ts[b] and seek_delta[b] of the window loop (NULL: 0 and
+ * 2 * n_audio_ctx). out_id[b] = the chosen token, out_tid[b] = the most likely timestamp
+ * (device int32). The token ids equal the reference's; the log-sum-exp sums agree to f32
+ * rounding. */
+ZWG_API int zwg_whisper_sample(float* logits, size_t n_batch, size_t n_vocab, const int32_t* tokens,
+                               size_t tokens_stride, const int32_t* n_tokens, const int32_t* has_ts,
+                               const int32_t* seek_delta, const zwg_whisper_rules* rules, int32_t* out_id,
+                               int32_t* out_tid, void* stream);
+
+/* One window's state in the token loop of Engine.transcribe (src/transcribe.zig:292-365), in
+ * device memory. The caller sets seek (the window's first mel frame) and seek_end (mel frames
+ * of audio present, Mel.n_len_org); zwg_whisper_window_init sets the rest. After the loop:
+ * the result is tokens[0 .. result_len), the next window starts seek_delta frames later,
+ * failed with result_len 0 means nothing usable (the reference then moves on by a whole
+ * window). */
+typedef struct zwg_whisper_window {
+    int32_t seek;
+    int32_t seek_end;
+    int32_t n_tokens;     /* tokens sampled so far */
+    int32_t seek_delta;
+    int32_t has_ts;
+    int32_t result_len;
+    int32_t failed;
+    int32_t done;         /* the loop has ended for this window */
+} zwg_whisper_window;
+
+ZWG_API int zwg_whisper_window_init(zwg_whisper_window* win, size_t n_batch, const zwg_whisper_rules* rules,
+                                    void* stream);
+
+/* One step of the loop for every window that has not ended: Engine.sample on its logits row,
+ * then the loop body's bookkeeping (src/transcribe.zig:319-364): the token and the best
+ * timestamp appended at tokens/tids[b * cap + n_tokens] (device int32), seek_delta, has_ts,
+ * result_len, failed and done updated. next_token[b] (device int32) is the decoder's next
+ * input; a window that has ended keeps its last token there. n_max: the loop's token limit
+ * (n_text_ctx / 2 - 4 in the reference), at most cap. */
+ZWG_API int zwg_whisper_step(float* logits, size_t n_batch, size_t n_vocab, zwg_whisper_window* win, int32_t* tokens,
+                             int32_t* tids, size_t cap, const zwg_whisper_rules* rules, size_t n_max,
+                             int32_t* next_token, void* stream);
+
+/* Scratch bytes zwg_whisper_decode_q8 needs for a prompt of n_prompt tokens. */
+ZWG_API size_t zwg_whisper_decode_scratch_bytes(const zwg_dec_state* st, size_t n_vocab, size_t n_prompt);
+
+/* The whole token loop of one window for each of the state's n_batch windows, on the device:
+ * Decoder.forward of the prompt [n_batch][n_prompt] (device int32; the windows share its
+ * length), then up to n_max (0: n_text_ctx / 2 - 4) steps of zwg_whisper_step and
+ * zwg_dec_forward_q8. Tokens never leave the device; the host reads the windows' states
+ * (n_batch * 32 bytes) every check_every steps (0: only at the end) and stops once every
+ * window is done. The cross K/V must be set (zwg_dec_set_audio_q8) and win[b].seek, seek_end
+ * filled; on return win, tokens and tids [n_batch][cap] hold each window's loop as the
+ * reference leaves it. Synchronizes `stream`. */
+ZWG_API int zwg_whisper_decode_q8(zwg_dec_state* st, const zwg_dec_weights* w, const zwg_whisper_rules* rules,
+                                  const int32_t* prompt, size_t n_prompt, size_t n_max, zwg_whisper_window* win,
+                                  int32_t* tokens, int32_t* tids, size_t cap, size_t check_every, void* scratch,
+                                  size_t scratch_bytes, void* stream);
+
 /* ---- Whisper encoder on the device (src/encoder.zig:118-179) ----------------------------
  * f16 weights as in the model file (exact in f16); every product on tcgen05 tensor cores with
  * f16 operands (activations rounded to f16) and f32 accumulation; attention on the bf16

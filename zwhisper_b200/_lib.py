@@ -23,6 +23,26 @@ c_size = ctypes.c_size_t
 c_ptr = ctypes.c_void_p
 
 
+class WhisperRulesC(ctypes.Structure):
+    """zwg_whisper_rules: the special token ids and options of Engine.sample
+    (src/transcribe.zig:491-580, src/model.zig:37-47); hotword arrays are device pointers."""
+
+    _fields_ = [
+        ("eot", ctypes.c_int32), ("sot", ctypes.c_int32), ("translate", ctypes.c_int32),
+        ("transcribe", ctypes.c_int32), ("solm", ctypes.c_int32), ("prev", ctypes.c_int32),
+        ("nosp", ctypes.c_int32), ("not_", ctypes.c_int32), ("beg", ctypes.c_int32), ("space", ctypes.c_int32),
+        ("n_audio_ctx", ctypes.c_int32), ("max_initial_ts", ctypes.c_float), ("hotword_bias", ctypes.c_float),
+        ("hotwords", c_ptr), ("hotword_offsets", c_ptr), ("n_hotwords", ctypes.c_int32),
+    ]
+
+
+class WhisperWindowC(ctypes.Structure):
+    """zwg_whisper_window: one window's state in the token loop (src/transcribe.zig:292-365)."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in ("seek", "seek_end", "n_tokens", "seek_delta", "has_ts", "result_len",
+                                               "failed", "done")]
+
+
 class AttnShapeC(ctypes.Structure):
     """zwg_attn_shape (include/zwgpu.h), the C mirror of AttnShape (src/ops.zig:477-492)."""
 
@@ -166,6 +186,16 @@ SIGNATURES = {
     "zwg_linear_q8_gelu": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr, c_size, c_ptr, c_ptr]),
     "zwg_dec_set_audio_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(DecWeightsC), c_size, c_ptr, c_ptr]),
     "zwg_dec_scratch_bytes": (c_size, [c_ptr, c_size]),
+    "zwg_whisper_rules_default": (ctypes.c_int, [ctypes.POINTER(WhisperRulesC)]),
+    "zwg_whisper_sample": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_size, c_ptr, c_ptr, c_ptr,
+                                          ctypes.POINTER(WhisperRulesC), c_ptr, c_ptr, c_ptr]),
+    "zwg_whisper_window_init": (ctypes.c_int, [c_ptr, c_size, ctypes.POINTER(WhisperRulesC), c_ptr]),
+    "zwg_whisper_step": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr, c_size,
+                                        ctypes.POINTER(WhisperRulesC), c_size, c_ptr, c_ptr]),
+    "zwg_whisper_decode_scratch_bytes": (c_size, [c_ptr, c_size, c_size]),
+    "zwg_whisper_decode_q8": (ctypes.c_int, [c_ptr, ctypes.POINTER(DecWeightsC), ctypes.POINTER(WhisperRulesC), c_ptr,
+                                             c_size, c_size, c_ptr, c_ptr, c_ptr, c_size, c_size, c_ptr, c_size,
+                                             c_ptr]),
     "zwg_enc_scratch_bytes": (c_size, [ctypes.POINTER(EncWeightsC), c_size]),
     "zwg_mel_frames": (c_size, [c_size]),
     "zwg_mel_scratch_bytes": (c_size, []),

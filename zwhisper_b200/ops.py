@@ -738,6 +738,91 @@ def linear_q8_gelu(x, q, scales, bias=None, out=None):
     return out
 
 
+class WhisperRules:
+    """zwg_whisper_rules: the special token ids and options of Engine.sample
+    (src/transcribe.zig:491-580). `hotwords` is a list of forms (token id lists), in the
+    reference's order; they are copied to the device once."""
+
+    def __init__(self, hotwords=(), hotword_bias: float = 5.0, max_initial_ts: float = 1.0, n_audio_ctx: int = 1500,
+                 device: int = 0, **token_ids):
+        torch = _torch()
+        self.c = _lib.WhisperRulesC()
+        _lib.check(_lib.load().zwg_whisper_rules_default(ctypes.byref(self.c)))
+        for k, v in token_ids.items():
+            setattr(self.c, k, int(v))
+        self.c.n_audio_ctx = n_audio_ctx
+        self.c.max_initial_ts = max_initial_ts
+        self.c.hotword_bias = hotword_bias
+        self._keep = []
+        forms = [list(f) for f in hotwords]
+        if forms:
+            flat = [t for f in forms for t in f] or [0]
+            offs = [0]
+            for f in forms:
+                offs.append(offs[-1] + len(f))
+            d = torch.device("cuda", device)
+            ht = torch.tensor(flat, dtype=torch.int32, device=d)
+            ho = torch.tensor(offs, dtype=torch.int32, device=d)
+            self._keep = [ht, ho]
+            self.c.hotwords, self.c.hotword_offsets, self.c.n_hotwords = ht.data_ptr(), ho.data_ptr(), len(forms)
+
+
+def whisper_sample(logits, tokens=None, n_tokens=None, has_ts=None, seek_delta=None, rules: WhisperRules = None):
+    """Engine.sample (src/transcribe.zig:491-580) on each row of logits [n_batch][n_vocab]
+    (CUDA f32, modified in place) with the device sampler (zwg_whisper_sample). tokens: CUDA
+    int32 [n_batch][cap] with n_tokens [n_batch] of them sampled so far; has_ts, seek_delta:
+    CUDA int32 [n_batch]. Returns (ids, tids), CUDA int32 [n_batch]."""
+    torch = _torch()
+    nb, nv = logits.shape
+    rules = rules or WhisperRules(device=logits.device.index or 0)
+    ids = torch.empty(nb, dtype=torch.int32, device=logits.device)
+    tids = torch.empty_like(ids)
+    tp = _dev_ptr(tokens, torch.int32, "tokens") if tokens is not None else None
+    stride = tokens.shape[1] if tokens is not None else 0
+    ntp = _dev_ptr(n_tokens, torch.int32, "n_tokens") if n_tokens is not None else None
+    hp = _dev_ptr(has_ts, torch.int32, "has_ts") if has_ts is not None else None
+    sp = _dev_ptr(seek_delta, torch.int32, "seek_delta") if seek_delta is not None else None
+    _lib.check(_lib.load().zwg_whisper_sample(_dev_ptr(logits, torch.float32, "logits"), nb, nv, tp, stride, ntp, hp,
+                                              sp, ctypes.byref(rules.c), ids.data_ptr(), tids.data_ptr(),
+                                              _stream_of(logits)))
+    return ids, tids
+
+
+def whisper_decode_q8(state: "DecoderState", weights: "DecoderWeightsQ8", prompt, seek, seek_end,
+                      rules: WhisperRules = None, n_max: int = 0, check_every: int = 8, scratch=None):
+    """The token loop of one window per state window on the device (zwg_whisper_decode_q8):
+    prompt CUDA int32 [n_batch][n_prompt]; seek, seek_end: per-window mel frames (lists).
+    The cross K/V must be set. Returns one dict per window: tokens, tids, result_len,
+    seek_delta, has_ts, failed."""
+    torch = _torch()
+    nb = state.n_batch
+    dev = prompt.device
+    rules = rules or WhisperRules(device=dev.index or 0)
+    n_prompt = prompt.numel() // nb
+    cap = n_max or (state.n_text_ctx // 2 - 4)
+    win = torch.zeros(nb, 8, dtype=torch.int32, device=dev)
+    win[:, 0] = torch.tensor(list(seek), dtype=torch.int32)
+    win[:, 1] = torch.tensor(list(seek_end), dtype=torch.int32)
+    tokens = torch.full((nb, cap), -1, dtype=torch.int32, device=dev)
+    tids = torch.full((nb, cap), -1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    need = lib.zwg_whisper_decode_scratch_bytes(state._h, weights.n_vocab, n_prompt)
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+    _lib.check(lib.zwg_whisper_decode_q8(state._h, ctypes.byref(weights.c_struct()), ctypes.byref(rules.c),
+                                         _dev_ptr(prompt, torch.int32, "prompt"), n_prompt, n_max, win.data_ptr(),
+                                         tokens.data_ptr(), tids.data_ptr(), cap, check_every, scratch.data_ptr(),
+                                         scratch.numel(), _stream_of(prompt)))
+    w = win.cpu().numpy()
+    tk, td = tokens.cpu().numpy(), tids.cpu().numpy()
+    out = []
+    for b in range(nb):
+        n = int(w[b, 2])
+        out.append({"tokens": tk[b, :n].tolist(), "tids": td[b, :n].tolist(), "result_len": int(w[b, 5]),
+                    "seek_delta": int(w[b, 3]), "has_ts": bool(w[b, 4]), "failed": bool(w[b, 6])})
+    return out
+
+
 class DecoderWeightsQ8:
     """The Whisper decoder's weights on the device (decoder.Decoder / decoder.Layer,
     src/decoder.zig:13-60) and the zwg_dec_weights struct that points at them. `tensors` maps
