@@ -58,13 +58,29 @@ def from_q8_0(data: bytes, n: int, k: int) -> Tuple[np.ndarray, np.ndarray]:
 
 
 def linear(x: np.ndarray, q: np.ndarray, scale: np.ndarray, bias: Optional[np.ndarray] = None) -> np.ndarray:
+    """out = x . W^T (+ bias) with W = q * scale per block of 32, summed in float64 (the
+    reference's per-block f32 dots scaled by the block's scale, src/gemm.zig:268-351, to
+    well below f32 rounding). Row chunks of W go through one float64 matrix product each."""
     x = np.asarray(x, np.float32)
     m, k = x.shape
     n = q.shape[0]
-    xb = x.reshape(m, k // BLOCK, BLOCK).astype(np.float64)
-    qb = q.reshape(n, k // BLOCK, BLOCK).astype(np.float64)
-    t = np.einsum("mbi,nbi->mnb", xb, qb)  # per-block dots
-    out = (t * scale.astype(np.float64)[None]).sum(-1)
+    if m <= 8:
+        # a few rows: per-block dots, then the scales (no float64 copy of the weights)
+        xb = x.reshape(m, k // BLOCK, BLOCK).astype(np.float64)
+        qb = q.reshape(n, k // BLOCK, BLOCK).astype(np.float64)
+        t = np.einsum("mbi,nbi->mnb", xb, qb)
+        out = (t * scale.astype(np.float64)[None]).sum(-1)
+        if bias is not None:
+            out = out + np.asarray(bias, np.float64)[None]
+        return out.astype(np.float32)
+    x64 = x.astype(np.float64)
+    out = np.empty((m, n), np.float64)
+    step = max(1, (1 << 24) // max(k, 1))  # ~128 MB of float64 weights per chunk
+    for n0 in range(0, n, step):
+        n1 = min(n, n0 + step)
+        w = (q[n0:n1].reshape(n1 - n0, k // BLOCK, BLOCK).astype(np.float64)
+             * scale[n0:n1].astype(np.float64)[..., None]).reshape(n1 - n0, k)
+        out[:, n0:n1] = x64 @ w.T
     if bias is not None:
         out = out + np.asarray(bias, np.float64)[None]
     return out.astype(np.float32)
