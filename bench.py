@@ -191,6 +191,17 @@ class CpuSample:
             self.run(self.q, self.k, self.v, self.out)
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_windows_per_s(min_seconds: float = 10.0, max_reps: int = 40, threads: int = 0):
     """Windows/s of the CPU restatement, repeated until min_seconds of work."""
     s = CpuSample(threads)
@@ -207,31 +218,73 @@ def cpu_windows_per_s(min_seconds: float = 10.0, max_reps: int = 40, threads: in
                       f"oracle/attn_ref.c ({s.isa}), {el:.1f} s", "isa": s.isa}
 
 
+def reference_binary_baseline(threads: int):
+    """The reference's shipped binary (copied into oracle/_ref by the build) timed by its own
+    `bench <threads>` command on the base.en attention shape (src/bench.zig:50-77), next to
+    the C restatement on the same shape and threads. None when the binary is absent or does
+    not run on this host."""
+    import numpy as np
+
+    from oracle import attention as OA
+    from oracle import cref, ref_binary
+    rb = ref_binary.bench_attention(threads)
+    if rb is None:
+        return None
+    n_ctx, ns, H = 1500, 512, 8
+    run = cref.Runner(OA.mha_shape(n_ctx, n_ctx, ns, H, False), threads)
+    rng = np.random.default_rng(0)
+    q, k, v = ((rng.standard_normal(n_ctx * ns, dtype=np.float32) * SIGMA) for _ in range(3))
+    out = np.zeros(n_ctx * ns, np.float32)
+    run(q, k, v, out)
+    reps, t0 = 0, time.perf_counter()
+    while reps < 20 or time.perf_counter() - t0 < 1.0:
+        run(q, k, v, out)
+        reps += 1
+    ms = (time.perf_counter() - t0) / reps * 1e3
+    return {"shape": "base.en encoder attention, 8 heads x 1500 x 1500, d 64 (the binary's bench line)",
+            "threads": threads,
+            "binary": {"ms": rb["ms"], "gflops": rb["gflops"], "line": rb["line"]},
+            "port": {"ms": ms, "gflops": ref_binary.ATTN_FLOP / ms / 1e6},
+            "binary_windows_per_s_equiv": rb["gflops"] * 1e9 / (FLOP_PER_WINDOW_LAYER * N_LAYER),
+            "note": "windows/s the binary's attention rate gives on the small.en window's 82.9 GFLOP"}
+
+
 def run_reference(args, rank, world):
-    """The reference's CPU attention on the host cores: each step is one window through all
-    12 layers (a bounded sample of the 64-window workload)."""
+    """The reference's CPU attention on the host cores, on the same job as our arm: each step
+    is all 64 windows through all 12 layers (the C restatement of attentionEx with all host
+    threads; every window reuses one set of Q/K/V, the work being compute-bound)."""
     if rank != 0:
         return
     s = CpuSample()
-    for _ in range(args.warmup):
-        s.window()
+    s.window()  # warm-up
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        for _ in range(WINDOWS):
+            s.window()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        s.window()
+        for _ in range(WINDOWS):
+            s.window()
     el = time.perf_counter() - t0
-    value = args.steps / el
+    value = WINDOWS * args.steps / el
+    rb = reference_binary_baseline(s.threads)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "whisper small.en encoder attention (configs[2]), "
-                                                     "1 window x 12 layers per step (bounded sample)",
-                                        "n_ctx": N_CTX, "n_state": N_STATE, "n_head": N_HEAD, "n_layer": N_LAYER},
+        "data": "synthetic", "config": {"workload": "whisper small.en encoder self-attention (configs[2]): 64 "
+                                                     "windows x 12 layers x 12 heads, n_ctx 1500, d 64",
+                                        "windows": WINDOWS, "n_ctx": N_CTX, "n_state": N_STATE, "n_head": N_HEAD,
+                                        "n_layer": N_LAYER},
+        "same_config": True,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": s.threads, "kind": "port",
-                         "sample": f"1 window x {N_LAYER} layers per step, oracle/attn_ref.c ({s.isa}); "
-                                   "the reference's Zig source cannot be built here (no Zig toolchain)"},
+                         "sample": f"{WINDOWS} windows x {N_LAYER} layers per step (the whole job), oracle/attn_ref.c "
+                                   f"({s.isa}), f32; the reference's Zig source cannot be built here (no Zig "
+                                   "toolchain)", "cpu": cpu_model()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if rb is not None:
+        line["cpu_baseline"]["reference_binary"] = rb
     print(json.dumps(line), flush=True)
 
 
@@ -269,89 +322,89 @@ def time_cuda(fn, steps, stream=None):
     return s.elapsed_time(e) * 1e-3
 
 
-def secondary_decode(dev, hbm_peak, steps=20, warmup=3):
-    """Decode-attention workloads (configs 1, 3, 4) at one GPU: one step = one new token
-    for every item through all layers' attention (f32 K/V, the reference's precision),
-    captured once in a CUDA graph and replayed."""
+def secondary_decode(dev, hbm_peak, rank, world, steps=20, warmup=3):
+    """Decode-attention workloads (configs 1, 3, 4): one step = one new token for every item
+    through all layers' attention (f32 K/V, the reference's precision), captured once in a
+    CUDA graph and replayed. Items (windows, sequences) are sharded over the ranks; the
+    figures are the whole job's (items of all ranks over the slowest rank's time) and the
+    per-GPU HBM fraction."""
     import torch
 
     from zwhisper_b200 import ops
     res = []
-
-    def run_case(name, metric, B, layers, calls):
-        # calls: list of (shape, q, k, v, out, ws, batch_strides, bytes_per_layer_call)
-        def step():
-            for _ in range(layers):
-                for sh, q, k, v, o, ws, bs, _ in calls:
-                    ops.attention_dev(q, k, v, sh, o, n_batch=B, batch_strides=bs, workspace=ws)
-        t = time_graph(step, steps, warmup)
-        per_step = t / steps
-        byts = layers * sum(c[7] for c in calls)
-        res.append({"workload": name, "metric": metric, "value": B / per_step, "unit": "tok/s",
-                    "ms_per_step": per_step * 1e3,
-                    "roofline": {"bound": "hbm", "achieved": byts / per_step / 1e9, "peak": hbm_peak,
-                                 "unit": "GB/s", "frac": byts / per_step / 1e9 / hbm_peak, "traffic": None}})
-
     g = torch.Generator(device=dev)
-    g.manual_seed(1)
+    g.manual_seed(1 + rank)
 
     def randn(*shape):
         return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32)
 
-    # config 1: whisper base.en decoder step, 32 windows, 6 layers; self over 224 of 448, cross over 1500
-    B, H, d, ns = 32, 8, 64, 512
-    ck, cv = randn(B, 448, ns), randn(B, 448, ns)
-    xk, xv = randn(B, 1500, ns), randn(B, 1500, ns)
+    # config 1: whisper base.en decoder step, 32 windows, 6 layers, each with its own self
+    # cache (224 of 448 positions) and cross K/V (1500 frames)
+    B_all, H, d, ns, L = 32, 8, 64, 512, 6
+    b0, b1 = shard(B_all, rank, world)
+    B = b1 - b0
+    layers = [(randn(B, 448, ns), randn(B, 448, ns), randn(B, 1500, ns), randn(B, 1500, ns)) for _ in range(L)]
     q, o = randn(B, 1, ns), torch.empty(B, 1, ns, device=dev)
     sh_s = ops.mha_shape(1, 224, ns, H, True)
     sh_c = ops.mha_shape(1, 1500, ns, H, False)
     ws_s = torch.empty(max(1, ops.attention_workspace_bytes(sh_s, B)), dtype=torch.uint8, device=dev)
     ws_c = torch.empty(max(1, ops.attention_workspace_bytes(sh_c, B)), dtype=torch.uint8, device=dev)
-    run_case("whisper base.en decoder self+cross attention step (configs[1]): 32 windows, 6 layers",
-             "whisper_base_en_decoder_attention_tok_per_s", B, 6,
-             [(sh_s, q, ck, cv, o, ws_s, (ns, 448 * ns, 448 * ns, ns), B * 224 * ns * 4 * 2),
-              (sh_c, q, xk, xv, o, ws_c, (ns, 1500 * ns, 1500 * ns, ns), B * 1500 * ns * 4 * 2)])
-    del ck, cv, xk, xv
+
+    def step1():
+        for ck, cv, xk, xv in layers:
+            ops.attention_dev(q, ck, cv, sh_s, o, n_batch=B, batch_strides=(ns, 448 * ns, 448 * ns, ns), workspace=ws_s)
+            ops.attention_dev(q, xk, xv, sh_c, o, n_batch=B, batch_strides=(ns, 1500 * ns, 1500 * ns, ns),
+                              workspace=ws_c)
+    t = max_over_ranks(time_graph(step1, steps, warmup) / steps, world)
+    byts = L * B_all * (224 + 1500) * ns * 4 * 2
+    res.append({"workload": f"whisper base.en decoder self+cross attention step (configs[1]): {B_all} windows "
+                            f"({B} per GPU), {L} layers with distinct caches",
+                "metric": "whisper_base_en_decoder_attention_tok_per_s", "value": B_all / t, "unit": "tok/s",
+                "ms_per_step": t * 1e3, "math": "f32",
+                "roofline": {"bound": "hbm", "achieved": byts / world / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": byts / world / t / 1e9 / hbm_peak, "traffic": None, "per": "GPU"}})
+    del layers
     # configs 3 and 4: Qwen2 decode over the transposed key cache at the mean cache length,
     # through the state's decode entry point (zwg_llm_attn_decode, src/llm.zig:191-202) over
     # the state's own per-layer caches
-    for cfg, B, layers, H, Hkv, d, n_kv in (("configs[3] Qwen2.5-0.5B", 16, 24, 14, 2, 64, 2128),
+    for cfg, B_all, L, H, Hkv, d, n_kv in (("configs[3] Qwen2.5-0.5B", 16, 24, 14, 2, 64, 2128),
                                            ("configs[4] Qwen2.5-1.5B", 64, 28, 12, 2, 128, 2256)):
         n_ctx = 2560
-        kvw = Hkv * d
-        st = ops.LlmState(layers, B, H, Hkv, d, n_ctx, device=dev.index or 0)
-        for layer in range(layers):
+        b0, b1 = shard(B_all, rank, world)
+        B = b1 - b0
+        st = ops.LlmState(L, B, H, Hkv, d, n_ctx, device=dev.index or 0)
+        for layer in range(L):
             for t_ in st.cache_views(layer):
                 t_.normal_(generator=g)
         q, o = randn(B, 1, H * d), torch.empty(B, 1, H * d, device=dev)
-        byts = B * n_kv * kvw * 4 * 2
+        byts = B_all * n_kv * Hkv * d * 4 * 2 * L
 
-        def step(st=st, q=q, o=o, layers=layers, n_kv=n_kv):
-            for layer in range(layers):
+        def step(st=st, q=q, o=o, L=L, n_kv=n_kv):
+            for layer in range(L):
                 st.attn(layer, q, n_kv - 1, out=o)
         # math "f32": the SIMT split-K kernel (the reference's arithmetic); "tf32": the
         # tcgen05 kernel (tf32 operands, f32 accumulation; parity within max-abs 2e-3)
         for math, kernel in (("f32", "decode_tma_kernel"), ("tf32", "decode_tc_kernel")):
             ops.set_math(math)
             try:
-                t = time_graph(step, steps, warmup) / steps
+                t = max_over_ranks(time_graph(step, steps, warmup) / steps, world)
             finally:
                 ops.set_math("f32")
-            achieved = layers * byts / t / 1e9
+            achieved = byts / world / t / 1e9
             traffic = profiled_traffic("decode_tma_qwen15_b16.txt", B) if (d == 128 and math == "f32") else None
-            res.append({"workload": f"{cfg} decode attention, {B} sequences x {layers} layers, n_kv={n_kv} "
-                                    f"(mean of the decode), K^T cache n_ctx={n_ctx}, math {math} ({kernel})",
-                        "metric": "qwen_decode_attention_tok_per_s", "value": B / t, "unit": "tok/s",
+            res.append({"workload": f"{cfg} decode attention, {B_all} sequences ({B} per GPU) x {L} layers, "
+                                    f"n_kv={n_kv} (mean of the decode), K^T cache n_ctx={n_ctx}, math {math} ({kernel})",
+                        "metric": "qwen_decode_attention_tok_per_s", "value": B_all / t, "unit": "tok/s",
                         "ms_per_step": t * 1e3, "math": math,
                         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                                     "frac": achieved / hbm_peak, "traffic": traffic,
-                                     "bytes_per_launch": byts}})
+                                     "frac": achieved / hbm_peak, "traffic": traffic, "per": "GPU",
+                                     "bytes_per_step": byts}})
         st.close()
     torch.cuda.empty_cache()
     return res
 
 
-def secondary_prefill(dev, tc_peak, peak_kind, steps=2, warmup=1):
+def secondary_prefill(dev, tc_peak, peak_kind, rank, world, steps=2, warmup=1):
     """Qwen2 prefill attention (configs 3 and 4) at one GPU: one step = the whole 2000-token
     prompt in 256-token causal chunks (src/llm.zig:257-266) through every layer, for every
     sequence, on the tf32 tensor-core kernel over f32 K^T/V caches (distinct per layer)."""
@@ -360,11 +413,13 @@ def secondary_prefill(dev, tc_peak, peak_kind, steps=2, warmup=1):
     from zwhisper_b200 import ops
     res = []
     g = torch.Generator(device=dev)
-    g.manual_seed(2)
+    g.manual_seed(2 + rank)
     ops.set_math("tf32", dev.index or 0)
     try:
-        for cfg, B, layers, H, Hkv, d in (("configs[3] Qwen2.5-0.5B", 16, 24, 14, 2, 64),
-                                          ("configs[4] Qwen2.5-1.5B", 64, 28, 12, 2, 128)):
+        for cfg, B_all, layers, H, Hkv, d in (("configs[3] Qwen2.5-0.5B", 16, 24, 14, 2, 64),
+                                              ("configs[4] Qwen2.5-1.5B", 64, 28, 12, 2, 128)):
+            b0, b1 = shard(B_all, rank, world)
+            B = b1 - b0
             n_prompt, chunk, n_ctx = 2000, 256, 2048
             kvw = Hkv * d
             kts = [torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev) for _ in range(layers)]
@@ -383,17 +438,18 @@ def secondary_prefill(dev, tc_peak, peak_kind, steps=2, warmup=1):
             for _ in range(warmup):
                 step()
             torch.cuda.synchronize()
-            t = time_cuda(step, steps) / steps
+            t = max_over_ranks(time_cuda(step, steps) / steps, world)
             ops.sync()
             pairs = n_prompt * (n_prompt + 1) // 2
-            flops = 4 * d * H * layers * pairs * B
+            flops = 4 * d * H * layers * pairs * B_all
             peak = tc_peak / 2
             res.append({"workload": f"{cfg} prefill attention: {n_prompt}-token prompt in {chunk}-token causal "
-                                    f"chunks, {B} sequences x {layers} layers, tf32 tensor cores over f32 caches",
-                        "metric": "qwen_prefill_attention_tok_per_s", "value": B * n_prompt / t, "unit": "tok/s",
-                        "ms_per_step": t * 1e3,
-                        "roofline": {"bound": "tensor", "achieved": flops / t / 1e12, "peak": peak,
-                                     "unit": "TFLOP/s", "frac": flops / t / 1e12 / peak,
+                                    f"chunks, {B_all} sequences ({B} per GPU) x {layers} layers, tf32 tensor cores "
+                                    "over f32 caches",
+                        "metric": "qwen_prefill_attention_tok_per_s", "value": B_all * n_prompt / t, "unit": "tok/s",
+                        "ms_per_step": t * 1e3, "math": "tf32",
+                        "roofline": {"bound": "tensor", "achieved": flops / world / t / 1e12, "peak": peak,
+                                     "unit": "TFLOP/s", "frac": flops / world / t / 1e12 / peak, "per": "GPU",
                                      "peak_source": f"{peak_kind} bf16 (burst) / 2: dense tf32 runs at half the "
                                                     "bf16 rate", "traffic": None,
                                      "flops_per_step": flops}})
@@ -404,7 +460,7 @@ def secondary_prefill(dev, tc_peak, peak_kind, steps=2, warmup=1):
     return res
 
 
-def secondary_encoder(dev, tc_peak, peak_kind, steps=3, warmup=2):
+def secondary_encoder(dev, tc_peak, peak_kind, rank, world, steps=3, warmup=2):
     """The whole Whisper small.en encoder on the device for 64 consecutive
     windows: mel rows, both convolutions, 12 pre-norm blocks (f16 tcgen05 GEMMs with fused
     bias / GELU / residual epilogues, the bf16 attention kernel) and ln_post
@@ -414,7 +470,9 @@ def secondary_encoder(dev, tc_peak, peak_kind, steps=3, warmup=2):
     from oracle import whisper as W
     from zwhisper_b200 import ops
     hp = W.SMALL_EN
-    B, n_ctx, ns, L = 64, hp.n_audio_ctx, hp.n_audio_state, hp.n_audio_layer
+    B_all, n_ctx, ns, L = 64, hp.n_audio_ctx, hp.n_audio_state, hp.n_audio_layer
+    b0, b1 = shard(B_all, rank, world)
+    B = b1 - b0
     Wg = ops.EncoderWeightsF16(W.weights_dict(W.synth_model(hp, seed=0, encoder_only=True)), L, hp.n_audio_head,
                                device=dev.index or 0)
     g = torch.Generator(device=dev)
@@ -422,19 +480,21 @@ def secondary_encoder(dev, tc_peak, peak_kind, steps=3, warmup=2):
     mel = torch.randn(hp.n_mels, B * 2 * n_ctx, generator=g, device=dev) * 0.5
     out = torch.empty(B, n_ctx, ns, device=dev)
     scratch = torch.empty(Wg.scratch_bytes(B), dtype=torch.uint8, device=dev)
-    t = time_graph(lambda: ops.encoder_forward(Wg, mel, B, out=out, scratch=scratch), steps, warmup) / steps
+    t = max_over_ranks(time_graph(lambda: ops.encoder_forward(Wg, mel, B, out=out, scratch=scratch), steps,
+                                  warmup) / steps, world)
     T = 2 * n_ctx
-    flops = B * (2 * T * ns * 3 * hp.n_mels + 2 * n_ctx * ns * 3 * ns
-                 + L * (2 * n_ctx * ns * 12 * ns + 4 * n_ctx * n_ctx * ns))
+    flops = B_all * (2 * T * ns * 3 * hp.n_mels + 2 * n_ctx * ns * 3 * ns
+                     + L * (2 * n_ctx * ns * 12 * ns + 4 * n_ctx * n_ctx * ns))
     del Wg, mel, out, scratch
     torch.cuda.empty_cache()
-    return [{"workload": f"configs[2] Whisper small.en whole encoder (convolutions, {L} blocks, ln_post), {B} "
-                         "windows: f16 tcgen05 GEMMs + bf16 attention",
-             "metric": "whisper_small_en_encoder_windows_per_s", "value": B / t, "unit": "windows/s",
+    return [{"workload": f"configs[2] Whisper small.en whole encoder (convolutions, {L} blocks, ln_post), {B_all} "
+                         f"windows ({B} per GPU): f16 tcgen05 GEMMs + bf16 attention",
+             "metric": "whisper_small_en_encoder_windows_per_s", "value": B_all / t, "unit": "windows/s",
              "ms_per_step": t * 1e3,
-             "roofline": {"bound": "tensor", "achieved": flops / t / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
-                          "frac": flops / t / 1e12 / tc_peak, "peak_source": f"{peak_kind} bf16 (burst); f16 "
-                          "runs at the bf16 rate", "traffic": None, "flops_per_step": flops}}]
+             "math": "f16 GEMM operands (activations rounded to f16), bf16 attention operands, f32 accumulation",
+             "roofline": {"bound": "tensor", "achieved": flops / world / t / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
+                          "frac": flops / world / t / 1e12 / tc_peak, "peak_source": f"{peak_kind} bf16 (burst); f16 "
+                          "runs at the bf16 rate", "traffic": None, "flops_per_step": flops, "per": "GPU"}}]
 
 
 def secondary_q8(dev, hbm_peak, steps=20, warmup=3):
@@ -469,7 +529,7 @@ def secondary_q8(dev, hbm_peak, steps=20, warmup=3):
     byts = layers * sum(n * k * 1.125 for n, k in shapes)
     res.append({"workload": "Qwen2.5-1.5B decode-step projections, 1 sequence x 28 layers x 7 Q8 linears "
                             "(q/k/v/o/gate/up/down), int8 blocks of 32 + f32 scales",
-                "metric": "q8_projection_weight_GBps", "value": byts / t / 1e9, "unit": "GB/s",
+                "metric": "q8_projection_weight_GBps", "value": byts / t / 1e9, "unit": "GB/s", "math": "f32",
                 "ms_per_step": t * 1e3,
                 "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
                              "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
@@ -481,6 +541,7 @@ def secondary_q8(dev, hbm_peak, steps=20, warmup=3):
     byts = 51864 * 512 * 1.125
     res.append({"workload": "Whisper base.en logits, 51864 x 512 Q8 weights, 1 token",
                 "metric": "q8_logits_weight_GBps", "value": byts / t / 1e9, "unit": "GB/s", "ms_per_step": t * 1e3,
+                "math": "f32",
                 "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
                              "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
     torch.cuda.empty_cache()
@@ -569,7 +630,7 @@ def whisper_base_decoder(dev, seed=7):
     return W
 
 
-def secondary_step(dev, hbm_peak, steps=10, warmup=3):
+def secondary_step(dev, hbm_peak, rank, world, steps=10, warmup=3):
     """The whole Qwen2.5-1.5B greedy decode step on the device (the "next" rows around the
     attention, src/llm.zig:169-216, 313-321): embedding, 28 layers of RMSNorm, Q8 q/k/v with
     bias + RoPE + K^T/V append in one launch, decode attention over n_kv = 2256, wo +
@@ -584,36 +645,43 @@ def secondary_step(dev, hbm_peak, steps=10, warmup=3):
     wbytes = (c["n_layer"] * (2 * 1536 * 1536 + 2 * 256 * 1536 + 3 * c["n_ff"] * 1536) + c["n_vocab"] * 1536) * 1.125
     res = []
     from zwhisper_b200 import ops
-    for B in (1, 64):
-        st, step = qwen15_step_fn(W, B, n_ctx, n_kv - 1, dev)
+    # one sequence (the reference's own generate loop) on one GPU; configs[4]'s 64 sequences
+    # sharded over the ranks, each GPU holding all the weights
+    for B_all in ((1, 64) if world == 1 else (64,)):
+        b0, b1 = shard(B_all, rank, world)
+        B = b1 - b0
+        st, step = qwen15_step_fn(W, B, n_ctx, n_kv - 1, dev, seed=6 + rank)
         kv = B * c["n_layer"] * n_kv * c["n_head_kv"] * c["d"] * 2 * 4
-        byts = wbytes + kv
+        byts = wbytes + kv   # per GPU
         # math "tf32" changes only the attention (the tcgen05 decode kernel)
         for math in ("f32", "tf32"):
             ops.set_math(math)
             try:
-                t = time_graph(step, steps, warmup) / steps
+                t = max_over_ranks(time_graph(step, steps, warmup) / steps, world)
             finally:
                 ops.set_math("f32")
-            res.append({"workload": f"Qwen2.5-1.5B greedy decode step on the device, {B} sequence(s) x 28 layers + "
-                                    f"logits (vocab 151936) + penalized argmax, Q8 weights, n_kv={n_kv}, "
-                                    f"attention math {math}",
-                        "metric": "qwen_decode_step_tok_per_s", "value": B / t, "unit": "tok/s",
-                        "ms_per_step": t * 1e3, "math": math,
+            res.append({"workload": f"Qwen2.5-1.5B greedy decode step on the device, {B_all} sequence(s) ({B} per "
+                                    f"GPU) x 28 layers + logits (vocab 151936) + penalized argmax, Q8 weights, "
+                                    f"n_kv={n_kv}, attention math {math}",
+                        "metric": "qwen_decode_step_tok_per_s", "value": B_all / t, "unit": "tok/s",
+                        "ms_per_step": t * 1e3, "math": f"f32 projections, {math} attention",
                         "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                                     "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
+                                     "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts,
+                                     "per": "GPU"}})
         st.close()
         torch.cuda.empty_cache()
     del W
     torch.cuda.empty_cache()
     # the Whisper base.en decoder step: 32 windows, 6 layers, 224 of 448 cache
     # positions filled, cross-attention over 1500 frames, Q8 weights, logits and argmax
-    B, n_past, na, ns = 32, 224, 1500, 512
+    B_all, n_past, na, ns = 32, 224, 1500, 512
+    b0, b1 = shard(B_all, rank, world)
+    B = b1 - b0
     Wd = whisper_base_decoder(dev)
     from zwhisper_b200 import ops
     st = ops.DecoderState(6, B, ns, 8, 448, na, device=dev.index or 0)
     g = torch.Generator(device=dev)
-    g.manual_seed(8)
+    g.manual_seed(8 + rank)
     for w in range(B):
         st.set_audio_q8(Wd, w, torch.randn(na, ns, generator=g, device=dev))
     tok = torch.randint(0, 51864, (B, 1), generator=g, device=dev, dtype=torch.int32)
@@ -624,18 +692,20 @@ def secondary_step(dev, hbm_peak, steps=10, warmup=3):
     def wstep():
         st.forward_q8(Wd, tok, n_past, x=x, logits=logits, scratch=scratch)
         ops.llm_greedy(logits, penalty=1.0, out=tok.view(-1))
-    t = time_graph(wstep, steps, warmup) / steps
+    t = max_over_ranks(time_graph(wstep, steps, warmup) / steps, world)
     # per layer q, k, v, o, cq, co (n_state^2 each) and the two mlp matrices (4 n_state^2
     # each); ck and cv are read only by set_audio
     wbytes = (6 * (6 * ns * ns + 8 * ns * ns) + 51864 * ns) * 1.125
     kv = B * 6 * (n_past + 1 + na) * ns * 4 * 2
-    byts = wbytes + kv
-    res.append({"workload": f"Whisper base.en decoder step on the device (configs[1]): {B} windows x 6 layers "
-                            f"(self over {n_past + 1} of 448, cross over {na}) + logits (vocab 51864) + argmax, "
-                            f"Q8 weights",
-                "metric": "whisper_decoder_step_tok_per_s", "value": B / t, "unit": "tok/s", "ms_per_step": t * 1e3,
+    byts = wbytes + kv   # per GPU
+    res.append({"workload": f"Whisper base.en decoder step on the device (configs[1]): {B_all} windows ({B} per GPU) "
+                            f"x 6 layers (self over {n_past + 1} of 448, cross over {na}) + logits (vocab 51864) + "
+                            f"argmax, Q8 weights",
+                "metric": "whisper_decoder_step_tok_per_s", "value": B_all / t, "unit": "tok/s",
+                "ms_per_step": t * 1e3, "math": "f32",
                 "roofline": {"bound": "hbm", "achieved": byts / t / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                             "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts}})
+                             "frac": byts / t / 1e9 / hbm_peak, "traffic": None, "bytes_per_step": byts,
+                             "per": "GPU"}})
     st.close()
     del Wd
     torch.cuda.empty_cache()
@@ -724,12 +794,18 @@ def run_ours(args, rank, world, local):
 
     secondary = None
     cpu = None
-    if world == 1 and not args.no_secondary:
-        secondary = (secondary_decode(dev, hbm_peak) + secondary_prefill(dev, tc_peak, peak_kind) +
-                     secondary_encoder(dev, tc_peak, peak_kind) + secondary_q8(dev, hbm_peak) +
-                     secondary_step(dev, hbm_peak))
+    if not args.no_secondary:
+        # every rank runs the same workloads (its shard of each) and the same max-over-ranks
+        # reductions; the one-sequence Q8 projections run on one GPU only
+        secondary = (secondary_decode(dev, hbm_peak, rank, world) +
+                     secondary_prefill(dev, tc_peak, peak_kind, rank, world) +
+                     secondary_encoder(dev, tc_peak, peak_kind, rank, world) +
+                     (secondary_q8(dev, hbm_peak) if world == 1 else []) +
+                     secondary_step(dev, hbm_peak, rank, world))
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_windows_per_s(min_seconds=args.cpu_seconds)
+        cpu["cpu"] = cpu_model()
+        cpu["reference_binary"] = reference_binary_baseline(cpu["cores"])
 
     if rank != 0:
         return
@@ -757,9 +833,15 @@ def run_ours(args, rank, world, local):
         "clocks": clk,
     }
     if cpu is not None:
-        line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu")}
+        if cpu.get("reference_binary"):
+            line["cpu_baseline"]["reference_binary"] = cpu["reference_binary"]
     if secondary is not None:
         line["secondary"] = secondary
+        # the same figures in short, last in the line
+        line["secondary_summary"] = [
+            {"metric": r["metric"], "math": r.get("math"), "value": round(r["value"], 1), "unit": r["unit"],
+             "frac": round(r["roofline"]["frac"], 3), "of": r["roofline"]["unit"]} for r in secondary]
     print(json.dumps(line), flush=True)
 
 
