@@ -790,6 +790,13 @@ def run_ours(args, rank, world, local):
     e2e_value = WINDOWS * e2e_steps / t_e2e
     h2d = N_LAYER * 3 * WINDOWS * N_CTX * N_STATE * 4
     d2h = N_LAYER * WINDOWS * N_CTX * N_STATE * 4
+    # the bound the host-pointer contract sets: this step's bytes over the measured copy rates
+    # (pinned memory, one direction at a time, one Q tensor of this rank's windows, CUDA events)
+    dbuf = torch.empty(nel, dtype=torch.float32, device=dev)
+    h2d_gbs = nel * 4 / time_cuda(lambda: dbuf.copy_(hq, non_blocking=True), 3) * 3 / 1e9
+    d2h_gbs = nel * 4 / time_cuda(lambda: ho.copy_(dbuf, non_blocking=True), 3) * 3 / 1e9
+    del dbuf
+    t_bound = max(h2d / world / (h2d_gbs * 1e9), d2h / world / (d2h_gbs * 1e9))
     del hq, hk, hv, ho
 
     secondary = None
@@ -820,6 +827,8 @@ def run_ours(args, rank, world, local):
                                   f"per GPU over {world}, no collective",
                    "l2": "inputs larger than L2: distinct Q/K/V per layer, 5.3 GB per step"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "copy_bound": {"h2d_gbs": h2d_gbs, "d2h_gbs": d2h_gbs, "windows_per_s": WINDOWS / t_bound,
+                               "note": "the step's copies at the measured pinned copy rates, directions overlapped"},
                 "path": "zwg_attention_batch_host (ops.attentionEx drop-in), math mode bf16, pinned f32 host "
                         "buffers, conversion + tcgen05 kernel + copies on two streams",
                 "steps": e2e_steps},
