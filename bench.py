@@ -385,11 +385,11 @@ def secondary_decode(dev, hbm_peak, rank, world, steps=20, warmup=3):
         # math "f32": the SIMT split-K kernel (the reference's arithmetic); "tf32": the
         # tcgen05 kernel (tf32 operands, f32 accumulation; parity within max-abs 2e-3)
         for math, kernel in (("f32", "decode_tma_kernel"), ("tf32", "decode_tc_kernel")):
-            ops.set_math(math)
+            ops.set_math(math, dev.index or 0)
             try:
                 t = max_over_ranks(time_graph(step, steps, warmup) / steps, world)
             finally:
-                ops.set_math("f32")
+                ops.set_math("f32", dev.index or 0)
             achieved = byts / world / t / 1e9
             traffic = profiled_traffic("decode_tma_qwen15_b16.txt", B) if (d == 128 and math == "f32") else None
             res.append({"workload": f"{cfg} decode attention, {B_all} sequences ({B} per GPU) x {L} layers, "
@@ -655,11 +655,11 @@ def secondary_step(dev, hbm_peak, rank, world, steps=10, warmup=3):
         byts = wbytes + kv   # per GPU
         # math "tf32" changes only the attention (the tcgen05 decode kernel)
         for math in ("f32", "tf32"):
-            ops.set_math(math)
+            ops.set_math(math, dev.index or 0)
             try:
                 t = max_over_ranks(time_graph(step, steps, warmup) / steps, world)
             finally:
-                ops.set_math("f32")
+                ops.set_math("f32", dev.index or 0)
             res.append({"workload": f"Qwen2.5-1.5B greedy decode step on the device, {B_all} sequence(s) ({B} per "
                                     f"GPU) x 28 layers + logits (vocab 151936) + penalized argmax, Q8 weights, "
                                     f"n_kv={n_kv}, attention math {math}",
