@@ -25,8 +25,8 @@
 //               stored into the tile's P columns (the A operand of the PV MMA) once the
 //               previous PV has read them, f32 row sums, O rescaled in TMEM only when the
 //               running max grows by more than 2^8 (otherwise the stale max is kept:
-//               numerator and denominator share it); after the last tile, O / l is written
-//               to global memory as f32.
+//               numerator and denominator share it); after the last tile, O / l goes out
+//               by TMA stores staged in the item's Q tile buffer (the epilogue below).
 // TMEM columns per query tile t: S at 256t (128), P at 256t + 128 (64 columns of bf16
 // pairs), O at 256t + 192 (64); the two tiles fill all 512.
 // Keys past n_ctx come from the TMA's zero fill and are masked to -inf before the max; query
@@ -114,25 +114,83 @@ struct Smem {
 
 constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;  // + alignment slack
 
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-struct Work {
-    int n_items, n_pairs, n_tiles;
-};
-
 __device__ __forceinline__ void decode_item(int item, int n_pairs, int n_head, int& win, int& head, int& pair) {
     pair = item % n_pairs;
     head = (item / n_pairs) % n_head;
     win = item / (n_pairs * n_head);
 }
 
+// Epilogue of one warp's 32 rows: O / l is staged in the item's Q tile buffer (4 KB per
+// warp, 128-byte rows in the 128-byte swizzle the TMA store reads; the tile's S MMAs have
+// all completed by now) and written by TMA stores of [32 rows][32 f32] (two, f32 out) or
+// [32 rows][64 f16] (one), whole 128-byte lines, instead of one row per thread. Rows past
+// n_ctx fall outside the tensor map and are not written. Lane 0 then waits until the
+// stores have read the staging and releases the Q buffer to the producer.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+template <bool OUT_F16>
+__device__ __forceinline__ void write_out(const CUtensorMap* tm_o, Smem& sm, const uint32_t (&o)[64], float l,
+                                          int it, int t, int quarter, int lane, int win, int head, int pair) {
+    const float inv = l > 0.f ? 1.0f / l : 0.f;
+    uint8_t* stage = sm.q[it & 1][t] + quarter * 4096;
+    const uint32_t row_addr = smem_u32(stage) + lane * 128;
+    const int sw = lane & 7;
+    const int row0 = pair * 2 * BM + t * BM + quarter * 32;
+    if (OUT_F16) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            uint32_t h[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                __half2 p2 = __floats2half2_rn(__uint_as_float(o[8 * c + 2 * u]) * inv,
+                                               __uint_as_float(o[8 * c + 2 * u + 1]) * inv);
+                h[u] = *reinterpret_cast<uint32_t*>(&p2);
+            }
+            st_shared_v4(row_addr + ((c ^ sw) << 4), h[0], h[1], h[2], h[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_3d(tm_o, stage, head * D, row0, win);
+            bulk_commit_group();
+        }
+    } else {
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            if (half) {
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+            }
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const int i = half * 32 + 4 * c;
+                st_shared_v4(row_addr + ((c ^ sw) << 4), __float_as_uint(__uint_as_float(o[i]) * inv),
+                             __float_as_uint(__uint_as_float(o[i + 1]) * inv),
+                             __float_as_uint(__uint_as_float(o[i + 2]) * inv),
+                             __float_as_uint(__uint_as_float(o[i + 3]) * inv));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_3d(tm_o, stage, head * D + half * 32, row0, win);
+                bulk_commit_group();
+            }
+        }
+    }
+    if (lane == 0) {
+        bulk_wait_read0();
+        mbar_arrive(&sm.q_empty[it & 1]);
+    }
+    __syncwarp();
+}
+
 // OUT_F16: the output is f16 (the operand of the output projection) instead of f32.
 template <bool OUT_F16>
 __global__ void __launch_bounds__(THREADS, 1)
     enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, void* __restrict__ out, int n_ctx, int n_head,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o, int n_ctx, int n_head,
                        int n_items, int* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -151,7 +209,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; b++) {
             mbar_init(&sm.q_full[b], 1);
-            mbar_init(&sm.q_empty[b], 2);  // one commit from each MMA issuer
+            mbar_init(&sm.q_empty[b], 8);  // lane 0 of every softmax warp, after its output store
             mbar_init(&sm.s_full[b], 1);
             mbar_init(&sm.s_free[b], 128);
             mbar_init(&sm.p_full[b], 128);
@@ -258,7 +316,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mma_commit(&sm.pv_done[t]);
                     mma_commit(&sm.kv_empty[s]);
                 }
-                if (ok) mma_commit(&sm.q_empty[qb]);
                 g += n_tiles;
             }
         }
@@ -358,47 +415,21 @@ tmem_st64(p_addr, pk);  // the row's 64 bf16 pairs, one store
                 tc_fence_before();
                 mbar_arrive(&sm.p_full[t]);
             }
-            // ---- epilogue: O / l -> out[win][q0 + row][head * 64 ..]
+            // ---- epilogue: O / l by TMA stores staged in this item's Q tile buffer
             if (!ok || !(ok = mbar_wait_warp(&sm.pv_done[t], (g + n_tiles - 1) & 1, err))) break;
             tc_fence_after();
-            const float inv = l > 0.f ? 1.0f / l : 0.f;
-            const int grow = pair * 2 * BM + t * BM + row;
-            const size_t oidx = ((size_t)win * n_ctx + grow) * (size_t)(n_head * D) + head * D;
-#pragma unroll
-            for (int cc = 0; cc < D / 32; cc++) {
-                uint32_t o[32];
-                tmem_ld32(o_addr + cc * 32, o);
+            {
+                uint32_t o[64];
+                tmem_ld64(o_addr, o);
                 tmem_ld_wait();
-                if (grow < n_ctx) {
-                    if (OUT_F16) {
-                        uint4* orow = reinterpret_cast<uint4*>(static_cast<__half*>(out) + oidx + cc * 32);
-#pragma unroll
-                        for (int i = 0; i < 32; i += 8) {
-                            uint32_t h[4];
-#pragma unroll
-                            for (int u = 0; u < 4; u++) {
-                                __half2 p2 = __floats2half2_rn(__uint_as_float(o[i + 2 * u]) * inv,
-                                                               __uint_as_float(o[i + 2 * u + 1]) * inv);
-                                h[u] = *reinterpret_cast<uint32_t*>(&p2);
-                            }
-                            orow[i / 8] = make_uint4(h[0], h[1], h[2], h[3]);
-                        }
-                    } else {
-                        float* orow = static_cast<float*>(out) + oidx + cc * 32;
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            float4 v4 = make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                                                    __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-                            *reinterpret_cast<float4*>(orow + i) = v4;
-                        }
-                    }
-                }
+                write_out<OUT_F16>(&tm_o, sm, o, l, it, t, quarter, lane, win, head, pair);
             }
             tc_fence_before();
             g += n_tiles;
         }
     }
 
+    if (warp >= 4 && lane == 0) bulk_wait0();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -427,15 +458,31 @@ static bool make_map(CUtensorMap* map, const void* base, int n_batch, int n_ctx,
     return r == CUDA_SUCCESS;
 }
 
+static bool make_out_map(CUtensorMap* map, void* base, int n_batch, int n_ctx, int n_head, bool f16) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return false;
+    const cuuint64_t row = (cuuint64_t)n_head * 64;
+    const cuuint64_t esz = f16 ? 2 : 4;
+    cuuint64_t dims[3] = {row, (cuuint64_t)n_ctx, (cuuint64_t)n_batch};
+    cuuint64_t strides[2] = {row * esz, row * esz * (cuuint64_t)n_ctx};
+    cuuint32_t box[3] = {f16 ? 64u : 32u, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 int enc_tc_launch(const EncTcParams& p, cudaStream_t st) {
     using namespace enc_tc;
     const size_t ld = p.ld_qkv ? p.ld_qkv : (size_t)p.n_head * 64;
     if (ld < (size_t)p.n_head * 64 || ld % 8) return -1;
-    CUtensorMap mq, mk, mv;
+    if (((uintptr_t)p.out & 15) != 0) return -1;
+    CUtensorMap mq, mk, mv, mo;
     if (!make_map(&mq, p.q, p.n_batch, p.n_ctx, p.n_head, ld) || !make_map(&mk, p.k, p.n_batch, p.n_ctx, p.n_head, ld) ||
-        !make_map(&mv, p.v, p.n_batch, p.n_ctx, p.n_head, ld))
+        !make_map(&mv, p.v, p.n_batch, p.n_ctx, p.n_head, ld) ||
+        !make_out_map(&mo, p.out, p.n_batch, p.n_ctx, p.n_head, p.out_f16 != 0))
         return -1;
-    // the shared-memory opt-in is a per-device function attribute
     static std::mutex mu;
     static bool attr_set[64][2] = {};
     int dev = 0;
@@ -455,7 +502,7 @@ int enc_tc_launch(const EncTcParams& p, cudaStream_t st) {
     const long long n_items = (long long)p.n_batch * p.n_head * ((n_tiles + 1) / 2);
     if (n_items > (1ll << 30)) return -1;
     const int grid = (int)std::min<long long>(n_items, sm_count[dev] > 0 ? sm_count[dev] : 148);
-    kern<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mk, mv, p.out, p.n_ctx, p.n_head, (int)n_items, p.err);
+    kern<<<grid, THREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p.n_ctx, p.n_head, (int)n_items, p.err);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
