@@ -180,9 +180,18 @@ ZWG_API int zwg_q8_quantize(const float* w, size_t n, size_t k, int8_t* q, float
  * out[m][n] = x[m][k] . W[n][k]^T + bias[n], W = q * scale per block of 32; bias may be NULL.
  * Device pointers; x [m][k] and out [m][n] f32 row-major, k a multiple of 32, x and q
  * 16-byte aligned. f32 arithmetic; up to 15 rows of x stream the weight bytes once per 8
- * rows, 16 or more run as a register-tiled product (the weights read once per tile). */
+ * rows, 16 or more run as a tiled product (the weights read once per tile): on the tcgen05
+ * tensor cores when k is a multiple of 64 (each 32-wide block dot formed exactly from int8
+ * weights and three bf16 pieces of each activation, then scaled as the reference does),
+ * else on a register-tiled CUDA-core kernel. */
 ZWG_API int zwg_linear_q8(const float* x, size_t m, size_t k, const int8_t* q, const float* scales,
                           const float* bias, size_t n, float* out, void* stream);
+
+/* Whether the Q8 products of 16 or more rows with k a multiple of 64 (zwg_linear_q8, the
+ * decoder / LLM projections and the SiLU pair) run on the tcgen05 kernel (1, the default)
+ * or on the register-tiled CUDA-core kernel (0). Process-wide; returns the previous
+ * setting; a negative argument only queries it. */
+ZWG_API int zwg_q8_tensor_cores(int enable);
 
 /* ---- library-owned device state (the device-resident API) ---------------------------
  * The reference keeps its attention buffers inside the decoder and the LLM

@@ -154,6 +154,7 @@ SIGNATURES = {
     "zwg_selftest_timeout": (ctypes.c_int, []),
     "zwg_q8_quantize": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr]),
     "zwg_linear_q8": (ctypes.c_int, [c_ptr, c_size, c_size, c_ptr, c_ptr, c_ptr, c_size, c_ptr, c_ptr]),
+    "zwg_q8_tensor_cores": (ctypes.c_int, [ctypes.c_int]),
     "zwg_dec_state_create": (ctypes.c_int, [c_size, c_size, c_size, c_size, c_size, c_size, ctypes.POINTER(c_ptr)]),
     "zwg_dec_state_destroy": (ctypes.c_int, [c_ptr]),
     "zwg_dec_state_cache": (ctypes.c_int, [c_ptr, c_size, ctypes.POINTER(c_ptr), ctypes.POINTER(c_ptr),

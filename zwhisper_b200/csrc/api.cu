@@ -42,6 +42,12 @@ Ctx* cur() {
     return t_cur;
 }
 
+int* current_err_word() {
+    int dev = -1;
+    if (!t_cur || cudaGetDevice(&dev) != cudaSuccess || dev != t_cur->device) return nullptr;
+    return t_cur->err;
+}
+
 // Elements spanned by `rows` rows of `width` elements at `stride`.
 size_t span(size_t rows, size_t stride, size_t width) { return rows ? (rows - 1) * stride + width : 0; }
 

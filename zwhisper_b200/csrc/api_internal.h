@@ -80,6 +80,10 @@ struct Tickets {
 
 // The calling thread's context (zwg_init), or nullptr with the last error set.
 Ctx* cur();
+// The device error word of the calling thread's context when that context is on the current
+// device, else nullptr (no error is recorded either way). For launchers below the C API
+// that have no context argument.
+int* current_err_word();
 // Record the calling thread's last error (printf format); return ZWG_ERROR.
 int fail(const char* fmt, ...);
 int cuda_fail(const char* what, cudaError_t e);

@@ -148,6 +148,12 @@ int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const f
 int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, const float* sg, const float* bg,
                         const int8_t* wu, const float* su, const float* bu, size_t n_ff, float* out, int sm_count,
                         cudaStream_t st);
+// The same products on the tcgen05 tensor cores (q8_tc.cu) for m >= 16 and k a multiple of
+// 64 (wu/su/bu non-null: the SiLU pair). Returns 1 when the shape is not covered (the caller
+// runs the register-tiled kernel), 0 after a launch, -1 on a launch failure.
+int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
+                 int mode, const int8_t* wu, const float* su, const float* bu, float* out, int sm_count,
+                 cudaStream_t st);
 struct PairParams;
 // The RoPE pair of q8_pair_launch on the same tiles.
 int q8_gemm_rope_launch(const PairParams& p, int sm_count, cudaStream_t st);

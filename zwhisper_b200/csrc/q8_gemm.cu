@@ -644,6 +644,10 @@ int launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws
 // q8_linear_launch. Returns -1 on a bad argument or a launch failure.
 int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
                    int mode, float* out, int sm_count, cudaStream_t st) {
+    if (m > 0 && n > 0) {
+        const int r = q8_tc_launch(x, m, k, wq, ws, bias, n, mode, nullptr, nullptr, nullptr, out, sm_count, st);
+        if (r != 1) return r;
+    }
     const PairParams none{};
     return launch(x, m, k, wq, ws, bias, n, mode, q8g::PE_NONE, none, out, sm_count, st);
 }
@@ -652,6 +656,10 @@ int q8_gemm_launch(const float* x, size_t m, size_t k, const int8_t* wq, const f
 int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, const float* sg, const float* bg,
                         const int8_t* wu, const float* su, const float* bu, size_t n_ff, float* out, int sm_count,
                         cudaStream_t st) {
+    if (m > 0 && n_ff > 0 && wu) {
+        const int r = q8_tc_launch(x, m, k, wg, sg, bg, n_ff, LIN_STORE, wu, su, bu, out, sm_count, st);
+        if (r != 1) return r;
+    }
     PairParams pp{};
     pp.wq[0] = wg;
     pp.ws[0] = sg;

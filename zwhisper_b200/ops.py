@@ -143,6 +143,13 @@ def set_math(mode: str, device: int = 0) -> None:
     _lib.check(_lib.load().zwg_set_math(code))
 
 
+def q8_tensor_cores(enable: Optional[bool] = None) -> bool:
+    """Whether Q8 products of 16 or more rows with k a multiple of 64 run on the tcgen05
+    kernel (zwg_q8_tensor_cores, process-wide, default on). With an argument, sets it and
+    returns the previous setting; without, returns the current one."""
+    return bool(_lib.load().zwg_q8_tensor_cores(-1 if enable is None else int(bool(enable))))
+
+
 # ---- scratch sizers (src/ops.zig:545-560): device workspace in floats ----------------------
 
 def attention_workspace_bytes(sh: AttnShape, n_batch: int = 1) -> int:
