@@ -60,6 +60,10 @@ CASES = [
     (2, 16, 2, 128, 1024, 500, 77, True),     # group 8: 16 queries per tile, 128 rows
     (2, 4, 4, 64, 512, 0, 150, False),        # MHA, not causal, n_kv 150
     (1, 24, 2, 64, 768, 333, 100, True),      # group 12: 10 queries per tile, 120 rows
+    # more items than CTAs (one per SM): each CTA runs several query tiles in a row, the
+    # item-to-item hand-over of Q, the score buffers, O and the PV barriers
+    (16, 14, 2, 64, 2048, 1792, 208, True),   # 0.5B last chunk, 384 items
+    (16, 12, 2, 128, 2048, 1792, 208, True),  # 1.5B last chunk, 320 items
 ]
 
 

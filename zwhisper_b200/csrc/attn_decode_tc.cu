@@ -79,7 +79,7 @@ struct Smem {
     alignas(1024) uint8_t v[NST][Cfg<D>::V_BYTES];
     uint64_t q_full;
     uint64_t k_full[NST], k_empty[NST], v_full[NST], v_empty[NST];
-    uint64_t s_full[2], p_full[2], pv_done, drain;
+    uint64_t s_full[2], p_full[2], pv_done[2], drain;
     uint32_t tmem_base;
     int abort_flag;
     int last;
@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
             mbar_init(&sm.s_full[s], 1);
             mbar_init(&sm.p_full[s], 32);
         }
-        mbar_init(&sm.pv_done, 1);
+        mbar_init(&sm.pv_done[0], 1);
+        mbar_init(&sm.pv_done[1], 1);
         mbar_init(&sm.drain, 1);
         fence_mbar_init();
     }
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
                     const uint64_t bd = smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512);
                     mma_tf32_ts(tmem + O_COL, tmem + s * BN + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                mma_commit(&sm.pv_done);
+                mma_commit(&sm.pv_done[j & 1]);
                 mma_commit(&sm.v_empty[st]);
                 if (j + 2 < n_t && !(ok = issue_s(j + 2))) break;
             }
@@ -329,11 +330,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
             // PV(j - 1) must be done before O is rescaled; without a rescale P(j) is handed to
             // the MMA thread first (its buffer's last reader, PV(j - 2), is already done) and
             // the wait comes after, so PV(j) queues behind PV(j - 1) at once. Either way the
-            // warp waits for every PV once, in order, which keeps the parity waits exact.
+            // warp waits for every PV once, in order. PV completions alternate between two
+            // barriers, so PV(j) completing before the wait for PV(j - 1) cannot put that
+            // barrier's phase two ahead of the parity waited for.
             // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows must.
             const bool any_rescale = __any_sync(0xffffffffu, rescale);
             if (j > 0 && any_rescale) {
-                if (!(ok = mbar_wait_warp(&sm.pv_done, (j - 1) & 1, err))) break;
+                if (!(ok = mbar_wait_warp(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, err))) break;
                 tc_fence_after();
 #pragma unroll
                 for (int cc = 0; cc < D / 32; cc++) {
@@ -359,11 +362,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
             tc_fence_before();
             mbar_arrive(&sm.p_full[s]);
             if (j > 0 && !any_rescale) {
-                if (!(ok = mbar_wait_warp(&sm.pv_done, (j - 1) & 1, err))) break;
+                if (!(ok = mbar_wait_warp(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, err))) break;
                 tc_fence_after();
             }
         }
-        if (ok) ok = mbar_wait_warp(&sm.pv_done, (n_t - 1) & 1, err);
+        if (ok) ok = mbar_wait_warp(&sm.pv_done[(n_t - 1) & 1], ((n_t - 1) >> 1) & 1, err);
         if (ok) {
             // ---- epilogue: the output (one piece) or this piece's partial
             tc_fence_after();

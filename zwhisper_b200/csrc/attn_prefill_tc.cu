@@ -12,25 +12,32 @@
 // second copy of the cache exists.
 //   - A tile is 128 rows = qn consecutive queries x the `group` query heads of one kv head
 //     (row = query * group + head-in-group), so one K/V tile feeds every head of the group
-//     and the rows of a tile share nearly the same causal limit. Q comes in by one 4-d TMA
-//     box per 32-column chunk ([qn][group][32 floats], 128-byte swizzle): exactly the
-//     K-major A operand.
-//   - K^T tiles are 64 keys x d, loaded as two [d][32 keys] boxes: the MN-major B operand
-//     of S = Q K^T, read straight from the transposed cache. V tiles are 64 keys x d, loaded
-//     as [64 keys][32 columns] boxes: the MN-major B operand of O += P V. An MN-major tf32
+//     and the rows of a tile share nearly the same causal limit. Key tiles are 128 wide: a
+//     score MMA of N = 128 runs near the full tf32 rate, where N = 64 with an MN-major B
+//     operand measured half of it.
+//   - Q lives in TMEM (row m in lane m, one f32 per column): the softmax warps load each
+//     item's rows from global memory and store them with tcgen05.st, and S = Q K^T is the
+//     A-from-TMEM form of tcgen05.mma. Shared memory then holds only the K/V ring.
+//   - K^T tiles are [d][128 keys] (four [d][32 keys] boxes): the MN-major B operand of
+//     S = Q K^T, read straight from the transposed cache. V tiles are [128 keys][d] (d / 32
+//     boxes of [128 keys][32 columns]): the MN-major B operand of O += P V. An MN-major tf32
 //     operand must be in the 128-byte swizzle with 32-byte atoms (descriptor layout 1, TMA
 //     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B); the 16-byte-atom swizzle that serves K-major
 //     operands gives an MMA that writes zeros.
-//   - TMEM: two 64-column score buffers (S of tile j in buffer j % 2; the softmax writes the
-//     probabilities P back over the scores as tf32, and P is the TMEM A operand of the PV
-//     MMA) and a d-column O accumulator: 256 columns.
-//   - Warp 0: TMA producer (lane 0: Q and K^T, lane 1: V, each with its own 2-stage ring,
-//     so a K^T load never waits behind a V slot). Warp 1: TMEM allocation and the single
-//     MMA-issuing thread, order S0 S1 | PV0 S2 | PV1 S3 ...: the next scores are computed
-//     while the softmax works on the current ones, and S(j+2) overwrites buffer j % 2 only
-//     after PV(j) in issue order (tcgen05.mma from one thread executes in order). Warps
-//     2-5: softmax, one thread per row (TMEM lane), online max in base 2 kept stale unless
-//     it grows by more than 2^8, exp2 on the MUFU, P rounded to tf32 (round to nearest).
+//   - One ring of slots (a K^T or V tile each: three of 64 KB at d = 128, six of 32 KB at
+//     d = 64) holds the tiles in the order the MMAs consume them: K0 K1 V0 K2 V1 K3 ...
+//     V(n-1). A slot is released by the commit of the MMAs that read it. (Parts of 32 KB
+//     released half-way through a tile measured slower at d = 128: 0.46 against 0.34 ms.)
+//   - TMEM: Q (d columns), two 128-column score buffers (S of tile j in buffer j % 2; the
+//     softmax writes the probabilities P back over the scores as tf32, and P is the TMEM A
+//     operand of the PV MMA) and a d-column O accumulator: 512 columns, one CTA per SM.
+//   - Warp 0 lane 0: TMA producer. Warp 1: TMEM allocation and the single MMA-issuing
+//     thread, order S0 S1 | PV0 S2 | PV1 S3 ...: the next scores are computed while the
+//     softmax works on the current ones, and S(j+2) overwrites buffer j % 2 only after PV(j)
+//     in issue order (tcgen05.mma from one thread executes in order). Warps 2-5: Q into
+//     TMEM, then the softmax, one thread per row (TMEM lane), online max in base 2 kept
+//     stale unless it grows by more than 2^8, exp2 on the MUFU, P rounded to tf32 (round to
+//     nearest), and the epilogue O / l.
 //   - Persistent grid over (sequence, kv head, query tile) items, a pair's tiles adjacent.
 // Every wait is bounded; a wait that runs out records kErrTimeout, the CTA drains its own
 // copies and MMAs with bounded waits, frees TMEM and returns.
@@ -50,31 +57,40 @@ namespace prefill_tc {
 using namespace sm100;
 
 constexpr int BM = 128;                // rows per tile = TMEM lanes
-constexpr int BN = 64;                 // keys per tile
+constexpr int BN = 128;                // keys per tile
 constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
-constexpr uint32_t TMEM_COLS = 256;    // S/P buffers 2 x 64 columns, O up to 128 columns
-constexpr uint32_t O_COL = 2 * BN;
 
+// Pairs of exponentials per 16 evaluated by exp2_poly2 on the FMA pipe (relative error
+// 1e-4, below tf32's rounding of P); the others use the MUFU ex2, 16 per clock per SM.
+constexpr int POLY_PAIRS = 4;
+
+// A non-negative f32 rounded to tf32 (nearest, ties away from zero) with integer operations,
+// which keeps the conversion off the pipe the MUFU exponentials use.
+__device__ __forceinline__ uint32_t tf32_rna_pos(float v) { return (__float_as_uint(v) + 0x1000u) & 0xffffe000u; }
+
+// Two score buffers (S(j+1) is computed while the softmax works on S(j)), one CTA per SM
+// with 512 TMEM columns; the ring has three 64 KB slots at d = 128, six 32 KB slots at
+// d = 64. (Measured at d = 64, config 3's last chunk: one score buffer with two CTAs per SM
+// and 256 columns each took 0.104 ms against 0.096 ms for this layout.)
 template <int D>
 struct Cfg {
-    static constexpr uint32_t Q_CHUNK = BM * 128;           // [128 rows][32 floats]
-    static constexpr uint32_t Q_BYTES = (D / 32) * Q_CHUNK;
+    static constexpr int SBUF = 2;                          // score buffers
+    static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t K_CHUNK = D * 128;            // [D rows][32 keys]
-    static constexpr uint32_t K_BYTES = 2 * K_CHUNK;
-    static constexpr uint32_t V_CHUNK = BN * 128;           // [64 keys][32 floats]
-    static constexpr uint32_t V_BYTES = (D / 32) * V_CHUNK;
-    // d = 64: 96 KB of tiles, two CTAs per SM; d = 128: 192 KB, one
-    static constexpr int CTAS_PER_SM = D == 64 ? 2 : 1;
+    static constexpr uint32_t V_CHUNK = BN * 128;           // [128 keys][32 floats]
+    static constexpr uint32_t SLOT = BN * D * 4;            // one K^T or V tile
+    static constexpr int NSLOT = D == 128 ? 3 : 6;
+    static constexpr uint32_t Q_COL = 0;
+    static constexpr uint32_t S_COL = D;                    // + buffer * BN
+    static constexpr uint32_t O_COL = D + SBUF * BN;
+    static_assert(O_COL + D <= TMEM_COLS, "TMEM columns");
 };
 
 template <int D>
 struct Smem {
-    alignas(1024) uint8_t q[Cfg<D>::Q_BYTES];
-    alignas(1024) uint8_t k[2][Cfg<D>::K_BYTES];
-    alignas(1024) uint8_t v[2][Cfg<D>::V_BYTES];
-    uint64_t q_full, q_empty;
-    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-    uint64_t s_full[2], p_full[2], pv_done, drain;
+    alignas(1024) uint8_t ring[Cfg<D>::NSLOT][Cfg<D>::SLOT];
+    uint64_t full[Cfg<D>::NSLOT], empty[Cfg<D>::NSLOT];
+    uint64_t q_full, s_full[Cfg<D>::SBUF], p_full[Cfg<D>::SBUF], pv_done[2], drain;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -85,6 +101,8 @@ constexpr size_t smem_bytes() {
 }
 
 struct Args {
+    const float* q;
+    size_t q_stride, q_bs;
     float* out;
     size_t out_stride, out_bs;
     int n_q, n_kv, n_head_kv, group, qn, rows, n_mt, n_items, causal;
@@ -115,10 +133,10 @@ __device__ __forceinline__ int item_tiles(const Args& a, int mt) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const Args a) {
+__global__ void __launch_bounds__(THREADS, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Args a) {
     using C = Cfg<D>;
+    constexpr int NS = C::NSLOT;
     extern __shared__ uint8_t smem_raw[];
     Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
@@ -130,33 +148,23 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
     __syncthreads();
     if (sm.abort_flag) return;
 
-    // Rows of the Q tile the loads never write (qn * group < 128 when 128 is not a multiple
-    // of the group) are zeroed once, so their scores stay finite.
-    if (a.rows < BM) {
-        const int n16 = (BM - a.rows) * 8;  // 16-byte words per chunk
-        for (int c = 0; c < D / 32; c++) {
-            uint4* p = reinterpret_cast<uint4*>(sm.q + c * C::Q_CHUNK + a.rows * 128);
-            for (int i = threadIdx.x; i < n16; i += THREADS) p[i] = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-    }
     if (threadIdx.x == 0) {
-        mbar_init(&sm.q_full, 1);
-        mbar_init(&sm.q_empty, 1);
-        for (int s = 0; s < 2; s++) {
-            mbar_init(&sm.k_full[s], 1);
-            mbar_init(&sm.k_empty[s], 1);
-            mbar_init(&sm.v_full[s], 1);
-            mbar_init(&sm.v_empty[s], 1);
+        for (int s = 0; s < NS; s++) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        mbar_init(&sm.q_full, 128);
+        for (int s = 0; s < C::SBUF; s++) {
             mbar_init(&sm.s_full[s], 1);
             mbar_init(&sm.p_full[s], 128);
         }
-        mbar_init(&sm.pv_done, 1);
+        mbar_init(&sm.pv_done[0], 1);
+        mbar_init(&sm.pv_done[1], 1);
         mbar_init(&sm.drain, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(&sm.tmem_base, TMEM_COLS);
+        tmem_alloc(&sm.tmem_base, C::TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -165,63 +173,49 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
     const uint32_t tmem = sm.tmem_base;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producers
-        // Each lane counts the loads it issued per barrier, and at exit (normal or not) waits
-        // for the last of them, so no copy is in flight when the CTA releases its memory.
+        // ------------------------------------------------------------ TMA producer
+        // Loads go into the ring in the order the MMAs consume them; at exit (normal or not)
+        // the last loads are waited for, so no copy is in flight when the CTA's memory goes.
         if (lane == 0) {
-            prefetch_tmap(&tm_q);
             prefetch_tmap(&tm_k);
-            uint32_t g = 0, n_q_loads = 0, n_k_loads = 0;  // K^T tile n goes to stage n % 2
-            bool ok = true;
-            for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
-                int b, kh, mt;
-                item_of(a, idx, b, kh, mt);
-                const int n_t = item_tiles(a, mt);
-                if (n_q_loads > 0 && !(ok = mbar_wait(&sm.q_empty, (n_q_loads - 1) & 1, err))) break;
-                mbar_arrive_expect_tx(&sm.q_full, (D / 32) * a.rows * 128);
-                for (int c = 0; c < D / 32; c++)
-                    tma_load_4d(&tm_q, &sm.q_full, sm.q + c * C::Q_CHUNK, c * 32, kh * a.group, mt * a.qn, b);
-                n_q_loads++;
-                for (int j = 0; j < n_t; j++) {
-                    const uint32_t gj = g + j, s = gj & 1;
-                    if (gj >= 2 && !(ok = mbar_wait(&sm.k_empty[s], ((gj >> 1) - 1) & 1, err))) break;
-                    mbar_arrive_expect_tx(&sm.k_full[s], C::K_BYTES);
-                    tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s], j * BN, kh * D, b);
-                    tma_load_3d(&tm_k, &sm.k_full[s], sm.k[s] + C::K_CHUNK, j * BN + 32, kh * D, b);
-                    n_k_loads++;
-                }
-                g += n_t;
-            }
-            if (n_q_loads > 0) mbar_wait_drain(&sm.q_full, (n_q_loads - 1) & 1);
-            if (n_k_loads > 0) mbar_wait_drain(&sm.k_full[0], (((n_k_loads + 1) >> 1) - 1) & 1);
-            if (n_k_loads > 1) mbar_wait_drain(&sm.k_full[1], ((n_k_loads >> 1) - 1) & 1);
-        } else if (lane == 1) {
             prefetch_tmap(&tm_v);
-            uint32_t g = 0, n_v_loads = 0;
+            uint32_t n = 0;
             bool ok = true;
+            auto load = [&](bool is_k, int j, int b, int kh) -> bool {
+                const uint32_t slot = n % NS;
+                if (n >= (uint32_t)NS && !mbar_wait(&sm.empty[slot], ((n / NS) - 1) & 1, err)) return false;
+                mbar_arrive_expect_tx(&sm.full[slot], C::SLOT);
+                uint8_t* dst = sm.ring[slot];
+                if (is_k) {
+#pragma unroll
+                    for (int c = 0; c < BN / 32; c++)
+                        tma_load_3d(&tm_k, &sm.full[slot], dst + c * C::K_CHUNK, j * BN + c * 32, kh * D, b);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < D / 32; c++)
+                        tma_load_3d(&tm_v, &sm.full[slot], dst + c * C::V_CHUNK, kh * D + c * 32, j * BN, b);
+                }
+                n++;
+                return true;
+            };
             for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
                 int b, kh, mt;
                 item_of(a, idx, b, kh, mt);
                 const int n_t = item_tiles(a, mt);
-                for (int j = 0; j < n_t; j++) {
-                    const uint32_t gj = g + j, s = gj & 1;
-                    if (gj >= 2 && !(ok = mbar_wait(&sm.v_empty[s], ((gj >> 1) - 1) & 1, err))) break;
-                    mbar_arrive_expect_tx(&sm.v_full[s], C::V_BYTES);
-                    for (int c = 0; c < D / 32; c++)
-                        tma_load_3d(&tm_v, &sm.v_full[s], sm.v[s] + c * C::V_CHUNK, kh * D + c * 32, j * BN, b);
-                    n_v_loads++;
+                for (int j = 0; ok && j < C::SBUF && j < n_t; j++) ok = load(true, j, b, kh);
+                for (int j = 0; ok && j < n_t; j++) {
+                    ok = load(false, j, b, kh);
+                    if (ok && j + C::SBUF < n_t) ok = load(true, j + C::SBUF, b, kh);
                 }
-                g += n_t;
             }
-            if (n_v_loads > 0) mbar_wait_drain(&sm.v_full[0], (((n_v_loads + 1) >> 1) - 1) & 1);
-            if (n_v_loads > 1) mbar_wait_drain(&sm.v_full[1], ((n_v_loads >> 1) - 1) & 1);
+            for (uint32_t i = n > (uint32_t)NS ? n - NS : 0; i < n; i++) mbar_wait_drain(&sm.full[i % NS], (i / NS) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_tf32(BM, BN, false, true);
             constexpr uint32_t idesc_o = idesc_tf32(BM, D, false, true);
-            uint32_t g = 0;
+            uint32_t n = 0, g = 0;
             int it = 0;
             bool ok = true;
             for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x, it++) {
@@ -229,40 +223,39 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
                 item_of(a, idx, b, kh, mt);
                 const int n_t = item_tiles(a, mt);
                 if (!(ok = mbar_wait(&sm.q_full, it & 1, err))) break;
-                const uint32_t q_addr = smem_u32(sm.q);
-                // S(j) = Q K^T(j) into score buffer (g + j) % 2
+                tc_fence_after();
+                // S(j) = Q K^T(j) into score buffer (g + j) % SBUF
                 auto issue_s = [&](int j) -> bool {
-                    const uint32_t gj = g + j, s = gj & 1;
-                    if (!mbar_wait(&sm.k_full[s], (gj >> 1) & 1, err)) return false;
+                    const uint32_t s = (g + j) % C::SBUF, slot = n % NS;
+                    if (!mbar_wait(&sm.full[slot], (n / NS) & 1, err)) return false;
                     tc_fence_after();
-                    const uint32_t k_addr = smem_u32(sm.k[s]);
+                    const uint32_t k_addr = smem_u32(sm.ring[slot]);
 #pragma unroll
-                    for (int kk = 0; kk < D / 8; kk++) {
-                        const uint64_t ad = smem_desc_sw128(q_addr + (kk >> 2) * C::Q_CHUNK + (kk & 3) * 32, 16, 1024);
-                        const uint64_t bd = smem_desc_sw128_32b(k_addr + kk * 1024, C::K_CHUNK, 512);
-                        mma_tf32_ss(tmem + s * BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
-                    }
-                    mma_commit(&sm.k_empty[s]);
+                    for (int kk = 0; kk < D / 8; kk++)
+                        mma_tf32_ts(tmem + C::S_COL + s * BN, tmem + C::Q_COL + kk * 8,
+                                    smem_desc_sw128_32b(k_addr + kk * 1024, C::K_CHUNK, 512), idesc_s, kk > 0 ? 1u : 0u);
+                    mma_commit(&sm.empty[slot]);
                     mma_commit(&sm.s_full[s]);
-                    if (j == n_t - 1) mma_commit(&sm.q_empty);  // the next item's Q may load
+                    n++;
                     return true;
                 };
-                ok = issue_s(0);
-                if (ok && n_t > 1) ok = issue_s(1);
+                for (int j = 0; ok && j < C::SBUF && j < n_t; j++) ok = issue_s(j);
                 for (int j = 0; ok && j < n_t; j++) {
-                    const uint32_t gj = g + j, s = gj & 1;
-                    if (!(ok = mbar_wait(&sm.p_full[s], (gj >> 1) & 1, err))) break;
-                    if (!(ok = mbar_wait(&sm.v_full[s], (gj >> 1) & 1, err))) break;
+                    const uint32_t gj = g + j, s = gj % C::SBUF;
+                    if (!(ok = mbar_wait(&sm.p_full[s], (gj / C::SBUF) & 1, err))) break;
+                    const uint32_t slot = n % NS;
+                    if (!(ok = mbar_wait(&sm.full[slot], (n / NS) & 1, err))) break;
                     tc_fence_after();
-                    const uint32_t v_addr = smem_u32(sm.v[s]);
+                    const uint32_t v_addr = smem_u32(sm.ring[slot]);
 #pragma unroll
-                    for (int kk = 0; kk < BN / 8; kk++) {
-                        const uint64_t bd = smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512);
-                        mma_tf32_ts(tmem + O_COL, tmem + s * BN + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    mma_commit(&sm.pv_done);
-                    mma_commit(&sm.v_empty[s]);
-                    if (j + 2 < n_t && !(ok = issue_s(j + 2))) break;
+                    for (int kk = 0; kk < BN / 8; kk++)
+                        mma_tf32_ts(tmem + C::O_COL, tmem + C::S_COL + s * BN + kk * 8,
+                                    smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512), idesc_o,
+                                    (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_commit(&sm.empty[slot]);
+                    n++;
+                    mma_commit(&sm.pv_done[gj & 1]);
+                    if (j + C::SBUF < n_t && !(ok = issue_s(j + C::SBUF))) break;
                 }
                 g += n_t;
             }
@@ -286,35 +279,56 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
             const int i = mt * a.qn + il;
             const bool valid = row < a.rows && i < a.n_q;
             const int lim = a.causal ? min(a.n_kv - a.n_q + min(i, a.n_q - 1) + 1, a.n_kv) : a.n_kv;
+            // ---- this item's Q rows into TMEM (zeros for rows past the tile or the chunk);
+            // the previous item's score MMAs, the last readers of Q, completed before its
+            // last tile's scores were seen
+            {
+                const float* qrow = a.q + (size_t)b * a.q_bs + (size_t)(valid ? i : 0) * a.q_stride +
+                                    (size_t)(valid ? kh * a.group + hg : 0) * D;
+#pragma unroll
+                for (int cc = 0; cc < D / 32; cc++) {
+                    uint32_t v[32];
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4) {
+                        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (valid) f = __ldg(reinterpret_cast<const float4*>(qrow + cc * 32 + e));
+                        v[e] = __float_as_uint(f.x);
+                        v[e + 1] = __float_as_uint(f.y);
+                        v[e + 2] = __float_as_uint(f.z);
+                        v[e + 3] = __float_as_uint(f.w);
+                    }
+                    tmem_st32(tmem + lane_addr + C::Q_COL + cc * 32, v);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&sm.q_full);
+            }
             float m = 0.f, l = 0.f;
             for (int j = 0; j < n_t; j++) {
-                const uint32_t gj = g + j, s = gj & 1;
-                if (!(ok = mbar_wait_warp(&sm.s_full[s], (gj >> 1) & 1, err))) break;
+                const uint32_t gj = g + j, s = gj % C::SBUF;
+                if (!(ok = mbar_wait_warp(&sm.s_full[s], (gj / C::SBUF) & 1, err))) break;
                 tc_fence_after();
-                const uint32_t s_addr = tmem + lane_addr + s * BN;
-                uint32_t sr[64];
-                {
-                    uint32_t x[32], y[32];
-                    tmem_ld32(s_addr, x);
-                    tmem_ld32(s_addr + 32, y);
+                const uint32_t s_addr = tmem + lane_addr + C::S_COL + s * BN;
+                uint32_t sr[BN];
+#pragma unroll
+                for (int q4 = 0; q4 < BN / 32; q4++) {
+                    uint32_t x[32];
+                    tmem_ld32(s_addr + q4 * 32, x);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; e++) {
-                        sr[e] = x[e];
-                        sr[32 + e] = y[e];
-                    }
+                    for (int e = 0; e < 32; e++) sr[q4 * 32 + e] = x[e];
                 }
                 const int valid_keys = lim - j * BN;
                 if (valid_keys < BN) {
 #pragma unroll
-                    for (int e = 0; e < 64; e++)
+                    for (int e = 0; e < BN; e++)
                         if (e >= valid_keys) sr[e] = __float_as_uint(-INFINITY);
                 }
                 float mx[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) mx[e] = __uint_as_float(sr[e]);
 #pragma unroll
-                for (int e = 8; e < 64; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sr[e]));
+                for (int e = 8; e < BN; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sr[e]));
 #pragma unroll
                 for (int e = 0; e < 4; e++) mx[e] = fmaxf(mx[e], mx[e + 4]);
                 const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;
@@ -328,57 +342,65 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
                     m = m_tile;
                     rescale = true;
                 }
-                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+                float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
 #pragma unroll
-                for (int e = 0; e < 64; e++) {
-                    const uint32_t p = to_tf32(exp2_approx(fmaf(__uint_as_float(sr[e]), c, -m)));
-                    ls[e & 3] += __uint_as_float(p);
-                    sr[e] = p;
+                for (int e = 0; e < BN; e += 2) {
+                    const float2 x =
+                        __ffma2_rn(make_float2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), c2, nm2);
+                    const float2 pe = (((e >> 1) & 15) < POLY_PAIRS) ? exp2_poly2(x)
+                                                                    : make_float2(exp2_approx(x.x), exp2_approx(x.y));
+                    const uint32_t p0 = tf32_rna_pos(pe.x), p1 = tf32_rna_pos(pe.y);
+                    ls2[(e >> 1) & 1] = __fadd2_rn(ls2[(e >> 1) & 1], make_float2(__uint_as_float(p0), __uint_as_float(p1)));
+                    sr[e] = p0;
+                    sr[e + 1] = p1;
                 }
-                l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+                l = l * corr + ((ls2[0].x + ls2[0].y) + (ls2[1].x + ls2[1].y));
                 // PV(j - 1) must be done before O is rescaled; without a rescale P(j) is handed
-                // to the MMA thread first (its buffer's last reader, PV(j - 2), is already done)
-                // and the wait comes after, so PV(j) queues behind PV(j - 1) at once. Either way
-                // the warp waits for every PV once, in order, which keeps the parity waits exact.
+                // to the MMA thread first (its buffer's last reader, PV(j - SBUF), is already
+                // done) and the wait comes after, so PV(j) queues behind PV(j - 1) at once.
+                // Either way the warp waits for every PV once, in order. PV completions
+                // alternate between two barriers: PV(j) may complete before this warp's wait
+                // for PV(j - 1) (it needs only the other warps' p_full), and on one barrier
+                // that would put the phase two ahead of the parity being waited for; the
+                // next completion on PV(j - 1)'s barrier is PV(j + 1), which needs this warp.
                 // tcgen05.ld/st are warp-collective: the warp rescales if any of its rows must
                 // (corr is 1 in the others).
                 const bool any_rescale = __any_sync(0xffffffffu, rescale);
                 if (j > 0 && any_rescale) {
-                    if (!(ok = mbar_wait_warp(&sm.pv_done, (gj - 1) & 1, err))) break;
+                    if (!(ok = mbar_wait_warp(&sm.pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1, err))) break;
                     tc_fence_after();
                 }
                 if (any_rescale) {
 #pragma unroll
                     for (int cc = 0; cc < D / 32; cc++) {
                         uint32_t o[32];
-                        tmem_ld32(tmem + lane_addr + O_COL + cc * 32, o);
+                        tmem_ld32(tmem + lane_addr + C::O_COL + cc * 32, o);
                         tmem_ld_wait();
 #pragma unroll
                         for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-                        tmem_st32(tmem + lane_addr + O_COL + cc * 32, o);
+                        tmem_st32(tmem + lane_addr + C::O_COL + cc * 32, o);
                     }
                 }
-                {
-                    uint32_t x[32], y[32];
 #pragma unroll
-                    for (int e = 0; e < 32; e++) {
-                        x[e] = sr[e];
-                        y[e] = sr[32 + e];
-                    }
-                    tmem_st32(s_addr, x);
-                    tmem_st32(s_addr + 32, y);
+                for (int q4 = 0; q4 < BN / 32; q4++) {
+                    uint32_t x[32];
+#pragma unroll
+                    for (int e = 0; e < 32; e++) x[e] = sr[q4 * 32 + e];
+                    tmem_st32(s_addr + q4 * 32, x);
                 }
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&sm.p_full[s]);
                 if (j > 0 && !any_rescale) {
-                    if (!(ok = mbar_wait_warp(&sm.pv_done, (gj - 1) & 1, err))) break;
+                    if (!(ok = mbar_wait_warp(&sm.pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1, err))) break;
                     tc_fence_after();
                 }
             }
             if (!ok) break;
             // ---- epilogue: O / l -> out[b][i][(kh * group + hg) * D ..]
-            if (!(ok = mbar_wait_warp(&sm.pv_done, (g + n_t - 1) & 1, err))) break;
+            const uint32_t g_last = g + n_t - 1;
+            if (!(ok = mbar_wait_warp(&sm.pv_done[g_last & 1], (g_last >> 1) & 1, err))) break;
             tc_fence_after();
             const float inv = l > 0.f ? 1.0f / l : 0.f;
             float* orow = a.out + (size_t)b * a.out_bs + (size_t)(valid ? i : 0) * a.out_stride +
@@ -386,7 +408,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
 #pragma unroll
             for (int cc = 0; cc < D / 32; cc++) {
                 uint32_t o[32];
-                tmem_ld32(tmem + lane_addr + O_COL + cc * 32, o);
+                tmem_ld32(tmem + lane_addr + C::O_COL + cc * 32, o);
                 tmem_ld_wait();
                 if (valid) {
 #pragma unroll
@@ -406,7 +428,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
@@ -452,14 +474,10 @@ int launch_d(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaS
     const size_t q_bs = n_batch > 1 ? p.q_bs : p.n_q * p.q_stride;
     const size_t k_bs = n_batch > 1 ? p.k_bs : p.n_head_kv * p.d * p.kt_stride;
     const size_t v_bs = n_batch > 1 ? p.v_bs : p.n_kv * p.kv_stride;
-    CUtensorMap mq, mk, mv;
-    {
-        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)p.n_head, (cuuint64_t)p.n_q, (cuuint64_t)n_batch};
-        cuuint64_t strides[3] = {(cuuint64_t)D * 4, (cuuint64_t)p.q_stride * 4, (cuuint64_t)q_bs * 4};
-        cuuint32_t box[4] = {32, (cuuint32_t)group, (cuuint32_t)qn, 1};
-        if (!encode(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
-            return -1;
-    }
+    a.q = p.q;
+    a.q_stride = p.q_stride;
+    a.q_bs = q_bs;
+    CUtensorMap mk, mv;
     {
         cuuint64_t dims[3] = {(cuuint64_t)p.n_kv, (cuuint64_t)(p.n_head_kv * D), (cuuint64_t)n_batch};
         cuuint64_t strides[2] = {(cuuint64_t)p.kt_stride * 4, (cuuint64_t)k_bs * 4};
@@ -490,9 +508,9 @@ int launch_d(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaS
             attr_set[dev] = true;
         }
     }
-    const int slots = (sm_count > 0 ? sm_count : 148) * Cfg<D>::CTAS_PER_SM;
+    const int slots = sm_count > 0 ? sm_count : 148;
     const int grid = (int)std::min<long long>(n_items, slots);
-    prefill_tc_kernel<D><<<grid, THREADS, smem_bytes<D>(), st>>>(mq, mk, mv, a);
+    prefill_tc_kernel<D><<<grid, THREADS, smem_bytes<D>(), st>>>(mk, mv, a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

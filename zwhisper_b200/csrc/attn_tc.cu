@@ -82,27 +82,6 @@ __host__ __device__ constexpr uint32_t o_col(int t) { return t ? 448u : 192u; }
 #endif
 constexpr int POLY_PAIRS = ZWG_POLY_PAIRS;
 
-// 2^x from a Cody-Waite split x = j + f (j = round(x), |f| <= 0.5) and a degree-3 minimax
-// polynomial for 2^f fitted here (max relative error 1.0e-4, well below bf16 rounding of
-// P); 2^j is added into the exponent field. Inputs are clamped at -120 (so -inf gives
-// ~7.5e-37 rather than a wrapped exponent). Packed f32x2 arithmetic, two values at once.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
-    x.x = fmaxf(x.x, -120.f);
-    x.y = fmaxf(x.y, -120.f);
-    const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
-    const float2 r = __fadd2_rn(t, make_float2(-kRound, -kRound));
-    const float2 f = __ffma2_rn(r, make_float2(-1.f, -1.f), x);
-    float2 p = __ffma2_rn(make_float2(0.05500858277f, 0.05500858277f), f,
-                          make_float2(0.24221037328f, 0.24221037328f));
-    p = __ffma2_rn(p, f, make_float2(0.69328290224f, 0.69328290224f));
-    p = __ffma2_rn(p, f, make_float2(1.f, 1.f));
-    // the low bits of t hold j; shifting them into the exponent field scales by 2^j
-    p.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
-    p.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
-    return p;
-}
-
 struct Smem {
     uint8_t q[2][2][TILE_BYTES];  // [buffer][query tile], 1024-byte aligned tiles
     uint8_t k[NS][TILE_BYTES];
