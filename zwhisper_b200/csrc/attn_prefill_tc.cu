@@ -270,8 +270,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         const float c = 1.4426950408889634f * (D == 64 ? 0.125f : 0.08838834764831845f);  // log2(e)/sqrt(d)
         const int il = row / a.group, hg = row - il * a.group;
+        // An item's Q rows into TMEM (zeros for rows past the tile or the chunk). The next
+        // item's rows are written as soon as this item's last scores have been seen (its
+        // score MMAs, the last readers of Q, are complete), before this item's epilogue, so
+        // the next item's first score tiles are computed while the epilogue runs.
+        auto load_q = [&](int qidx) {
+            int qb, qkh, qmt;
+            item_of(a, qidx, qb, qkh, qmt);
+            const int qi = qmt * a.qn + il;
+            const bool qvalid = row < a.rows && qi < a.n_q;
+            const float* qrow = a.q + (size_t)qb * a.q_bs + (size_t)(qvalid ? qi : 0) * a.q_stride +
+                                (size_t)(qvalid ? qkh * a.group + hg : 0) * D;
+#pragma unroll
+            for (int cc = 0; cc < D / 32; cc++) {
+                uint32_t v[32];
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (qvalid) f = __ldg(reinterpret_cast<const float4*>(qrow + cc * 32 + e));
+                    v[e] = __float_as_uint(f.x);
+                    v[e + 1] = __float_as_uint(f.y);
+                    v[e + 2] = __float_as_uint(f.z);
+                    v[e + 3] = __float_as_uint(f.w);
+                }
+                tmem_st32(tmem + lane_addr + C::Q_COL + cc * 32, v);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&sm.q_full);
+        };
         uint32_t g = 0;
         bool ok = true;
+        if ((int)blockIdx.x < a.n_items) load_q(blockIdx.x);
         for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
             int b, kh, mt;
             item_of(a, idx, b, kh, mt);
@@ -279,30 +309,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int i = mt * a.qn + il;
             const bool valid = row < a.rows && i < a.n_q;
             const int lim = a.causal ? min(a.n_kv - a.n_q + min(i, a.n_q - 1) + 1, a.n_kv) : a.n_kv;
-            // ---- this item's Q rows into TMEM (zeros for rows past the tile or the chunk);
-            // the previous item's score MMAs, the last readers of Q, completed before its
-            // last tile's scores were seen
-            {
-                const float* qrow = a.q + (size_t)b * a.q_bs + (size_t)(valid ? i : 0) * a.q_stride +
-                                    (size_t)(valid ? kh * a.group + hg : 0) * D;
-#pragma unroll
-                for (int cc = 0; cc < D / 32; cc++) {
-                    uint32_t v[32];
-#pragma unroll
-                    for (int e = 0; e < 32; e += 4) {
-                        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (valid) f = __ldg(reinterpret_cast<const float4*>(qrow + cc * 32 + e));
-                        v[e] = __float_as_uint(f.x);
-                        v[e + 1] = __float_as_uint(f.y);
-                        v[e + 2] = __float_as_uint(f.z);
-                        v[e + 3] = __float_as_uint(f.w);
-                    }
-                    tmem_st32(tmem + lane_addr + C::Q_COL + cc * 32, v);
-                }
-                tmem_st_wait();
-                tc_fence_before();
-                mbar_arrive(&sm.q_full);
-            }
             float m = 0.f, l = 0.f;
             for (int j = 0; j < n_t; j++) {
                 const uint32_t gj = g + j, s = gj % C::SBUF;
@@ -398,6 +404,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
             if (!ok) break;
+            if (idx + (int)gridDim.x < a.n_items) load_q(idx + gridDim.x);
             // ---- epilogue: O / l -> out[b][i][(kh * group + hg) * D ..]
             const uint32_t g_last = g + n_t - 1;
             if (!(ok = mbar_wait_warp(&sm.pv_done[g_last & 1], (g_last >> 1) & 1, err))) break;
