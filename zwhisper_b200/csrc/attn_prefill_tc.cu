@@ -62,7 +62,11 @@ constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 soft
 
 // Pairs of exponentials per 16 evaluated by exp2_poly2 on the FMA pipe (relative error
 // 1e-4, below tf32's rounding of P); the others use the MUFU ex2, 16 per clock per SM.
-constexpr int POLY_PAIRS = 4;
+// Measured on B200 (last chunk of a 2000-token prompt; ms at d = 128 / d = 64): 0 -> 0.321 /
+// 0.0887, 1 -> 0.323 / 0.0882, 2 -> 0.326 / 0.0900, 3 -> 0.335 / 0.0927, 4 -> 0.331 /
+// 0.0970, 8 -> 0.344 / 0.1078. With the tf32 rounding done by integer operations the MUFU
+// is no longer the limit here (it was: cvt.rna.tf32 shared it with ex2).
+constexpr int POLY_PAIRS = 1;
 
 // A non-negative f32 rounded to tf32 (nearest, ties away from zero) with integer operations,
 // which keeps the conversion off the pipe the MUFU exponentials use.
