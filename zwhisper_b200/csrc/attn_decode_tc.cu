@@ -266,10 +266,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
                     const float4 f = valid ? __ldg(qrow + cc * 8 + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    r[4 * e] = to_tf32(f.x);
-                    r[4 * e + 1] = to_tf32(f.y);
-                    r[4 * e + 2] = to_tf32(f.z);
-                    r[4 * e + 3] = to_tf32(f.w);
+                    r[4 * e] = to_tf32_int(f.x);
+                    r[4 * e + 1] = to_tf32_int(f.y);
+                    r[4 * e + 2] = to_tf32_int(f.z);
+                    r[4 * e + 3] = to_tf32_int(f.w);
                 }
                 tmem_st32(tmem + C::Q_COL + cc * 32, r);
             }
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
             float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int e = 0; e < 64; e++) {
-                const uint32_t p = to_tf32(exp2_approx(fmaf(__uint_as_float(sr[e]), c_log2, -m)));
+                const uint32_t p = to_tf32_int(exp2_approx(fmaf(__uint_as_float(sr[e]), c_log2, -m)));
                 ls[e & 3] += __uint_as_float(p);
                 sr[e] = p;
             }

@@ -68,10 +68,6 @@ constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 soft
 // is no longer the limit here (it was: cvt.rna.tf32 shared it with ex2).
 constexpr int POLY_PAIRS = 1;
 
-// A non-negative f32 rounded to tf32 (nearest, ties away from zero) with integer operations,
-// which keeps the conversion off the pipe the MUFU exponentials use.
-__device__ __forceinline__ uint32_t tf32_rna_pos(float v) { return (__float_as_uint(v) + 0x1000u) & 0xffffe000u; }
-
 // Two score buffers (S(j+1) is computed while the softmax works on S(j)), one CTA per SM
 // with 512 TMEM columns; the ring has three 64 KB slots at d = 128, six 32 KB slots at
 // d = 64. (Measured at d = 64, config 3's last chunk: one score buffer with two CTAs per SM
@@ -360,7 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         __ffma2_rn(make_float2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), c2, nm2);
                     const float2 pe = (((e >> 1) & 15) < POLY_PAIRS) ? exp2_poly2(x)
                                                                     : make_float2(exp2_approx(x.x), exp2_approx(x.y));
-                    const uint32_t p0 = tf32_rna_pos(pe.x), p1 = tf32_rna_pos(pe.y);
+                    const uint32_t p0 = to_tf32_int(pe.x), p1 = to_tf32_int(pe.y);
                     ls2[(e >> 1) & 1] = __fadd2_rn(ls2[(e >> 1) & 1], make_float2(__uint_as_float(p0), __uint_as_float(p1)));
                     sr[e] = p0;
                     sr[e + 1] = p1;

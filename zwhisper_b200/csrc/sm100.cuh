@@ -177,6 +177,11 @@ ZWG_DEV void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint
         : "memory");
 }
 
+// f32 -> tf32 (round to nearest, ties away from zero) by integer operations: the same result
+// as to_tf32 for finite values, computed off the conversion pipe (which the MUFU exponentials
+// of a softmax also use).
+ZWG_DEV uint32_t to_tf32_int(float x) { return (__float_as_uint(x) + 0x1000u) & 0xffffe000u; }
+
 // f32 -> tf32 (round to nearest, ties away from zero), kept in a 32-bit container.
 ZWG_DEV uint32_t to_tf32(float x) {
     uint32_t y;
