@@ -212,8 +212,18 @@ int zwg_init(int device) {
         cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
         if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
             (e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaStreamCreateWithFlags(&c->outs, cudaStreamNonBlocking)) != cudaSuccess ||
             (e = cudaMalloc(&c->err, sizeof(int))) != cudaSuccess ||
             (e = cudaMemset(c->err, 0, sizeof(int))) != cudaSuccess) {
+            delete c;
+            return cuda_fail("context set-up", e);
+        }
+        for (int i = 0; i < Ctx::kSlots && e == cudaSuccess; i++) {
+            if ((e = cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming)) == cudaSuccess &&
+                (e = cudaEventCreateWithFlags(&c->ev_comp[i], cudaEventDisableTiming)) == cudaSuccess)
+                e = cudaEventCreateWithFlags(&c->ev_free[i], cudaEventDisableTiming);
+        }
+        if (e != cudaSuccess) {
             delete c;
             return cuda_fail("context set-up", e);
         }
@@ -230,13 +240,18 @@ int zwg_shutdown(void) {
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     cudaStreamSynchronize(c->side);
-    for (int i = 0; i < 2; i++) {
+    cudaStreamSynchronize(c->outs);
+    for (int i = 0; i < Ctx::kSlots; i++) {
         c->q[i].release(); c->k[i].release(); c->v[i].release(); c->out[i].release(); c->ws[i].release();
         c->qh[i].release(); c->kh[i].release(); c->vh[i].release();
+        cudaEventDestroy(c->ev_in[i]);
+        cudaEventDestroy(c->ev_comp[i]);
+        cudaEventDestroy(c->ev_free[i]);
     }
     cudaFree(c->err);
     cudaStreamDestroy(c->stream);
     cudaStreamDestroy(c->side);
+    cudaStreamDestroy(c->outs);
     g_ctx[c->device] = nullptr;
     delete c;
     t_cur = nullptr;
@@ -287,7 +302,11 @@ static bool tc_eligible(const zwg_attn_shape* sh) {
            sh->out_stride == ns && sh->n_head <= 64 && sh->n_q <= (1u << 20);
 }
 
-// Host-pointer path: stage inputs, run, copy the written head columns back.
+// Host-pointer path: stage inputs, run, copy the written head columns back. The batch runs in
+// chunks through a ring of device staging slots as a three-stage pipeline: copies in on one
+// stream, the kernels on another, copies out on a third, so the host-to-device link (the
+// larger direction for attention: q, k and v in, one output back) stays busy while earlier
+// chunks compute and return. A slot is refilled only after its previous chunk's copy out.
 static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const float* q, const float* k,
                      const float* v, float* out) {
     const Extents ex = extents(sh);
@@ -295,42 +314,59 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
     if (nb == 0 || sh->n_q == 0) return ZWG_OK;
     const size_t qbs = b ? b->q_batch_stride : 0, kbs = b ? b->k_batch_stride : 0;
     const size_t vbs = b ? b->v_batch_stride : 0, obs = b ? b->out_batch_stride : 0;
-    // items per chunk: bounded device staging, two chunks in flight on two streams
+    // items per chunk: at most 256 MB of f32 staging per slot, and about six chunks when
+    // the batch allows, so the pipeline's fill and drain are short
     const size_t item_bytes = (ex.q + ex.k + ex.v + ex.out) * sizeof(float);
-    size_t per = std::max<size_t>(1, (size_t)(512u << 20) / std::max<size_t>(item_bytes, 1));
-    per = std::min(per, nb);
-    if (nb > 1 && per == nb) per = (nb + 1) / 2;
+    size_t per = std::max<size_t>(1, (size_t)(256u << 20) / std::max<size_t>(item_bytes, 1));
+    per = std::min(per, std::max<size_t>(1, (nb + 5) / 6));
     const zwg_attn_shape& s = *sh;
-    cudaStream_t streams[2] = {c->stream, c->side};
-    int slot = 0;
-    for (size_t i0 = 0; i0 < nb; i0 += per, slot ^= 1) {
+    const bool tc = (c->math & ZWG_MATH_BF16) && tc_eligible(sh);
+    const size_t dq = ex.q, dk = ex.k, dv = ex.v, dout = ex.out;
+    cudaError_t e = cudaSuccess;
+    int rc = ZWG_OK;
+    size_t chunk = 0;
+    for (size_t i0 = 0; i0 < nb && rc == ZWG_OK; i0 += per, chunk++) {
         const size_t n = std::min(per, nb - i0);
-        cudaStream_t st = streams[slot];
-        // dense per-item layout on the device
-        const size_t dq = ex.q, dk = ex.k, dv = ex.v, dout = ex.out;
+        const int slot = (int)(chunk % Ctx::kSlots);
         zwg_batch db{n, dq, dk, dv, dout};
         Plan pl = plan_for(sh, n, c->sm_count);
-        if (!c->q[slot].ensure(n * dq * 4 + 16) || !c->k[slot].ensure(n * dk * 4 + 16) ||
-            !c->v[slot].ensure(n * dv * 4 + 16) || !c->out[slot].ensure(n * dout * 4 + 16) ||
-            !c->ws[slot].ensure(pl.ws_bytes + 16))
-            return fail("device staging allocation failed");
-        cudaError_t e = cudaSuccess;
+        // the slot's previous chunk has left the device before its buffers are reused (the
+        // host waits here so that a buffer can grow safely)
+        if (chunk >= (size_t)Ctx::kSlots && (e = cudaEventSynchronize(c->ev_free[slot])) != cudaSuccess) {
+            rc = cuda_fail("staging slot wait", e);
+            break;
+        }
+        if (!c->q[slot].ensure(per * dq * 4 + 16) || !c->k[slot].ensure(per * dk * 4 + 16) ||
+            !c->v[slot].ensure(per * dv * 4 + 16) || !c->out[slot].ensure(per * dout * 4 + 16) ||
+            !c->ws[slot].ensure(pl.ws_bytes + 16) ||
+            (tc && (!c->qh[slot].ensure(per * dq * 2 + 16) || !c->kh[slot].ensure(per * dq * 2 + 16) ||
+                    !c->vh[slot].ensure(per * dq * 2 + 16)))) {
+            rc = fail("device staging allocation failed");
+            break;
+        }
+        // ---- copies in
         for (size_t j = 0; j < n && e == cudaSuccess; j++) {
             const size_t it = i0 + j;
-            if (dq) e = cudaMemcpyAsync((float*)c->q[slot].ptr + j * dq, q + it * qbs, dq * 4, cudaMemcpyHostToDevice, st);
-            if (e == cudaSuccess && dk) e = cudaMemcpyAsync((float*)c->k[slot].ptr + j * dk, k + it * kbs, dk * 4, cudaMemcpyHostToDevice, st);
-            if (e == cudaSuccess && dv) e = cudaMemcpyAsync((float*)c->v[slot].ptr + j * dv, v + it * vbs, dv * 4, cudaMemcpyHostToDevice, st);
+            if (dq) e = cudaMemcpyAsync((float*)c->q[slot].ptr + j * dq, q + it * qbs, dq * 4, cudaMemcpyHostToDevice, c->side);
+            if (e == cudaSuccess && dk) e = cudaMemcpyAsync((float*)c->k[slot].ptr + j * dk, k + it * kbs, dk * 4, cudaMemcpyHostToDevice, c->side);
+            if (e == cudaSuccess && dv) e = cudaMemcpyAsync((float*)c->v[slot].ptr + j * dv, v + it * vbs, dv * 4, cudaMemcpyHostToDevice, c->side);
         }
-        if (e != cudaSuccess) return cuda_fail("host to device copy", e);
-        int rc;
-        if ((c->math & ZWG_MATH_BF16) && tc_eligible(sh)) {
+        if (e == cudaSuccess) e = cudaEventRecord(c->ev_in[slot], c->side);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->stream, c->ev_in[slot], 0);
+        if (e != cudaSuccess) {
+            rc = cuda_fail("host to device copy", e);
+            break;
+        }
+        // ---- the kernels
+        cudaStream_t st = c->stream;
+        if (tc) {
             const size_t ne = n * dq;  // q, k, v have the same extent here
-            if (!c->qh[slot].ensure(ne * 2 + 16) || !c->kh[slot].ensure(ne * 2 + 16) || !c->vh[slot].ensure(ne * 2 + 16))
-                return fail("device staging allocation failed");
             if (zwg::f32_to_bf16_launch((float*)c->q[slot].ptr, (uint16_t*)c->qh[slot].ptr, ne, st) ||
                 zwg::f32_to_bf16_launch((float*)c->k[slot].ptr, (uint16_t*)c->kh[slot].ptr, ne, st) ||
-                zwg::f32_to_bf16_launch((float*)c->v[slot].ptr, (uint16_t*)c->vh[slot].ptr, ne, st))
-                return cuda_fail("bf16 conversion", cudaGetLastError());
+                zwg::f32_to_bf16_launch((float*)c->v[slot].ptr, (uint16_t*)c->vh[slot].ptr, ne, st)) {
+                rc = cuda_fail("bf16 conversion", cudaGetLastError());
+                break;
+            }
             zwg::EncTcParams tp{(uint16_t*)c->qh[slot].ptr, (uint16_t*)c->kh[slot].ptr, (uint16_t*)c->vh[slot].ptr,
                                 (float*)c->out[slot].ptr, (int)n, (int)s.n_q, (int)s.n_head, c->err};
             rc = zwg::enc_tc_launch(tp, st) ? cuda_fail("enc_attn launch", cudaGetLastError()) : ZWG_OK;
@@ -338,16 +374,22 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
             rc = run_dev(c, &s, &db, (float*)c->q[slot].ptr, (float*)c->k[slot].ptr, (float*)c->v[slot].ptr,
                          (float*)c->out[slot].ptr, c->ws[slot].ptr, c->ws[slot].cap, st);
         }
-        if (rc) return rc;
-        // only the head columns of each output row are written, as in the reference
+        if (rc) break;
+        if ((e = cudaEventRecord(c->ev_comp[slot], st)) == cudaSuccess)
+            e = cudaStreamWaitEvent(c->outs, c->ev_comp[slot], 0);
+        // ---- copies out: only the head columns of each output row are written, as in the
+        // reference
         for (size_t j = 0; j < n && e == cudaSuccess; j++)
             e = cudaMemcpy2DAsync(out + (i0 + j) * obs, s.out_stride * 4, (float*)c->out[slot].ptr + j * dout,
-                                  s.out_stride * 4, s.n_head * s.d * 4, s.n_q, cudaMemcpyDeviceToHost, st);
-        if (e != cudaSuccess) return cuda_fail("device to host copy", e);
+                                  s.out_stride * 4, s.n_head * s.d * 4, s.n_q, cudaMemcpyDeviceToHost, c->outs);
+        if (e == cudaSuccess) e = cudaEventRecord(c->ev_free[slot], c->outs);
+        if (e != cudaSuccess) rc = cuda_fail("device to host copy", e);
     }
-    int rc = sync_and_check(c, c->side);
-    int rc2 = sync_and_check(c, c->stream);
-    return rc ? rc : rc2;
+    // every stage drains before the call returns, also after an error
+    const int r1 = sync_and_check(c, c->side);
+    const int r2 = sync_and_check(c, c->stream);
+    const int r3 = sync_and_check(c, c->outs);
+    return rc ? rc : r1 ? r1 : r2 ? r2 : r3;
 }
 
 int zwg_attention(const zwg_attn_shape* sh, const float* q, const float* k, const float* v, float* out) {

@@ -38,15 +38,20 @@ struct Ctx {
     int device = -1;
     int sm_count = 148;
     cudaStream_t stream = nullptr;
-    cudaStream_t side = nullptr;  // second stream for pipelined host batches
+    // host-pointer calls run as a three-stage pipeline over a ring of staging slots: copies
+    // in on `side`, the kernels on `stream`, copies out on `outs`, joined by events
+    cudaStream_t side = nullptr;
+    cudaStream_t outs = nullptr;
+    static constexpr int kSlots = 3;
+    cudaEvent_t ev_in[kSlots] = {}, ev_comp[kSlots] = {}, ev_free[kSlots] = {};
     int* err = nullptr;           // device error word
     // Counts the device errors sync_and_check has reported. A kernel that gave up may have
     // left a segment ticket behind, so kept-zero ticket buffers are cleared again when this
     // moved since their last clearing.
     std::atomic<unsigned> err_gen{0};
     int math = ZWG_MATH_F32;
-    DevBuf q[2], k[2], v[2], out[2], ws[2];
-    DevBuf qh[2], kh[2], vh[2];   // bf16 copies for the tensor-core path
+    DevBuf q[kSlots], k[kSlots], v[kSlots], out[kSlots], ws[kSlots];
+    DevBuf qh[kSlots], kh[kSlots], vh[kSlots];   // bf16 copies for the tensor-core path
 };
 
 // Segment tickets of the split decode kernels, kept by a state for its own calls (which run
