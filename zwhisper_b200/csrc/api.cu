@@ -314,11 +314,11 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
     if (nb == 0 || sh->n_q == 0) return ZWG_OK;
     const size_t qbs = b ? b->q_batch_stride : 0, kbs = b ? b->k_batch_stride : 0;
     const size_t vbs = b ? b->v_batch_stride : 0, obs = b ? b->out_batch_stride : 0;
-    // items per chunk: at most 256 MB of f32 staging per slot, and about six chunks when
+    // items per chunk: at most 256 MB of f32 staging per slot, and about twelve chunks when
     // the batch allows, so the pipeline's fill and drain are short
     const size_t item_bytes = (ex.q + ex.k + ex.v + ex.out) * sizeof(float);
     size_t per = std::max<size_t>(1, (size_t)(256u << 20) / std::max<size_t>(item_bytes, 1));
-    per = std::min(per, std::max<size_t>(1, (nb + 5) / 6));
+    per = std::min(per, std::max<size_t>(1, (nb + 11) / 12));
     const zwg_attn_shape& s = *sh;
     const bool tc = (c->math & ZWG_MATH_BF16) && tc_eligible(sh);
     const size_t dq = ex.q, dk = ex.k, dv = ex.v, dout = ex.out;
