@@ -17,8 +17,11 @@
 // f32 sums round, in another order than the reference's (the same bound as the CUDA-core
 // kernels: a few f32 ulps of the sum of |terms|).
 //
-// Tile: 128 weight rows (TMEM lanes) x 128 activation rows; a CTA walks its k range in steps
-// of 64 (two Q8 blocks).
+// Tile: 128 weight rows (TMEM lanes) x 128 activation rows (more than 64 rows of x) or x 64
+// activation rows with the three pieces stacked along N instead of K (16-64 rows: one N192
+// MMA per K16 slice into a 192-column accumulator whose three 64-column parts the scalers
+// sum; a third of the MMAs of the 128-row form, most of whose rows would be past m). A CTA
+// walks its k range in steps of 64 (two Q8 blocks). The 128-row form:
 //   warp 0      TMA producer: int8 weights [128 rows][64] (two [64][64] boxes for the SiLU
 //               pair: gate rows, then up rows) and f32 activations [128 rows][64] into a
 //               2-stage raw ring; rows past n or m are zero-filled.
@@ -57,12 +60,8 @@ namespace q8tc {
 using namespace sm100;
 
 constexpr int BM = 128;          // weight rows per tile (TMEM lanes)
-constexpr int TN = 128;          // activation rows per tile
 constexpr int BK = 64;           // k per step: two Q8 blocks
 constexpr int NP = 3;            // bf16 pieces of an activation
-constexpr int NSR = 2;           // raw stages
-constexpr int NSC = 2;           // converted stages
-constexpr int NSLOT = 4;         // block accumulators in TMEM
 constexpr int MAX_KS = 8;        // CTAs per cluster (k splits)
 constexpr int CONV_WARPS = 8;
 constexpr int SCALE_WARPS = 8;
@@ -70,27 +69,49 @@ constexpr int THREADS = 32 * (2 + CONV_WARPS + SCALE_WARPS);
 constexpr int CONV_THREADS = 32 * CONV_WARPS;
 constexpr int SCALE_THREADS = 32 * SCALE_WARPS;
 constexpr int SCALE_WARP0 = 2 + CONV_WARPS;
-constexpr int COLS = TN / 2;                      // activation rows per scaler thread
 constexpr uint32_t RAW_W = BM * BK;               // int8
-constexpr uint32_t RAW_X = TN * BK * 4;           // f32
 constexpr uint32_t CV_A = BM * BK * 2;            // bf16, 128-byte rows
-constexpr uint32_t CV_P = TN * BK * 2;            // one piece: bf16, 128-byte rows
-constexpr uint32_t TMEM_COLS = NSLOT * TN;
+constexpr uint32_t TMEM_COLS = 512;
 constexpr int PART_LD = BM + 4;                   // row stride of the split-K partial tile (floats)
 constexpr int PAIR_LD = BM / 2 + 4;               // row stride of the SiLU pair's exchange (floats)
 
+// The two tile forms. Large (more than 64 rows of x): 128 activation rows, the pieces along
+// K, one 128-column accumulator per Q8 block (six N128 MMAs per block). Small (16-64 rows):
+// 64 activation rows, the pieces stacked along N (rows p * 64 + r of the B operand), one
+// 192-column accumulator per block holding the three pieces' dots side by side, summed by
+// the scalers (two N192 MMAs per block: a third of the large form's MMAs, where those
+// would mostly multiply rows past m).
+template <bool SMALL>
+struct Tr {
+    static constexpr int TN = SMALL ? 64 : 128;            // activation rows per tile
+    static constexpr int NSR = SMALL ? 3 : 2;              // raw stages
+    static constexpr int NSC = SMALL ? 3 : 2;              // converted stages
+    static constexpr int NSLOT = SMALL ? 2 : 4;            // block accumulators in TMEM
+    static constexpr uint32_t ACC = SMALL ? NP * 64 : 128; // TMEM columns of one
+    static constexpr int COLS = TN / 2;                    // activation rows per scaler thread
+    static constexpr uint32_t RAW_X = TN * BK * 4;         // f32
+    static constexpr uint32_t CV_P = TN * BK * 2;          // one piece: bf16, 128-byte rows
+    static_assert(NSLOT * ACC <= TMEM_COLS, "TMEM columns");
+};
+
+template <bool SMALL>
 struct Smem {
-    uint8_t cv_a[NSC][CV_A];
-    uint8_t cv_b[NSC][NP * CV_P];
-    uint8_t raw_x[NSR][RAW_X];
-    uint8_t raw_w[NSR][RAW_W];
-    uint64_t raw_full[NSR], raw_empty[NSR], cv_full[NSC], cv_empty[NSC], acc_full[NSLOT], acc_empty[NSLOT];
+    using T = Tr<SMALL>;
+    uint8_t cv_a[T::NSC][CV_A];
+    uint8_t cv_b[T::NSC][NP * T::CV_P];
+    uint8_t raw_x[T::NSR][T::RAW_X];
+    uint8_t raw_w[T::NSR][RAW_W];
+    uint64_t raw_full[T::NSR], raw_empty[T::NSR], cv_full[T::NSC], cv_empty[T::NSC];
+    uint64_t acc_full[T::NSLOT], acc_empty[T::NSLOT];
     uint32_t tmem_base;
 };
-constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory of one CTA");
-static_assert(TN * PART_LD * 4 <= NSC * NP * CV_P, "the split-K partial tile fits in the operand ring");
-static_assert(THREADS * 112 <= 65536, "registers");
+template <bool SMALL>
+constexpr size_t smem_bytes() { return sizeof(Smem<SMALL>) + 1024; }
+static_assert(smem_bytes<false>() <= 227 * 1024 && smem_bytes<true>() <= 227 * 1024, "shared memory of one CTA");
+static_assert(Tr<false>::TN * PART_LD * 4 <= Tr<false>::NSC * NP * Tr<false>::CV_P &&
+                  Tr<true>::TN * PART_LD * 4 <= Tr<true>::NSC * NP * Tr<true>::CV_P,
+              "the split-K partial tile fits in the operand ring");
+static_assert(THREADS * 96 <= 65536, "registers");
 
 struct Args {
     int m, n, k, ks;             // ks: CTAs per cluster
@@ -199,12 +220,17 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, 
 }
 
 // PAIR: the SiLU pair (tile rows 0-63 the gate's rows j0.., 64-127 the up matrix's same rows)
-template <bool PAIR>
+// SMALL: the 64-row tile form (Tr)
+template <bool PAIR, bool SMALL>
 __global__ void __launch_bounds__(THREADS, 1)
     q8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wu,
                  const __grid_constant__ CUtensorMap tm_x, Args a) {
+    using T = Tr<SMALL>;
+    constexpr int TN = T::TN, NSR = T::NSR, NSC = T::NSC, NSLOT = T::NSLOT, COLS = T::COLS;
+    constexpr uint32_t RAW_X = T::RAW_X, CV_P = T::CV_P, ACC = T::ACC;
     extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem<SMALL>& sm =
+        *reinterpret_cast<Smem<SMALL>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int rows_w = PAIR ? BM / 2 : BM;               // weight rows of one matrix per tile
@@ -282,7 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16(BM, TN, true, false, false);
+            constexpr uint32_t idesc = idesc_f16(BM, SMALL ? NP * TN : TN, true, false, false);
             int blk = 0;
             for (int i = 0; ok && i < steps; i++) {
                 const int cs = i % NSC;
@@ -297,10 +323,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 2; kk++) {
                         const uint32_t ko = (uint32_t)(hb * 2 + kk) * 32;  // 16 bf16 = 32 bytes of k
+                        if constexpr (SMALL) {
+                            // the three pieces as one B operand of 192 rows: their dots side by side
+                            mma_f16_ss(tmem + slot * ACC, smem_desc_sw128(a_addr + ko, 16, 1024),
+                                       smem_desc_sw128(b_addr + ko, 16, 1024), idesc, kk ? 1u : 0u);
+                        } else {
 #pragma unroll
-                        for (int p = 0; p < NP; p++)
-                            mma_f16_ss(tmem + slot * TN, smem_desc_sw128(a_addr + ko, 16, 1024),
-                                       smem_desc_sw128(b_addr + p * CV_P + ko, 16, 1024), idesc, (kk | p) ? 1u : 0u);
+                            for (int p = 0; p < NP; p++)
+                                mma_f16_ss(tmem + slot * ACC, smem_desc_sw128(a_addr + ko, 16, 1024),
+                                           smem_desc_sw128(b_addr + p * CV_P + ko, 16, 1024), idesc,
+                                           (kk | p) ? 1u : 0u);
+                        }
                     }
                     mma_commit(&sm.acc_full[slot]);
                 }
@@ -336,7 +369,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // activations: row r, 8 f32 (chunk c8) -> one 16-byte chunk of each piece; rows
             // past m stay zero once written
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < TN / 32; u++) {
                 const int r = (ct >> 3) + 32 * u, c8 = ct & 7;
                 if (i >= NSC && r0 + r >= a.m) continue;
                 const uint4 x0 = ld_shared_v4(rx + r * (BK * 4) + c8 * 32);
@@ -381,14 +414,31 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
 #pragma unroll
             for (int h = 0; h < COLS / 16; h++) {
-                uint32_t v[16];
-                tmem_ld16(lane_base + slot * TN + h * 16, v);
-                tmem_ld_wait();
                 const float2 s2 = make_float2(s, s);
+                if constexpr (SMALL) {
+                    // the block dot of each row is (hi + mid) + lo over its three columns
+                    uint32_t vh[16], vm[16], vl[16];
+                    tmem_ld16(lane_base + slot * ACC + h * 16, vh);
+                    tmem_ld16(lane_base + slot * ACC + TN + h * 16, vm);
+                    tmem_ld16(lane_base + slot * ACC + 2 * TN + h * 16, vl);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int c = 0; c < 8; c++)
-                    acc2[h * 8 + c] = __ffma2_rn(s2, make_float2(__uint_as_float(v[2 * c]), __uint_as_float(v[2 * c + 1])),
-                                                 acc2[h * 8 + c]);
+                    for (int c = 0; c < 8; c++) {
+                        const float2 d = __fadd2_rn(
+                            __fadd2_rn(make_float2(__uint_as_float(vh[2 * c]), __uint_as_float(vh[2 * c + 1])),
+                                       make_float2(__uint_as_float(vm[2 * c]), __uint_as_float(vm[2 * c + 1]))),
+                            make_float2(__uint_as_float(vl[2 * c]), __uint_as_float(vl[2 * c + 1])));
+                        acc2[h * 8 + c] = __ffma2_rn(s2, d, acc2[h * 8 + c]);
+                    }
+                } else {
+                    uint32_t v[16];
+                    tmem_ld16(lane_base + slot * ACC + h * 16, v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int c = 0; c < 8; c++)
+                        acc2[h * 8 + c] = __ffma2_rn(
+                            s2, make_float2(__uint_as_float(v[2 * c]), __uint_as_float(v[2 * c + 1])), acc2[h * 8 + c]);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -501,21 +551,26 @@ int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const flo
     if (((uintptr_t)x & 15) || ((uintptr_t)wq & 15) || (pair && ((uintptr_t)wu & 15))) return 1;
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return 1;
     if (pair && mode != LIN_STORE) return 1;
+    // up to 64 rows the small tile form (pieces along N), else the large one
+    const bool small = m <= 64;
+    const int tn = small ? Tr<true>::TN : Tr<false>::TN;
     const int rows_w = pair ? BM / 2 : BM;
-    const size_t tiles_n = (n + rows_w - 1) / rows_w, tiles_m = (m + TN - 1) / TN;
+    const size_t tiles_n = (n + rows_w - 1) / rows_w, tiles_m = (m + tn - 1) / tn;
     if (tiles_n > 0x7fffffff || tiles_m > 65535) return 1;
-    // k splits (powers of two, at most 8, at least two k steps each) while the tiles alone
-    // would give fewer CTAs than SMs; the pair keeps whole k ranges
+    // k splits (powers of two, at most 8, at least two k steps each) while the doubled grid
+    // still fits in one wave (one CTA per SM): a second, mostly empty wave costs more than the
+    // longer k ranges; the pair keeps whole k ranges
     const size_t steps = k / BK;
     int ks = 1;
-    while (!pair && ks < MAX_KS && tiles_n * tiles_m * ks < (size_t)std::max(1, sm_count) && steps / (2 * ks) >= 2)
+    while (!pair && ks < MAX_KS && tiles_n * tiles_m * (size_t)(2 * ks) <= (size_t)std::max(1, sm_count) &&
+           steps / (2 * ks) >= 2)
         ks *= 2;
 
     CUtensorMap mw, mwu, mx;
     if (!map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, k, n, k, BK, rows_w)) return -1;
     if (pair && !map_2d(&mwu, CU_TENSOR_MAP_DATA_TYPE_UINT8, wu, k, n, k, BK, rows_w)) return -1;
     if (!pair) mwu = mw;
-    if (!map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, k, m, k * 4, BK, TN)) return -1;
+    if (!map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, k, m, k * 4, BK, (uint32_t)tn)) return -1;
 
     Args a{};
     a.m = (int)m;
@@ -531,22 +586,25 @@ int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const flo
     a.err = capi::current_err_word();
 
     static std::mutex mu;
-    static bool attr_set[64][2] = {};
+    static bool attr_set[64][4] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
-    auto kern = pair ? q8_tc_kernel<true> : q8_tc_kernel<false>;
+    const int variant = (pair ? 1 : 0) + (small ? 2 : 0);
+    auto kern = pair ? (small ? q8_tc_kernel<true, true> : q8_tc_kernel<true, false>)
+                     : (small ? q8_tc_kernel<false, true> : q8_tc_kernel<false, false>);
+    const size_t smem = small ? smem_bytes<true>() : smem_bytes<false>();
     {
         std::lock_guard<std::mutex> lk(mu);
-        if (!attr_set[dev][pair ? 1 : 0]) {
-            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
+        if (!attr_set[dev][variant]) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
                 return -1;
-            attr_set[dev][pair ? 1 : 0] = true;
+            attr_set[dev][variant] = true;
         }
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)tiles_n, (unsigned)tiles_m, (unsigned)ks);
     cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
