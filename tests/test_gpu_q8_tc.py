@@ -6,7 +6,9 @@ Each 32-wide block dot is formed on the tensor cores from exact operands (int8 w
 bf16, each f32 activation split into three bf16 pieces that sum to it exactly), so the only
 roundings are f32 sums: the products are held to the same bound as the other Q8 kernels,
 2e-6 of the sum of |terms| of each output (about 16 f32 ulps). Covered: every epilogue
-(store + bias, add into out, tanh GELU, the SiLU pair), partial row and column tiles, k
+(store + bias, add into out, tanh GELU, the SiLU pair, the Qwen2 q/k/v + RoPE pair here; the
+Whisper decoder's q/k/v product in tests/test_gpu_dec_step.py at 16 windows), the 64-row
+and 128-row tile forms, partial row and column tiles, k
 split over clusters of CTAs (deterministic), activations over a wide dynamic range, and the
 process-wide switch between the two kernels (which give different roundings, so the
 tensor-core kernel is seen to run)."""
@@ -147,3 +149,19 @@ def test_switch_round_trips(env):
     assert ops.q8_tensor_cores(False) is True
     assert ops.q8_tensor_cores() is False
     assert ops.q8_tensor_cores(True) is False
+
+
+@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "cuda_cores"])
+def test_rope_pair_both_kernels(env, tc):
+    """The Qwen2 q/k/v pair (bias, RoPE, q out, K^T scatter, V copy) at 16+ rows on either
+    kernel against the oracle: heads of d 64 (two per 128-row tile) and d 128 (one), single
+    tokens of 16 sequences (k split over a cluster) and 60- and 64-token chunks."""
+    torch, ops = env
+    from tests.test_gpu_llm_step import run_qkv
+    ops.q8_tensor_cores(tc)
+    try:
+        run_qkv(torch, ops, B=16, H=4, Hkv=2, d=64, n_ctx=32, chunks=[1, 1], seed=4)
+        run_qkv(torch, ops, B=8, H=14, Hkv=2, d=64, n_ctx=128, chunks=[60, 1], seed=5)
+        run_qkv(torch, ops, B=4, H=14, Hkv=2, d=128, n_ctx=128, chunks=[64, 1], seed=6, bias=False)
+    finally:
+        ops.q8_tensor_cores(True)

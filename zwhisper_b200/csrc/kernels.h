@@ -155,6 +155,11 @@ int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const flo
                  int mode, const int8_t* wu, const float* su, const float* bu, float* out, int sm_count,
                  cudaStream_t st);
 struct PairParams;
+// The RoPE pair and the Whisper decoder's q/k/v product on the tcgen05 kernel (q8_tc.cu),
+// for 16+ rows with k a multiple of 64 and every matrix's rows a multiple of 128; same
+// return convention as q8_tc_launch.
+int q8_tc_rope_launch(const PairParams& p, int sm_count, cudaStream_t st);
+int q8_tc_qkv_launch(const PairParams& p, int sm_count, cudaStream_t st);
 // The RoPE pair of q8_pair_launch on the same tiles.
 int q8_gemm_rope_launch(const PairParams& p, int sm_count, cudaStream_t st);
 // The Whisper decoder's q/k/v projections as one tiled product (16+ rows of x): q to

@@ -673,12 +673,20 @@ int q8_gemm_silu_launch(const float* x, size_t m, size_t k, const int8_t* wg, co
 // The Whisper decoder's q/k/v projections in one product (PE_QKV): p.x [m][p.k], p.wq/ws/bias
 // [3], p.d = n_state, q to p.q_out, k / v rows appended to p.cache_kt / p.cache_v.
 int q8_gemm_qkv_launch(const PairParams& p, int sm_count, cudaStream_t st) {
+    if (p.m > 0 && p.d > 0) {
+        const int r = q8_tc_qkv_launch(p, sm_count, st);
+        if (r != 1) return r;
+    }
     return launch(p.x, (size_t)p.m, (size_t)p.k, p.wq[0], p.ws[0], nullptr, (size_t)3 * p.d, LIN_STORE, q8g::PE_QKV,
                   p, nullptr, sm_count, st);
 }
 
 // The RoPE pair of q8_pair_launch (q/k/v + bias + RoPE + K^T / V append) on the tiles.
 int q8_gemm_rope_launch(const PairParams& p, int sm_count, cudaStream_t st) {
+    if (p.m > 0 && p.n_pairs > 0) {
+        const int r = q8_tc_rope_launch(p, sm_count, st);
+        if (r != 1) return r;
+    }
     return launch(p.x, (size_t)p.m, (size_t)p.k, p.wq[0], p.ws[0], nullptr, (size_t)p.n_pairs, LIN_STORE, q8g::PE_ROPE,
                   p, nullptr, sm_count, st);
 }

@@ -2,8 +2,10 @@
 // (sm_100a): ops.linear with Q8 weights (src/ops.zig:280-306 -> gemm.ntBlockQ,
 // src/gemm.zig:268-351) for a decoder step over many windows, an LLM step over many
 // sequences, prompt chunks and setAudio's 1500 rows, with the epilogues of
-// q8_linear_kernel (store + bias, add into out, tanh GELU) and the SiLU pair (gate and up,
-// src/llm.zig:206-208).
+// q8_linear_kernel (store + bias, add into out, tanh GELU), the SiLU pair (gate and up,
+// src/llm.zig:206-208), the Qwen2 q/k/v pair (bias, RoPE, q out, K^T scatter and V copy,
+// src/llm.zig:179-190, 221-238) and the Whisper decoder's q/k/v product (bias, q out, k and
+// v appended to the caches, src/decoder.zig:389-395).
 //
 //   out[r][j] = epilogue( sum over blocks b of  s[j][b] * sum_{i < 32} x[r][32b + i] * q[j][32b + i] )
 //
@@ -113,6 +115,12 @@ static_assert(Tr<false>::TN * PART_LD * 4 <= Tr<false>::NSC * NP * Tr<false>::CV
               "the split-K partial tile fits in the operand ring");
 static_assert(THREADS * 96 <= 65536, "registers");
 
+// Epilogue modes: a plain product, the SiLU pair, and two forms over the three q/k/v
+// matrices (a CTA's 128-row tile lies in one of them: tiles of matrix 0, then 1, then 2):
+// the Qwen2 RoPE pair (bias, rotation of rows i and i + d/2 of a head, q out, K^T scatter,
+// V copy) and the Whisper decoder's q/k/v (bias, q out, k and v appended to the caches).
+enum { EPI_PLAIN = 0, EPI_SILU = 1, EPI_ROPE = 2, EPI_QKV = 3 };
+
 struct Args {
     int m, n, k, ks;             // ks: CTAs per cluster
     int mode;                    // LIN_STORE / LIN_ADD / LIN_GELU
@@ -122,6 +130,8 @@ struct Args {
     const float* bias_u;
     float* out;
     int* err;
+    int tiles[3];                // ROPE / QKV: 128-row tiles of each matrix
+    PairParams pp;               // ROPE / QKV: the matrices' scales and biases, caches, tables
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
@@ -193,6 +203,61 @@ __device__ __forceinline__ void finish_pair(const Args& a, int row, int col, flo
     a.out[(size_t)row * a.n + col] = silu_mul(g, u);
 }
 
+// Element sel (0-2) of a kernel-parameter array by selects: a runtime index into the
+// parameter space would copy the whole argument struct to local memory.
+template <typename P>
+__device__ __forceinline__ P pick3(P const (&v)[3], int sel) {
+    return sel == 0 ? v[0] : sel == 1 ? v[1] : v[2];
+}
+
+// ROPE: x row r of the call, matrix sel, rows ra and ra + d/2 of a head (va, vb before bias)
+__device__ __forceinline__ void finish_rope(const PairParams& p, int r, int sel, int ra, float va, float vb) {
+    const int half = p.d >> 1, i = ra % p.d;
+    const float* bias = pick3(p.bias, sel);
+    if (bias) {
+        va = __fadd_rn(va, __ldg(bias + ra));
+        vb = __fadd_rn(vb, __ldg(bias + ra + half));
+    }
+    const int tok = p.m0 + r;
+    const int seq = tok / p.n_tok, t = tok - seq * p.n_tok;
+    const size_t pos = (size_t)p.n_past + t;
+    // separately rounded products and sums, as the reference's rope (src/llm.zig:221-238)
+    const float c = p.cos_tab[pos * half + i], s = p.sin_tab[pos * half + i];
+    const float lo = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+    const float hi = __fadd_rn(__fmul_rn(va, s), __fmul_rn(vb, c));
+    if (sel == 0) {
+        float* qo = p.q_out + (size_t)tok * p.n_head * p.d + ra;
+        qo[0] = lo;
+        qo[half] = hi;
+    } else {
+        float* kt = p.cache_kt + (size_t)seq * p.cache_bs;
+        kt[(size_t)ra * p.n_ctx + pos] = lo;
+        kt[(size_t)(ra + half) * p.n_ctx + pos] = hi;
+    }
+}
+
+// ROPE's v rows: bias, then the V cache at the token's position
+__device__ __forceinline__ void finish_rope_v(const PairParams& p, int r, int ra, float v) {
+    if (p.bias[2]) v = __fadd_rn(v, __ldg(p.bias[2] + ra));
+    const int tok = p.m0 + r;
+    const int seq = tok / p.n_tok, t = tok - seq * p.n_tok;
+    const size_t pos = (size_t)p.n_past + t;
+    p.cache_v[(size_t)seq * p.cache_bs + pos * ((size_t)p.n_head_kv * p.d) + ra] = v;
+}
+
+// QKV: x row r of the call (window r / n_tok, token r % n_tok), matrix sel, column col
+__device__ __forceinline__ void finish_qkv(const PairParams& p, int r, int sel, int col, float v) {
+    const float* bias = pick3(p.bias, sel);
+    if (bias) v = __fadd_rn(v, __ldg(bias + col));
+    if (sel == 0) {
+        p.q_out[(size_t)r * p.d + col] = v;
+        return;
+    }
+    const int seq = r / p.n_tok, t = r - seq * p.n_tok;
+    float* cache = sel == 1 ? p.cache_kt : p.cache_v;
+    cache[(size_t)seq * p.cache_bs + ((size_t)p.n_past + t) * p.d + col] = v;
+}
+
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
@@ -219,12 +284,15 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, 
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(map), "r"(c0), "r"(c1) : "memory");
 }
 
-// PAIR: the SiLU pair (tile rows 0-63 the gate's rows j0.., 64-127 the up matrix's same rows)
-// SMALL: the 64-row tile form (Tr)
-template <bool PAIR, bool SMALL>
+// EPI: the epilogue mode. The SiLU pair's tile rows 0-63 are the gate's rows j0.., 64-127
+// the up matrix's same rows (tm_w, tm_wu); ROPE and QKV read matrix sel's rows j0.. through
+// tm_w, tm_wu or tm_w3. SMALL: the 64-row tile form (Tr).
+template <int EPI, bool SMALL>
 __global__ void __launch_bounds__(THREADS, 1)
     q8_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wu,
-                 const __grid_constant__ CUtensorMap tm_x, Args a) {
+                 const __grid_constant__ CUtensorMap tm_w3, const __grid_constant__ CUtensorMap tm_x, Args a) {
+    constexpr bool PAIR = EPI == EPI_SILU;
+    constexpr bool SEC = EPI == EPI_ROPE || EPI == EPI_QKV;  // three matrices, one per tile
     using T = Tr<SMALL>;
     constexpr int TN = T::TN, NSR = T::NSR, NSC = T::NSC, NSLOT = T::NSLOT, COLS = T::COLS;
     constexpr uint32_t RAW_X = T::RAW_X, CV_P = T::CV_P, ACC = T::ACC;
@@ -234,7 +302,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int rows_w = PAIR ? BM / 2 : BM;               // weight rows of one matrix per tile
-    const int j0 = blockIdx.x * rows_w;
+    int sel = 0, j0 = blockIdx.x * rows_w;
+    if (SEC) {
+        const int bx = blockIdx.x;
+        sel = bx < a.tiles[0] ? 0 : bx < a.tiles[0] + a.tiles[1] ? 1 : 2;
+        j0 = (bx - (sel > 0 ? a.tiles[0] : 0) - (sel > 1 ? a.tiles[1] : 0)) * BM;
+    }
+    const CUtensorMap* tmw = (!SEC || sel == 0) ? &tm_w : sel == 1 ? &tm_wu : &tm_w3;
     const int r0 = blockIdx.y * TN;
     const int rank = blockIdx.z;                          // = the CTA's rank in its cluster
     const int steps_all = a.k / BK;
@@ -261,11 +335,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     // the weights are constants: warm L2 with this CTA's first steps before waiting for the
     // kernel that wrote x
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&tm_w);
+        prefetch_tmap(tmw);
         prefetch_tmap(&tm_x);
         if (PAIR) prefetch_tmap(&tm_wu);
         for (int i = 0; i < steps && i < 4; i++) {
-            tma_prefetch_2d(&tm_w, (s_begin + i) * BK, j0);
+            tma_prefetch_2d(tmw, (s_begin + i) * BK, j0);
             if (PAIR) tma_prefetch_2d(&tm_wu, (s_begin + i) * BK, j0);
         }
     }
@@ -296,7 +370,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (i >= NSR && !(ok = mbar_wait(&sm.raw_empty[rs], ((i / NSR) - 1) & 1, a.err))) break;
                 const int kc = (s_begin + i) * BK;
                 mbar_arrive_expect_tx(&sm.raw_full[rs], RAW_W + RAW_X);
-                tma_load_2d(&tm_w, &sm.raw_full[rs], sm.raw_w[rs], kc, j0);
+                tma_load_2d(tmw, &sm.raw_full[rs], sm.raw_w[rs], kc, j0);
                 if (PAIR) tma_load_2d(&tm_wu, &sm.raw_full[rs], sm.raw_w[rs] + RAW_W / 2, kc, j0);
                 tma_load_2d(&tm_x, &sm.raw_full[rs], sm.raw_x[rs], kc, r0);
                 issued = i + 1;
@@ -399,11 +473,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int jl = scaler ? (warp & 3) * 32 + lane : 0;   // tile row = TMEM lane
     const int cg = scaler ? (warp - SCALE_WARP0) >> 2 : 0; // which half of the activation rows
     const bool up = PAIR && jl >= BM / 2;
-    const int jrow = j0 + (PAIR ? (jl & (BM / 2 - 1)) : jl);
-    const bool row_ok = jrow < a.n;
+    const int jrow = j0 + (PAIR ? (jl & (BM / 2 - 1)) : jl);  // row of its matrix
+    // ROPE / QKV: every matrix has whole 128-row tiles (the launcher checks it)
+    const bool row_ok = SEC || jrow < a.n;
     if (scaler) {
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16) + cg * COLS;
-        const float* srow = (up ? a.wsu : a.ws) + (size_t)(row_ok ? jrow : 0) * nbk;
+        const float* sbase = SEC ? pick3(a.pp.ws, sel) : up ? a.wsu : a.ws;
+        const float* srow = sbase + (size_t)(row_ok ? jrow : 0) * nbk;
         const int b0 = s_begin * 2;
         float s_next = row_ok ? __ldg(srow + b0) : 0.f;
         for (int blk = 0; blk < 2 * steps; blk++) {
@@ -457,13 +533,39 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     float* part = reinterpret_cast<float*>(sm.cv_b[0]);
     const int cbase = cg * COLS;                           // first activation row of this thread
+    // ROPE: a head's rows i < d/2 finish the pair (i, i + d/2); the v matrix has no pairs
+    const int half = a.pp.d >> 1;
+    const bool rope_pairs = EPI == EPI_ROPE && sel != 2;
+    const bool second = rope_pairs && (jrow % a.pp.d) >= half;
     if (a.ks == 1) {
         if (scaler) {
-            if (!PAIR) {
+            if (EPI == EPI_PLAIN) {
                 if (row_ok) {
 #pragma unroll
                     for (int c = 0; c < COLS; c++)
                         if (r0 + cbase + c < a.m) finish(a, r0 + cbase + c, jrow, acc[c]);
+                }
+            } else if (EPI == EPI_QKV) {
+#pragma unroll
+                for (int c = 0; c < COLS; c++)
+                    if (r0 + cbase + c < a.m) finish_qkv(a.pp, r0 + cbase + c, sel, jrow, acc[c]);
+            } else if (EPI == EPI_ROPE) {
+                if (!rope_pairs) {
+#pragma unroll
+                    for (int c = 0; c < COLS; c++)
+                        if (r0 + cbase + c < a.m) finish_rope_v(a.pp, r0 + cbase + c, jrow, acc[c]);
+                } else {
+                    // sel is the CTA's: every scaler thread reaches the barrier
+                    if (second) {
+#pragma unroll
+                        for (int c = 0; c < COLS; c++) part[(cbase + c) * PART_LD + jl] = acc[c];
+                    }
+                    named_sync(1, SCALE_THREADS);
+                    if (!second)
+#pragma unroll
+                        for (int c = 0; c < COLS; c++)
+                            if (r0 + cbase + c < a.m)
+                                finish_rope(a.pp, r0 + cbase + c, sel, jrow, acc[c], part[(cbase + c) * PART_LD + jl + half]);
                 }
             } else {
                 if (up) {
@@ -491,16 +593,27 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t base[MAX_KS];
 #pragma unroll
             for (int rk = 0; rk < MAX_KS; rk++) base[rk] = rk < a.ks ? cluster_addr(part + jl, rk) : 0u;
-            for (int c = c0 + cg; c < c1; c += 2) {
+            // a RoPE pair's first row also sums its partner's column
+            const uint32_t partner = (uint32_t)half * 4;
+            for (int c = c0 + cg; c < c1 && !second; c += 2) {
                 if (r0 + c >= a.m) break;
-                float p[MAX_KS];
+                float p[MAX_KS], q[MAX_KS];
 #pragma unroll
-                for (int rk = 0; rk < MAX_KS; rk++) p[rk] = rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4) : 0.f;
-                float v = 0.f;
+                for (int rk = 0; rk < MAX_KS; rk++) {
+                    p[rk] = rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4) : 0.f;
+                    q[rk] = rope_pairs && rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4 + partner) : 0.f;
+                }
+                float v = 0.f, vb = 0.f;
 #pragma unroll
                 for (int rk = 0; rk < MAX_KS; rk++)
-                    if (rk < a.ks) v = __fadd_rn(v, p[rk]);
-                finish(a, r0 + c, jrow, v);
+                    if (rk < a.ks) {
+                        v = __fadd_rn(v, p[rk]);
+                        vb = __fadd_rn(vb, q[rk]);
+                    }
+                if (EPI == EPI_PLAIN) finish(a, r0 + c, jrow, v);
+                else if (EPI == EPI_QKV) finish_qkv(a.pp, r0 + c, sel, jrow, v);
+                else if (rope_pairs) finish_rope(a.pp, r0 + c, sel, jrow, v, vb);
+                else finish_rope_v(a.pp, r0 + c, jrow, v);
             }
         }
         // no CTA leaves while another may still read its partial tile
@@ -538,24 +651,31 @@ bool map_2d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t i
 
 }  // namespace
 
-// The tensor-core Q8 product when it applies: returns 1 (not taken: the caller runs the
-// CUDA-core kernel) for shapes it does not cover, 0 after a launch, -1 on a launch failure.
-// wu/su/bu non-null: the SiLU pair (out = silu(x . Wg^T + bg) * (x . Wu^T + bu)).
-int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
-                 int mode, const int8_t* wu, const float* su, const float* bu, float* out, int sm_count,
-                 cudaStream_t st) {
+namespace {
+
+// One launch of the tensor-core kernel for x [m][k] against the weight tiles of the mode
+// (PLAIN / SILU: n rows of wq (and wu); ROPE / QKV: the three matrices of pp, rows[i] each).
+// Returns 1 when the shape is not covered (the caller runs the CUDA-core kernel), 0 after a
+// launch, -1 on a launch failure.
+int tc_launch(int epi, const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias,
+              size_t n, int mode, const int8_t* wu, const float* su, const float* bu, const PairParams* pp,
+              const size_t* rows, float* out, int sm_count, cudaStream_t st) {
     using namespace q8tc;
-    const bool pair = wu != nullptr;
+    const bool pair = epi == EPI_SILU, sec = epi == EPI_ROPE || epi == EPI_QKV;
     if (!q8tc::g_enabled.load(std::memory_order_relaxed)) return 1;
     if (m < 16 || n == 0 || k == 0 || k % BK) return 1;
     if (((uintptr_t)x & 15) || ((uintptr_t)wq & 15) || (pair && ((uintptr_t)wu & 15))) return 1;
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return 1;
     if (pair && mode != LIN_STORE) return 1;
+    if (sec)
+        for (int i = 0; i < 3; i++)
+            if (rows[i] == 0 || rows[i] % BM || !pp->wq[i] || ((uintptr_t)pp->wq[i] & 15)) return 1;
     // up to 64 rows the small tile form (pieces along N), else the large one
     const bool small = m <= 64;
     const int tn = small ? Tr<true>::TN : Tr<false>::TN;
     const int rows_w = pair ? BM / 2 : BM;
-    const size_t tiles_n = (n + rows_w - 1) / rows_w, tiles_m = (m + tn - 1) / tn;
+    const size_t tiles_n = sec ? (rows[0] + rows[1] + rows[2]) / BM : (n + rows_w - 1) / rows_w;
+    const size_t tiles_m = (m + tn - 1) / tn;
     if (tiles_n > 0x7fffffff || tiles_m > 65535) return 1;
     // k splits (powers of two, at most 8, at least two k steps each) while the doubled grid
     // still fits in one wave (one CTA per SM): a second, mostly empty wave costs more than the
@@ -566,10 +686,18 @@ int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const flo
            steps / (2 * ks) >= 2)
         ks *= 2;
 
-    CUtensorMap mw, mwu, mx;
-    if (!map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, k, n, k, BK, rows_w)) return -1;
-    if (pair && !map_2d(&mwu, CU_TENSOR_MAP_DATA_TYPE_UINT8, wu, k, n, k, BK, rows_w)) return -1;
-    if (!pair) mwu = mw;
+    CUtensorMap mw, mwu, mw3, mx;
+    if (sec) {
+        if (!map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, pp->wq[0], k, rows[0], k, BK, BM) ||
+            !map_2d(&mwu, CU_TENSOR_MAP_DATA_TYPE_UINT8, pp->wq[1], k, rows[1], k, BK, BM) ||
+            !map_2d(&mw3, CU_TENSOR_MAP_DATA_TYPE_UINT8, pp->wq[2], k, rows[2], k, BK, BM))
+            return -1;
+    } else {
+        if (!map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, k, n, k, BK, rows_w)) return -1;
+        if (pair && !map_2d(&mwu, CU_TENSOR_MAP_DATA_TYPE_UINT8, wu, k, n, k, BK, rows_w)) return -1;
+        if (!pair) mwu = mw;
+        mw3 = mw;
+    }
     if (!map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, k, m, k * 4, BK, (uint32_t)tn)) return -1;
 
     Args a{};
@@ -584,14 +712,22 @@ int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const flo
     a.bias_u = bu;
     a.out = out;
     a.err = capi::current_err_word();
+    if (sec) {
+        a.pp = *pp;
+        for (int i = 0; i < 3; i++) a.tiles[i] = (int)(rows[i] / BM);
+    }
 
     static std::mutex mu;
-    static bool attr_set[64][4] = {};
+    static bool attr_set[64][8] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
-    const int variant = (pair ? 1 : 0) + (small ? 2 : 0);
-    auto kern = pair ? (small ? q8_tc_kernel<true, true> : q8_tc_kernel<true, false>)
-                     : (small ? q8_tc_kernel<false, true> : q8_tc_kernel<false, false>);
+    const int variant = epi * 2 + (small ? 1 : 0);
+    using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Args);
+    static const Kern kerns[8] = {q8_tc_kernel<EPI_PLAIN, false>, q8_tc_kernel<EPI_PLAIN, true>,
+                                  q8_tc_kernel<EPI_SILU, false>,  q8_tc_kernel<EPI_SILU, true>,
+                                  q8_tc_kernel<EPI_ROPE, false>,  q8_tc_kernel<EPI_ROPE, true>,
+                                  q8_tc_kernel<EPI_QKV, false>,   q8_tc_kernel<EPI_QKV, true>};
+    const Kern kern = kerns[variant];
     const size_t smem = small ? smem_bytes<true>() : smem_bytes<false>();
     {
         std::lock_guard<std::mutex> lk(mu);
@@ -615,7 +751,37 @@ int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const flo
     attr[1].val.clusterDim.z = (unsigned)ks;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, mw, mwu, mx, a) == cudaSuccess ? 0 : -1;
+    return cudaLaunchKernelEx(&cfg, kern, mw, mwu, mw3, mx, a) == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace
+
+// The tensor-core Q8 product when it applies: returns 1 (not taken: the caller runs the
+// CUDA-core kernel) for shapes it does not cover, 0 after a launch, -1 on a launch failure.
+// wu/su/bu non-null: the SiLU pair (out = silu(x . Wg^T + bg) * (x . Wu^T + bu)).
+int q8_tc_launch(const float* x, size_t m, size_t k, const int8_t* wq, const float* ws, const float* bias, size_t n,
+                 int mode, const int8_t* wu, const float* su, const float* bu, float* out, int sm_count,
+                 cudaStream_t st) {
+    return tc_launch(wu ? q8tc::EPI_SILU : q8tc::EPI_PLAIN, x, m, k, wq, ws, bias, n, mode, wu, su, bu, nullptr,
+                     nullptr, out, sm_count, st);
+}
+
+// The Qwen2 RoPE pair (q8_pair_launch's PAIR_ROPE) on the tensor cores: q, k and v of
+// p.n_head / p.n_head_kv heads of p.d rows, rows of each matrix a multiple of 128.
+int q8_tc_rope_launch(const PairParams& p, int sm_count, cudaStream_t st) {
+    const size_t rows[3] = {(size_t)p.n_head * p.d, (size_t)p.n_head_kv * p.d, (size_t)p.n_head_kv * p.d};
+    if (p.d <= 0 || q8tc::BM % p.d) return 1;
+    return tc_launch(q8tc::EPI_ROPE, p.x, (size_t)p.m, (size_t)p.k, p.wq[0], p.ws[0], nullptr,
+                     rows[0] + rows[1] + rows[2], LIN_STORE, nullptr, nullptr, nullptr, &p, rows, nullptr, sm_count,
+                     st);
+}
+
+// The Whisper decoder's q/k/v product (q8_gemm_qkv_launch's PE_QKV) on the tensor cores:
+// three matrices of p.d rows, p.d a multiple of 128.
+int q8_tc_qkv_launch(const PairParams& p, int sm_count, cudaStream_t st) {
+    const size_t rows[3] = {(size_t)p.d, (size_t)p.d, (size_t)p.d};
+    return tc_launch(q8tc::EPI_QKV, p.x, (size_t)p.m, (size_t)p.k, p.wq[0], p.ws[0], nullptr, 3 * (size_t)p.d,
+                     LIN_STORE, nullptr, nullptr, nullptr, &p, rows, nullptr, sm_count, st);
 }
 
 }  // namespace zwg
