@@ -412,6 +412,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<D>::CTAS_PER_SM)
         tc_fence_before();
     }
 
+    // warps whose loops ran in lane 0 alone reach the barrier converged
+    __syncwarp();
     __syncthreads();
     if (sm.last && !*(volatile int*)&sm.abort_flag) {
         // ---- merge of the segment's pieces: thread = (row, 4 columns)

@@ -431,6 +431,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     }
 
+    // warps whose loops ran in lane 0 alone reach the barrier converged
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

@@ -411,6 +411,8 @@ tmem_st64(p_addr, pk);  // the row's 64 bf16 pairs, one store
     }
 
     if (warp >= 4 && lane == 0) bulk_wait0();
+    // warps whose loops ran in lane 0 alone reach the barrier converged
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

@@ -266,10 +266,8 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
     return r;
 }
 
-__device__ __forceinline__ float ld_cluster(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
+__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, const void* dst, int c0, int c1) {
@@ -426,11 +424,32 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (i >= NSC && !(ok = mbar_wait_warp(&sm.cv_empty[cs], ((i / NSC) - 1) & 1, a.err))) break;
             const uint32_t rw = smem_u32(sm.raw_w[rs]), rx = smem_u32(sm.raw_x[rs]);
             const uint32_t ca = smem_u32(sm.cv_a[cs]), cb = smem_u32(sm.cv_b[cs]);
+            // Every shared load of the step is issued before the first conversion, so the
+            // thread waits out one load latency per step instead of one per chunk.
             // weights: row r, 16 int8 (chunk c4 of the 64-byte row) -> two 16-byte chunks
+            uint4 wv[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) wv[u] = ld_shared_v4(rw + ((ct >> 2) + 64 * u) * BK + (ct & 3) * 16);
+            // activations: row r, 8 f32 (chunk c8, two 16-byte halves) -> one 16-byte chunk
+            // of each piece. Lane map: the 8 lanes of a quarter warp take 4 chunks of row r
+            // (half 0 first) and the same 4 chunks of row r + 4 (half 1 first), so their
+            // loads fall in 8 distinct bank groups and so do their stores (swizzle r & 7
+            // differs in bit 2). Rows past m stay zero once written.
+            const int xh = (ct >> 2) & 1, q4 = (ct >> 3) & 3, cw = ct >> 5;
+            const int c8 = (ct & 3) + 4 * (q4 & 1);
+            const int xr = 4 * xh + (q4 >> 1) + 2 * (cw & 1) + 8 * (cw >> 1);
+            uint4 xa[TN / 32], xb[TN / 32];
+#pragma unroll
+            for (int u = 0; u < TN / 32; u++) {
+                const int r = xr + 32 * u;
+                if (i >= NSC && r0 + r >= a.m) continue;
+                xa[u] = ld_shared_v4(rx + r * (BK * 4) + c8 * 32 + xh * 16);
+                xb[u] = ld_shared_v4(rx + r * (BK * 4) + c8 * 32 + (xh ^ 1) * 16);
+            }
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 const int r = (ct >> 2) + 64 * u, c4 = ct & 3;
-                const uint4 w = ld_shared_v4(rw + r * BK + c4 * 16);
+                const uint4 w = wv[u];
                 uint4 o0, o1;
                 int8x4_to_bf16(w.x, o0.x, o0.y);
                 int8x4_to_bf16(w.y, o0.z, o0.w);
@@ -440,14 +459,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 st_shared_v4(ca + r * 128 + (((2 * c4) ^ sw) << 4), o0);
                 st_shared_v4(ca + r * 128 + (((2 * c4 + 1) ^ sw) << 4), o1);
             }
-            // activations: row r, 8 f32 (chunk c8) -> one 16-byte chunk of each piece; rows
-            // past m stay zero once written
 #pragma unroll
             for (int u = 0; u < TN / 32; u++) {
-                const int r = (ct >> 3) + 32 * u, c8 = ct & 7;
+                const int r = xr + 32 * u;
                 if (i >= NSC && r0 + r >= a.m) continue;
-                const uint4 x0 = ld_shared_v4(rx + r * (BK * 4) + c8 * 32);
-                const uint4 x1 = ld_shared_v4(rx + r * (BK * 4) + c8 * 32 + 16);
+                const uint4 x0 = xh ? xb[u] : xa[u];
+                const uint4 x1 = xh ? xa[u] : xb[u];
                 uint4 ph, pm, pl;
                 split3(__uint_as_float(x0.x), __uint_as_float(x0.y), ph.x, pm.x, pl.x);
                 split3(__uint_as_float(x0.z), __uint_as_float(x0.w), ph.y, pm.y, pl.y);
@@ -458,12 +475,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                 st_shared_v4(cb + CV_P + off, pm);
                 st_shared_v4(cb + 2 * CV_P + off, pl);
             }
+            // every raw value has been consumed: the stage goes back to the producer before
+            // the proxy fence below waits for this thread's stores
+            mbar_arrive(&sm.raw_empty[rs]);
             // the tensor core (async proxy) reads what these threads wrote
             fence_proxy_async_smem();
             mbar_arrive(&sm.cv_full[cs]);
-            mbar_arrive(&sm.raw_empty[rs]);
         }
     }
+    // the producer and MMA warps ran their loops in lane 0 alone: every warp reaches the
+    // CTA and cluster barriers below converged
+    __syncwarp();
 
     // ------------------------------------------------------------ scalers and epilogue
     float2 acc2[COLS / 2];                                 // (row 2c, row 2c + 1) of this thread's rows
@@ -580,44 +602,62 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
+        // Rank o owns activation rows [o R, (o + 1) R), R = TN / ks. Once every rank's MMAs
+        // are done with its operand ring (first cluster barrier), each scaler stores its
+        // partial rows straight into the owner's ring, as row rk R + (row - o R) of rank
+        // rk's block there: remote stores, which do not wait on the cluster's latency the
+        // way remote loads would. After the second barrier every owner sums its rows from
+        // its own shared memory in rank order (the same order, so the same sums, whatever
+        // the timing), and no CTA touches another's memory again.
+        const int R = TN / a.ks, lr = __ffs(R) - 1;       // ks is a power of two
+        const int c0 = rank * R;
+        cluster_sync();
         if (scaler) {
 #pragma unroll
-            for (int c = 0; c < COLS; c++) part[(cbase + c) * PART_LD + jl] = acc[c];
+            for (int c = 0; c < COLS; c++) {
+                const int row = cbase + c;
+                if (r0 + row >= a.m) break;
+                const int o = row >> lr;
+                st_cluster(cluster_addr(part + (rank * R + (row - o * R)) * PART_LD + jl, o), acc[c]);
+            }
         }
         cluster_sync();
         if (scaler && row_ok) {
-            // this CTA's share of the activation rows, summed over the ranks in order; all
-            // ranks' values of a row are loaded before the first add, so the remote loads
-            // overlap instead of waiting one after another
-            const int c0 = (rank * TN) / a.ks, c1 = ((rank + 1) * TN) / a.ks;
-            uint32_t base[MAX_KS];
+            // a RoPE pair's first row also sums its partner's column. Four rows at a time:
+            // every rank's values of the four are loaded before the first add.
+            const int c_end = min(c0 + R, a.m - r0);
+            for (int cb = c0 + cg; cb < c_end && !second; cb += 8) {
+                float v[4], vb[4];
 #pragma unroll
-            for (int rk = 0; rk < MAX_KS; rk++) base[rk] = rk < a.ks ? cluster_addr(part + jl, rk) : 0u;
-            // a RoPE pair's first row also sums its partner's column
-            const uint32_t partner = (uint32_t)half * 4;
-            for (int c = c0 + cg; c < c1 && !second; c += 2) {
-                if (r0 + c >= a.m) break;
-                float p[MAX_KS], q[MAX_KS];
+                for (int u = 0; u < 4; u++) {
+                    float p[MAX_KS], q[MAX_KS];
+                    const int c = min(cb + 2 * u, c0 + R - 1);
 #pragma unroll
-                for (int rk = 0; rk < MAX_KS; rk++) {
-                    p[rk] = rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4) : 0.f;
-                    q[rk] = rope_pairs && rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4 + partner) : 0.f;
-                }
-                float v = 0.f, vb = 0.f;
-#pragma unroll
-                for (int rk = 0; rk < MAX_KS; rk++)
-                    if (rk < a.ks) {
-                        v = __fadd_rn(v, p[rk]);
-                        vb = __fadd_rn(vb, q[rk]);
+                    for (int rk = 0; rk < MAX_KS; rk++) {
+                        const float* pr = part + (rk * R + (c - c0)) * PART_LD + jl;
+                        p[rk] = rk < a.ks ? pr[0] : 0.f;
+                        q[rk] = rope_pairs && rk < a.ks ? pr[half] : 0.f;
                     }
-                if (EPI == EPI_PLAIN) finish(a, r0 + c, jrow, v);
-                else if (EPI == EPI_QKV) finish_qkv(a.pp, r0 + c, sel, jrow, v);
-                else if (rope_pairs) finish_rope(a.pp, r0 + c, sel, jrow, v, vb);
-                else finish_rope_v(a.pp, r0 + c, jrow, v);
+                    v[u] = 0.f;
+                    vb[u] = 0.f;
+#pragma unroll
+                    for (int rk = 0; rk < MAX_KS; rk++)
+                        if (rk < a.ks) {
+                            v[u] = __fadd_rn(v[u], p[rk]);
+                            vb[u] = __fadd_rn(vb[u], q[rk]);
+                        }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int c = cb + 2 * u;
+                    if (c >= c_end) break;
+                    if (EPI == EPI_PLAIN) finish(a, r0 + c, jrow, v[u]);
+                    else if (EPI == EPI_QKV) finish_qkv(a.pp, r0 + c, sel, jrow, v[u]);
+                    else if (rope_pairs) finish_rope(a.pp, r0 + c, sel, jrow, v[u], vb[u]);
+                    else finish_rope_v(a.pp, r0 + c, jrow, v[u]);
+                }
             }
         }
-        // no CTA leaves while another may still read its partial tile
-        cluster_sync();
     }
 
     tc_fence_before();
@@ -653,6 +693,36 @@ bool map_2d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t i
 
 namespace {
 
+// How many clusters of cs CTAs (1 x 1 x cs) of kernel variant `variant` can be resident at
+// once on device dev (the occupancy API's answer, cached); 0 when the query fails.
+int max_clusters(int dev, int variant, const void* kern, size_t smem, int cs) {
+    static std::mutex mu;
+    static int cache[64][8][4] = {};
+    const int li = cs == 2 ? 1 : cs == 4 ? 2 : cs == 8 ? 3 : 0;
+    std::lock_guard<std::mutex> lk(mu);
+    int& slot = cache[dev][variant][li];
+    if (slot == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1, 1, (unsigned)cs);
+        cfg.blockDim = dim3(q8tc::THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 1;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = (unsigned)cs;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            n = 0;
+        }
+        slot = n > 0 ? n : -1;
+    }
+    return slot > 0 ? slot : 0;
+}
+
 // One launch of the tensor-core kernel for x [m][k] against the weight tiles of the mode
 // (PLAIN / SILU: n rows of wq (and wu); ROPE / QKV: the three matrices of pp, rows[i] each).
 // Returns 1 when the shape is not covered (the caller runs the CUDA-core kernel), 0 after a
@@ -677,14 +747,6 @@ int tc_launch(int epi, const float* x, size_t m, size_t k, const int8_t* wq, con
     const size_t tiles_n = sec ? (rows[0] + rows[1] + rows[2]) / BM : (n + rows_w - 1) / rows_w;
     const size_t tiles_m = (m + tn - 1) / tn;
     if (tiles_n > 0x7fffffff || tiles_m > 65535) return 1;
-    // k splits (powers of two, at most 8, at least two k steps each) while the doubled grid
-    // still fits in one wave (one CTA per SM): a second, mostly empty wave costs more than the
-    // longer k ranges; the pair keeps whole k ranges
-    const size_t steps = k / BK;
-    int ks = 1;
-    while (!pair && ks < MAX_KS && tiles_n * tiles_m * (size_t)(2 * ks) <= (size_t)std::max(1, sm_count) &&
-           steps / (2 * ks) >= 2)
-        ks *= 2;
 
     CUtensorMap mw, mwu, mw3, mx;
     if (sec) {
@@ -704,7 +766,6 @@ int tc_launch(int epi, const float* x, size_t m, size_t k, const int8_t* wq, con
     a.m = (int)m;
     a.n = (int)n;
     a.k = (int)k;
-    a.ks = ks;
     a.mode = mode;
     a.ws = ws;
     a.wsu = su;
@@ -737,6 +798,18 @@ int tc_launch(int epi, const float* x, size_t m, size_t k, const int8_t* wq, con
             attr_set[dev][variant] = true;
         }
     }
+    // k splits (powers of two, at most 8, at least two k steps each) while the doubled grid
+    // still fits in one wave (one CTA per SM) and its clusters can all be resident at once
+    // (a cluster lies within one GPC, so fewer clusters of 4 or 8 fit than SMs / size): a
+    // second, mostly empty wave costs more than the longer k ranges; the pair keeps whole k
+    // ranges
+    const size_t steps = k / BK;
+    int ks = 1;
+    while (!pair && ks < MAX_KS && tiles_n * tiles_m * (size_t)(2 * ks) <= (size_t)std::max(1, sm_count) &&
+           steps / (2 * ks) >= 2 &&
+           tiles_n * tiles_m <= (size_t)max_clusters(dev, variant, (const void*)kern, smem, 2 * ks))
+        ks *= 2;
+    a.ks = ks;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)tiles_n, (unsigned)tiles_m, (unsigned)ks);
     cfg.blockDim = dim3(THREADS);
