@@ -336,15 +336,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int i = 0; i < BN; i++)
                         if (i >= valid) sr[i] = __float_as_uint(-INFINITY);
                 }
-                // row max over 8 independent partial maxima
+                // row max over 8 independent partial maxima, two new scores per three-input max
                 float mxp[8];
 #pragma unroll
-                for (int k = 0; k < 8; k++) mxp[k] = __uint_as_float(sr[k]);
+                for (int k = 0; k < 8; k++) mxp[k] = fmaxf(__uint_as_float(sr[k]), __uint_as_float(sr[k + 8]));
 #pragma unroll
-                for (int i = 8; i < BN; i++) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sr[i]));
+                for (int i = 16; i < BN; i += 16)
 #pragma unroll
-                for (int k = 0; k < 4; k++) mxp[k] = fmaxf(mxp[k], mxp[k + 4]);
-                const float m_tile = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])) * c;
+                    for (int k = 0; k < 8; k++)
+                        mxp[k] = fmax3(mxp[k], __uint_as_float(sr[i + k]), __uint_as_float(sr[i + 8 + k]));
+                const float m_tile =
+                    fmaxf(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], fmax3(mxp[5], mxp[6], mxp[7]))) * c;
                 // the running max is kept stale unless it grows by more than 2^8
                 const bool rescale = j > 0 && m_tile > m + 8.0f;
                 const float m_old = m;

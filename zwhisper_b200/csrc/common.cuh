@@ -53,6 +53,14 @@ ZWG_DEV float2 exp2_poly2(float2 x) {
     return p;
 }
 
+// max of three floats in one instruction (PTX three-input max.f32, sm_100a); a NaN operand
+// is ignored as by fmaxf
+ZWG_DEV float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 ZWG_DEV float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
