@@ -896,6 +896,8 @@ def run_kernel_case(args):
     `decode_whisper` = the split-K kernel on 32 base.en windows of cross-attention;
     `prefill_qwen` = the tf32 prefill kernel on the last 208-query chunk of a 2000-token
     prompt for 64 Qwen2.5-1.5B sequences (one layer, 268 MB of K^T/V, above L2);
+    `prefill_qwen05` = the same chunk for 16 Qwen2.5-0.5B sequences (d 64, config 3's shape;
+    33.5 MB of K^T/V);
     `q8_logits` = the Q8 linear kernel on the Whisper base.en logits product (51864 x 512);
     `step_qwen15` = one whole Qwen2.5-1.5B greedy decode step for one sequence (n_kv 2256),
     every kernel of the step in launch order (about 200 launches); `step_whisper_base` = one
@@ -1015,8 +1017,9 @@ def run_kernel_case(args):
         def fn():
             ops.encoder_forward(Wg, mel, B, out=out, scratch=scratch)
         work = f"the whole small.en encoder for {B} windows"
-    elif args.kernel_case == "prefill_qwen":
-        B, H, Hkv, d, n_ctx, n_past, n_q = 64, 12, 2, 128, 2048, 1792, 208
+    elif args.kernel_case in ("prefill_qwen", "prefill_qwen05"):
+        B, H, Hkv, d, n_ctx, n_past, n_q = ((64, 12, 2, 128, 2048, 1792, 208) if args.kernel_case == "prefill_qwen"
+                                            else (16, 14, 2, 64, 2048, 1792, 208))
         q = torch.randn(B, n_q, H * d, generator=g, device=dev)
         kt = torch.randn(B, Hkv, d, n_ctx, generator=g, device=dev)
         v = torch.randn(B, n_ctx, Hkv * d, generator=g, device=dev)
@@ -1059,7 +1062,7 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernel-case", choices=["enc_tc", "decode_qwen", "decode_qwen05", "decode_qwen_b1", "decode_tc_qwen64",
-                                             "decode_tc_qwen_b1", "decode_whisper", "prefill_qwen",
+                                             "decode_tc_qwen_b1", "decode_whisper", "prefill_qwen", "prefill_qwen05",
                                              "q8_logits", "step_qwen15", "step_whisper_base", "pair_qwen15",
                                              "gemm_mlp2", "encoder_small_en", "q8_gateup64", "decode_tc_qwen05"],
                     default=None)
