@@ -89,6 +89,73 @@ def test_prefill_tf32_matches_oracle(env, B, H, Hkv, d, n_ctx, n_past, n_q, caus
         np.testing.assert_allclose(got[b].reshape(-1), want, atol=TC_ATOL, rtol=TC_RTOL)
 
 
+# d = 64 launches with enough items run two query tiles per item (a K/V tile feeds both, one
+# softmax warpgroup each) when that form needs fewer waves of items by its weight (a paired
+# item ~1.74 single ones) on 148 SMs; these shapes are chosen to take it: an even and an odd
+# number of query tiles (the last pair's second tile past the end), several items per CTA,
+# and a non-causal MHA launch.
+PAIRED = [
+    # B, H, Hkv, d, n_ctx, n_past, n_q, causal
+    (16, 14, 2, 64, 2048, 1856, 144, True),   # 8 query tiles: 256 tiles, 128 pairs
+    (16, 14, 2, 64, 1024, 900, 120, True),    # 7 query tiles: 224 tiles, 128 pairs
+    (16, 14, 2, 64, 2048, 0, 256, True),      # first chunk: 480 tiles, 256 pairs
+    (64, 4, 4, 64, 512, 0, 150, False),       # MHA, not causal: 512 tiles, 256 pairs
+]
+
+
+@pytest.mark.parametrize("B,H,Hkv,d,n_ctx,n_past,n_q,causal", PAIRED)
+def test_prefill_tf32_two_tiles_per_item(env, B, H, Hkv, d, n_ctx, n_past, n_q, causal):
+    torch, ops = env
+    import re
+    rng = np.random.default_rng(2000 + n_past + n_q + B)
+    n_kv = n_past + n_q
+    kvw = Hkv * d
+    q = rng.standard_normal((B, n_q, H * d), dtype=np.float32)
+    kt = rng.standard_normal((B, Hkv, d, n_ctx), dtype=np.float32)
+    v = rng.standard_normal((B, n_ctx, kvw), dtype=np.float32)
+    sh = ops.AttnShape(n_q, n_kv, H, Hkv, d, H * d, kvw, H * d, causal, n_ctx)
+    dev = torch.device("cuda:0")
+    if torch.cuda.get_device_properties(dev).multi_processor_count != 148:
+        pytest.skip("the shapes are chosen for 148 SMs")
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q, kt, v))
+    out = torch.full_like(tq, float("nan"))
+    names = kernels_run(torch, lambda: ops.attention_dev(tq, tk, tv, sh, out, n_batch=B))
+    assert any(re.search(r"prefill_tc_kernel<64, ?2>", n) for n in names), names
+    got = out.cpu().numpy()
+    sho = A.AttnShape(n_q, n_kv, H, Hkv, d, H * d, kvw, H * d, causal, n_ctx)
+    for b in range(B):
+        want = A.attention_ex(q[b].reshape(-1), kt[b].reshape(-1), v[b].reshape(-1), sho)
+        np.testing.assert_allclose(got[b].reshape(-1), want, atol=TC_ATOL, rtol=TC_RTOL)
+
+
+def test_prefill_tf32_rescale_path_two_tiles(env):
+    """The rescale test's key growth with enough sequences for the paired form (20 x 2
+    (sequence, kv head) pairs x 13 query tiles: 520 tiles, 280 pairs)."""
+    torch, ops = env
+    import re
+    rng = np.random.default_rng(77)
+    B, H, Hkv, d, n_ctx, n_past, n_q = 20, 12, 2, 64, 2048, 1744, 256
+    n_kv = n_past + n_q
+    slope = 0.5 + rng.random((B, n_q, 1), dtype=np.float32)
+    q = (slope + 0.1 * rng.standard_normal((B, n_q, H * d), dtype=np.float32)).astype(np.float32)
+    pos = np.arange(n_ctx, dtype=np.float32)
+    kt = (0.2 * pos / 64 + 0.1 * rng.standard_normal((B, Hkv, d, n_ctx), dtype=np.float32)).astype(np.float32)
+    v = rng.standard_normal((B, n_ctx, Hkv * d), dtype=np.float32)
+    sh = ops.AttnShape(n_q, n_kv, H, Hkv, d, H * d, Hkv * d, H * d, True, n_ctx)
+    dev = torch.device("cuda:0")
+    if torch.cuda.get_device_properties(dev).multi_processor_count != 148:
+        pytest.skip("the shape is chosen for 148 SMs")
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q, kt, v))
+    out = torch.full_like(tq, float("nan"))
+    names = kernels_run(torch, lambda: ops.attention_dev(tq, tk, tv, sh, out, n_batch=B))
+    assert any(re.search(r"prefill_tc_kernel<64, ?2>", n) for n in names), names
+    sho = A.AttnShape(n_q, n_kv, H, Hkv, d, H * d, Hkv * d, H * d, True, n_ctx)
+    got = out.cpu().numpy()
+    for b in (0, 7, 19):
+        want = A.attention_ex(q[b].reshape(-1), kt[b].reshape(-1), v[b].reshape(-1), sho)
+        np.testing.assert_allclose(got[b].reshape(-1), want, atol=TC_ATOL, rtol=TC_RTOL)
+
+
 @pytest.mark.parametrize("d", [64, 128])
 def test_prefill_tf32_rescale_path(env, d):
     """Keys scaled up with their position make the scores grow tile by tile, so the running

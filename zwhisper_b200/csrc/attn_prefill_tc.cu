@@ -39,6 +39,10 @@
 //     stale unless it grows by more than 2^8, exp2 on the MUFU, P rounded to tf32 (round to
 //     nearest), and the epilogue O / l.
 //   - Persistent grid over (sequence, kv head, query tile) items, a pair's tiles adjacent.
+//   - d = 64, launches with enough items: two query tiles per item (one score buffer each,
+//     a softmax warpgroup each, ring order K0 V0 K1 V1 ..., MMA order S_0(0) S_1(0) | PV_0(j)
+//     S_0(j+1) PV_1(j) S_1(j+1) ...), chosen at launch when it needs fewer item-waves by its
+//     weight; Cfg below.
 // Every wait is bounded; a wait that runs out records kErrTimeout, the CTA drains its own
 // copies and MMAs with bounded waits, frees TMEM and returns.
 #include <cuda.h>
@@ -58,7 +62,6 @@ using namespace sm100;
 
 constexpr int BM = 128;                // rows per tile = TMEM lanes
 constexpr int BN = 128;                // keys per tile
-constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
 
 // Pairs of exponentials per 16 evaluated by exp2_poly2 on the FMA pipe (relative error
 // 1e-4, below tf32's rounding of P); the others use the MUFU ex2, 16 per clock per SM.
@@ -68,36 +71,57 @@ constexpr int THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 soft
 // is no longer the limit here (it was: cvt.rna.tf32 shared it with ex2).
 constexpr int POLY_PAIRS = 1;
 
-// Two score buffers (S(j+1) is computed while the softmax works on S(j)), one CTA per SM
-// with 512 TMEM columns; the ring has three 64 KB slots at d = 128, six 32 KB slots at
-// d = 64. (Measured at d = 64, config 3's last chunk: one score buffer with two CTAs per SM
-// and 256 columns each took 0.104 ms against 0.096 ms for this layout.)
-template <int D>
+// One CTA per SM with 512 TMEM columns; the ring has three 64 KB slots at d = 128, six
+// 32 KB slots at d = 64.
+//   d = 128: one query tile per item, two score buffers (S(j+1) is computed while the
+//            softmax works on S(j)); warp 0 TMA, warp 1 MMA, warps 2-5 softmax.
+//   d = 64:  two query tiles per item (NT = 2) that share every K/V tile, one score buffer
+//            each, a softmax warpgroup each (warps 4-7 and 8-11; warps 0-3 are the control
+//            warpgroup: 0 TMA, 1 MMA): while one tile's softmax runs, the tensor core works
+//            on the other tile, and each K/V tile feeds twice the rows. At d = 64 one query
+//            tile's MMAs (S 8 x N128 and PV 16 x N64, the latter at half rate) take ~2,000
+//            clocks per key tile against ~1,750 for its softmax, so a single tile per CTA
+//            left the tensor core waiting for every P. TMEM per tile: Q 64, S 128, O 64.
+template <int D, int NT_ = 1>
 struct Cfg {
-    static constexpr int SBUF = 2;                          // score buffers
+    static constexpr int NT = NT_;                          // query tiles per item
+    static_assert(NT == 1 || D == 64, "two query tiles per item fit TMEM at d = 64 only");
+    static constexpr int SBUF = NT == 2 ? 1 : 2;            // score buffers per query tile
+    static constexpr int THREADS = NT == 2 ? 384 : 192;
+    static constexpr int SM_WARP0 = NT == 2 ? 4 : 2;        // first softmax warp
     static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t TILE_COLS = TMEM_COLS / NT;   // TMEM columns of one query tile
     static constexpr uint32_t K_CHUNK = D * 128;            // [D rows][32 keys]
     static constexpr uint32_t V_CHUNK = BN * 128;           // [128 keys][32 floats]
     static constexpr uint32_t SLOT = BN * D * 4;            // one K^T or V tile
     static constexpr int NSLOT = D == 128 ? 3 : 6;
-    static constexpr uint32_t Q_COL = 0;
-    static constexpr uint32_t S_COL = D;                    // + buffer * BN
-    static constexpr uint32_t O_COL = D + SBUF * BN;
-    static_assert(O_COL + D <= TMEM_COLS, "TMEM columns");
+    static constexpr uint32_t Q_COL = 0;                    // + tile * TILE_COLS
+    static constexpr uint32_t S_COL = D;                    // + tile * TILE_COLS + buffer * BN
+    static constexpr uint32_t O_COL = D + SBUF * BN;        // + tile * TILE_COLS
+    static_assert(O_COL + D <= TILE_COLS, "TMEM columns");
 };
 
-template <int D>
+// d = 64 register split (setmaxnreg): launched at 168 per thread (65536 / 384 rounded down
+// to a multiple of 8) = 64512; the control warpgroup gives back to 56 and the two softmax
+// warpgroups take 224: 128 * 56 + 256 * 224 = 64512, the launch total exactly.
+constexpr uint32_t REGS_CONTROL = 56;
+constexpr uint32_t REGS_SOFTMAX = 224;
+static_assert(128 * REGS_CONTROL + 256 * REGS_SOFTMAX <= Cfg<64, 2>::THREADS * 168, "register split exceeds the launch");
+
+template <int D, int NT_>
 struct Smem {
-    alignas(1024) uint8_t ring[Cfg<D>::NSLOT][Cfg<D>::SLOT];
-    uint64_t full[Cfg<D>::NSLOT], empty[Cfg<D>::NSLOT];
-    uint64_t q_full, s_full[Cfg<D>::SBUF], p_full[Cfg<D>::SBUF], pv_done[2], drain;
+    using C = Cfg<D, NT_>;
+    static constexpr int NT = C::NT, SBUF = C::SBUF;
+    alignas(1024) uint8_t ring[C::NSLOT][C::SLOT];
+    uint64_t full[C::NSLOT], empty[C::NSLOT];
+    uint64_t q_full[NT], s_full[NT][SBUF], p_full[NT][SBUF], pv_done[NT][2], drain;
     uint32_t tmem_base;
     int abort_flag;
 };
 
-template <int D>
+template <int D, int NT>
 constexpr size_t smem_bytes() {
-    return sizeof(Smem<D>) + 1024;  // + alignment slack
+    return sizeof(Smem<D, NT>) + 1024;  // + alignment slack
 }
 
 struct Args {
@@ -105,7 +129,7 @@ struct Args {
     size_t q_stride, q_bs;
     float* out;
     size_t out_stride, out_bs;
-    int n_q, n_kv, n_head_kv, group, qn, rows, n_mt, n_items, causal;
+    int n_q, n_kv, n_head_kv, group, qn, rows, n_mt, n_units, n_items, causal;
     int* err;
 };
 
@@ -115,30 +139,33 @@ struct Args {
 // re-read its pair's 2 MB of K/V from DRAM: 2.3 GB of DRAM reads for 0.35 GB of inputs in
 // a 64-sequence launch.) The static stride over the persistent grid deals each CTA a mix
 // of long and short tiles.
-__device__ __forceinline__ void item_of(const Args& a, int idx, int& b, int& kh, int& mt) {
-    const int bh = idx / a.n_mt;
-    mt = a.n_mt - 1 - (idx - bh * a.n_mt);
+// An item is unit u of (sequence b, kv head kh): query tiles u * NT .. u * NT + NT - 1
+// (a tile past the last holds no valid rows).
+__device__ __forceinline__ void item_of(const Args& a, int idx, int& b, int& kh, int& u) {
+    const int bh = idx / a.n_units;
+    u = a.n_units - 1 - (idx - bh * a.n_units);
     b = bh / a.n_head_kv;
     kh = bh - b * a.n_head_kv;
 }
 
-// Key tiles a query tile needs: up to the causal limit of its last query.
-__device__ __forceinline__ int item_tiles(const Args& a, int mt) {
+// Key tiles an item needs: up to the causal limit of the last query of its last tile.
+template <int NT>
+__device__ __forceinline__ int item_tiles(const Args& a, int u) {
     int keys = a.n_kv;
     if (a.causal) {
-        const int last_q = min((mt + 1) * a.qn, a.n_q) - 1;
+        const int last_q = min(min((u + 1) * NT, a.n_mt) * a.qn, a.n_q) - 1;
         keys = min(a.n_kv - a.n_q + last_q + 1, a.n_kv);
     }
     return (keys + BN - 1) / BN;
 }
 
-template <int D>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int D, int NT>
+__global__ void __launch_bounds__(Cfg<D, NT>::THREADS, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const Args a) {
-    using C = Cfg<D>;
+    using C = Cfg<D, NT>;
     constexpr int NS = C::NSLOT;
     extern __shared__ uint8_t smem_raw[];
-    Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem<D, NT>& sm = *reinterpret_cast<Smem<D, NT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     int* err = a.err;
@@ -153,13 +180,15 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        mbar_init(&sm.q_full, 128);
-        for (int s = 0; s < C::SBUF; s++) {
-            mbar_init(&sm.s_full[s], 1);
-            mbar_init(&sm.p_full[s], 128);
+        for (int t = 0; t < NT; t++) {
+            mbar_init(&sm.q_full[t], 128);
+            for (int s = 0; s < C::SBUF; s++) {
+                mbar_init(&sm.s_full[t][s], 1);
+                mbar_init(&sm.p_full[t][s], 128);
+            }
+            mbar_init(&sm.pv_done[t][0], 1);
+            mbar_init(&sm.pv_done[t][1], 1);
         }
-        mbar_init(&sm.pv_done[0], 1);
-        mbar_init(&sm.pv_done[1], 1);
         mbar_init(&sm.drain, 1);
         fence_mbar_init();
     }
@@ -172,10 +201,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
-    if (warp == 0) {
+    if (warp < C::SM_WARP0) {
+      if constexpr (NT == 2) regs_dec<REGS_CONTROL>();
+      if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
-        // Loads go into the ring in the order the MMAs consume them; at exit (normal or not)
-        // the last loads are waited for, so no copy is in flight when the CTA's memory goes.
+        // Loads go into the ring in the order the MMAs first read them (one tile: K0 K1 V0
+        // K2 V1 K3 ...; two: K0 V0 K1 V1 ...); at exit (normal or not) the last loads are
+        // waited for, so no copy is in flight when the CTA's memory goes.
         if (lane == 0) {
             prefetch_tmap(&tm_k);
             prefetch_tmap(&tm_v);
@@ -199,13 +231,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                 return true;
             };
             for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
-                int b, kh, mt;
-                item_of(a, idx, b, kh, mt);
-                const int n_t = item_tiles(a, mt);
-                for (int j = 0; ok && j < C::SBUF && j < n_t; j++) ok = load(true, j, b, kh);
-                for (int j = 0; ok && j < n_t; j++) {
-                    ok = load(false, j, b, kh);
-                    if (ok && j + C::SBUF < n_t) ok = load(true, j + C::SBUF, b, kh);
+                int b, kh, u;
+                item_of(a, idx, b, kh, u);
+                const int n_t = item_tiles<NT>(a, u);
+                if constexpr (NT == 1) {
+                    for (int j = 0; ok && j < C::SBUF && j < n_t; j++) ok = load(true, j, b, kh);
+                    for (int j = 0; ok && j < n_t; j++) {
+                        ok = load(false, j, b, kh);
+                        if (ok && j + C::SBUF < n_t) ok = load(true, j + C::SBUF, b, kh);
+                    }
+                } else {
+                    for (int j = 0; ok && j < n_t; j++) {
+                        ok = load(true, j, b, kh);
+                        if (ok) ok = load(false, j, b, kh);
+                    }
                 }
             }
             for (uint32_t i = n > (uint32_t)NS ? n - NS : 0; i < n; i++) mbar_wait_drain(&sm.full[i % NS], (i / NS) & 1);
@@ -219,43 +258,91 @@ __global__ void __launch_bounds__(THREADS, 1)
             int it = 0;
             bool ok = true;
             for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x, it++) {
-                int b, kh, mt;
-                item_of(a, idx, b, kh, mt);
-                const int n_t = item_tiles(a, mt);
-                if (!(ok = mbar_wait(&sm.q_full, it & 1, err))) break;
+                int b, kh, u;
+                item_of(a, idx, b, kh, u);
+                const int n_t = item_tiles<NT>(a, u);
+                for (int t = 0; ok && t < NT; t++) ok = mbar_wait(&sm.q_full[t], it & 1, err);
+                if (!ok) break;
                 tc_fence_after();
-                // S(j) = Q K^T(j) into score buffer (g + j) % SBUF
-                auto issue_s = [&](int j) -> bool {
-                    const uint32_t s = (g + j) % C::SBUF, slot = n % NS;
-                    if (!mbar_wait(&sm.full[slot], (n / NS) & 1, err)) return false;
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_u32(sm.ring[slot]);
+                if constexpr (NT == 1) {
+                    // S(j) = Q K^T(j) into score buffer (g + j) % SBUF
+                    auto issue_s = [&](int j) -> bool {
+                        const uint32_t s = (g + j) % C::SBUF, slot = n % NS;
+                        if (!mbar_wait(&sm.full[slot], (n / NS) & 1, err)) return false;
+                        tc_fence_after();
+                        const uint32_t k_addr = smem_u32(sm.ring[slot]);
 #pragma unroll
-                    for (int kk = 0; kk < D / 8; kk++)
-                        mma_tf32_ts(tmem + C::S_COL + s * BN, tmem + C::Q_COL + kk * 8,
-                                    smem_desc_sw128_32b(k_addr + kk * 1024, C::K_CHUNK, 512), idesc_s, kk > 0 ? 1u : 0u);
-                    mma_commit(&sm.empty[slot]);
-                    mma_commit(&sm.s_full[s]);
-                    n++;
-                    return true;
-                };
-                for (int j = 0; ok && j < C::SBUF && j < n_t; j++) ok = issue_s(j);
-                for (int j = 0; ok && j < n_t; j++) {
-                    const uint32_t gj = g + j, s = gj % C::SBUF;
-                    if (!(ok = mbar_wait(&sm.p_full[s], (gj / C::SBUF) & 1, err))) break;
-                    const uint32_t slot = n % NS;
-                    if (!(ok = mbar_wait(&sm.full[slot], (n / NS) & 1, err))) break;
-                    tc_fence_after();
-                    const uint32_t v_addr = smem_u32(sm.ring[slot]);
+                        for (int kk = 0; kk < D / 8; kk++)
+                            mma_tf32_ts(tmem + C::S_COL + s * BN, tmem + C::Q_COL + kk * 8,
+                                        smem_desc_sw128_32b(k_addr + kk * 1024, C::K_CHUNK, 512), idesc_s, kk > 0 ? 1u : 0u);
+                        mma_commit(&sm.empty[slot]);
+                        mma_commit(&sm.s_full[0][s]);
+                        n++;
+                        return true;
+                    };
+                    for (int j = 0; ok && j < C::SBUF && j < n_t; j++) ok = issue_s(j);
+                    for (int j = 0; ok && j < n_t; j++) {
+                        const uint32_t gj = g + j, s = gj % C::SBUF;
+                        if (!(ok = mbar_wait(&sm.p_full[0][s], (gj / C::SBUF) & 1, err))) break;
+                        const uint32_t slot = n % NS;
+                        if (!(ok = mbar_wait(&sm.full[slot], (n / NS) & 1, err))) break;
+                        tc_fence_after();
+                        const uint32_t v_addr = smem_u32(sm.ring[slot]);
 #pragma unroll
-                    for (int kk = 0; kk < BN / 8; kk++)
-                        mma_tf32_ts(tmem + C::O_COL, tmem + C::S_COL + s * BN + kk * 8,
-                                    smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512), idesc_o,
-                                    (j > 0 || kk > 0) ? 1u : 0u);
-                    mma_commit(&sm.empty[slot]);
-                    n++;
-                    mma_commit(&sm.pv_done[gj & 1]);
-                    if (j + C::SBUF < n_t && !(ok = issue_s(j + C::SBUF))) break;
+                        for (int kk = 0; kk < BN / 8; kk++)
+                            mma_tf32_ts(tmem + C::O_COL, tmem + C::S_COL + s * BN + kk * 8,
+                                        smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512), idesc_o,
+                                        (j > 0 || kk > 0) ? 1u : 0u);
+                        mma_commit(&sm.empty[slot]);
+                        n++;
+                        mma_commit(&sm.pv_done[0][gj & 1]);
+                        if (j + C::SBUF < n_t && !(ok = issue_s(j + C::SBUF))) break;
+                    }
+                } else {
+                    // Two query tiles over the ring K0 V0 K1 V1 ...: K(j) is load n0 + 2j,
+                    // V(j) load n0 + 2j + 1. Order S_0(0) S_1(0), then per key tile j:
+                    // PV_0(j) S_0(j+1) PV_1(j) S_1(j+1). Each tile has one score buffer:
+                    // S_t(j+1) overwrites P_t(j) only after PV_t(j) in issue order, and S_t(j)
+                    // completes after PV_t(j-1), so the softmax may write P_t(j) and rescale
+                    // O_t as soon as it sees S_t(j). A slot is released by its second reader.
+                    const uint32_t n0 = n;
+                    auto issue_s = [&](int t, int j) -> bool {
+                        const uint32_t ln = n0 + 2u * (uint32_t)j, slot = ln % NS;
+                        if (t == 0) {
+                            if (!mbar_wait(&sm.full[slot], (ln / NS) & 1, err)) return false;
+                            tc_fence_after();
+                        }
+                        const uint32_t k_addr = smem_u32(sm.ring[slot]);
+                        const uint32_t tc = (uint32_t)t * C::TILE_COLS;
+#pragma unroll
+                        for (int kk = 0; kk < D / 8; kk++)
+                            mma_tf32_ts(tmem + tc + C::S_COL, tmem + tc + C::Q_COL + kk * 8,
+                                        smem_desc_sw128_32b(k_addr + kk * 1024, C::K_CHUNK, 512), idesc_s, kk > 0 ? 1u : 0u);
+                        if (t == NT - 1) mma_commit(&sm.empty[slot]);
+                        mma_commit(&sm.s_full[t][0]);
+                        return true;
+                    };
+                    for (int t = 0; ok && t < NT && n_t > 0; t++) ok = issue_s(t, 0);
+                    for (int j = 0; ok && j < n_t; j++) {
+                        const uint32_t gj = g + j;
+                        for (int t = 0; ok && t < NT; t++) {
+                            if (!(ok = mbar_wait(&sm.p_full[t][0], gj & 1, err))) break;
+                            const uint32_t ln = n0 + 2u * (uint32_t)j + 1u, slot = ln % NS;
+                            if (t == 0 && !(ok = mbar_wait(&sm.full[slot], (ln / NS) & 1, err))) break;
+                            tc_fence_after();
+                            const uint32_t v_addr = smem_u32(sm.ring[slot]);
+                            const uint32_t tc = (uint32_t)t * C::TILE_COLS;
+#pragma unroll
+                            for (int kk = 0; kk < BN / 8; kk++)
+                                mma_tf32_ts(tmem + tc + C::O_COL, tmem + tc + C::S_COL + kk * 8,
+                                            smem_desc_sw128_32b(v_addr + kk * 1024, C::V_CHUNK, 512), idesc_o,
+                                            (j > 0 || kk > 0) ? 1u : 0u);
+                            if (t == NT - 1) mma_commit(&sm.empty[slot]);
+                            mma_commit(&sm.pv_done[t][gj & 1]);
+                            if (j + 1 < n_t && !(ok = issue_s(t, j + 1))) break;
+                        }
+                    }
+                    n = n0 + 2u * (uint32_t)n_t;
                 }
                 g += n_t;
             }
@@ -263,8 +350,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             mma_commit(&sm.drain);
             mbar_wait_drain(&sm.drain, 0);
         }
+      }
     } else {
-        // ------------------------------------------------------------ softmax warps 2-5
+        if constexpr (NT == 2) regs_inc<REGS_SOFTMAX>();
+        // ------------------------------------------------------------ softmax warpgroups
+        const int t = NT == 2 ? (warp - C::SM_WARP0) >> 2 : 0;   // query tile of this warpgroup
+        const uint32_t tcol = (uint32_t)t * C::TILE_COLS;        // its TMEM columns
         const int quarter = warp & 3;                  // TMEM lanes this warp may access
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
@@ -275,9 +366,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // score MMAs, the last readers of Q, are complete), before this item's epilogue, so
         // the next item's first score tiles are computed while the epilogue runs.
         auto load_q = [&](int qidx) {
-            int qb, qkh, qmt;
-            item_of(a, qidx, qb, qkh, qmt);
-            const int qi = qmt * a.qn + il;
+            int qb, qkh, qu;
+            item_of(a, qidx, qb, qkh, qu);
+            const int qi = (qu * NT + t) * a.qn + il;     // past n_q for a tile past the last
             const bool qvalid = row < a.rows && qi < a.n_q;
             const float* qrow = a.q + (size_t)qb * a.q_bs + (size_t)(qvalid ? qi : 0) * a.q_stride +
                                 (size_t)(qvalid ? qkh * a.group + hg : 0) * D;
@@ -293,51 +384,49 @@ __global__ void __launch_bounds__(THREADS, 1)
                     v[e + 2] = __float_as_uint(f.z);
                     v[e + 3] = __float_as_uint(f.w);
                 }
-                tmem_st32(tmem + lane_addr + C::Q_COL + cc * 32, v);
+                tmem_st32(tmem + lane_addr + tcol + C::Q_COL + cc * 32, v);
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&sm.q_full);
+            mbar_arrive(&sm.q_full[t]);
         };
         uint32_t g = 0;
         bool ok = true;
         if ((int)blockIdx.x < a.n_items) load_q(blockIdx.x);
         for (int idx = blockIdx.x; ok && idx < a.n_items; idx += gridDim.x) {
-            int b, kh, mt;
-            item_of(a, idx, b, kh, mt);
-            const int n_t = item_tiles(a, mt);
+            int b, kh, u;
+            item_of(a, idx, b, kh, u);
+            const int n_t = item_tiles<NT>(a, u);
+            const int mt = u * NT + t;
             const int i = mt * a.qn + il;
             const bool valid = row < a.rows && i < a.n_q;
             const int lim = a.causal ? min(a.n_kv - a.n_q + min(i, a.n_q - 1) + 1, a.n_kv) : a.n_kv;
             float m = 0.f, l = 0.f;
             for (int j = 0; j < n_t; j++) {
                 const uint32_t gj = g + j, s = gj % C::SBUF;
-                if (!(ok = mbar_wait_warp(&sm.s_full[s], (gj / C::SBUF) & 1, err))) break;
+                if (!(ok = mbar_wait_warp(&sm.s_full[t][s], (gj / C::SBUF) & 1, err))) break;
                 tc_fence_after();
-                const uint32_t s_addr = tmem + lane_addr + C::S_COL + s * BN;
+                const uint32_t s_addr = tmem + lane_addr + tcol + C::S_COL + s * BN;
                 uint32_t sr[BN];
-#pragma unroll
-                for (int q4 = 0; q4 < BN / 32; q4++) {
-                    uint32_t x[32];
-                    tmem_ld32(s_addr + q4 * 32, x);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int e = 0; e < 32; e++) sr[q4 * 32 + e] = x[e];
-                }
+                tmem_ld128(s_addr, sr);  // the row's 128 scores, one load
+                tmem_ld_wait();
                 const int valid_keys = lim - j * BN;
                 if (valid_keys < BN) {
 #pragma unroll
                     for (int e = 0; e < BN; e++)
                         if (e >= valid_keys) sr[e] = __float_as_uint(-INFINITY);
                 }
+                // row max over 8 independent partial maxima, two new scores per three-input max
                 float mx[8];
 #pragma unroll
-                for (int e = 0; e < 8; e++) mx[e] = __uint_as_float(sr[e]);
+                for (int e = 0; e < 8; e++) mx[e] = fmaxf(__uint_as_float(sr[e]), __uint_as_float(sr[e + 8]));
 #pragma unroll
-                for (int e = 8; e < BN; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sr[e]));
+                for (int e0 = 16; e0 < BN; e0 += 16)
 #pragma unroll
-                for (int e = 0; e < 4; e++) mx[e] = fmaxf(mx[e], mx[e + 4]);
-                const float m_tile = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;
+                    for (int e = 0; e < 8; e++)
+                        mx[e] = fmax3(mx[e], __uint_as_float(sr[e0 + e]), __uint_as_float(sr[e0 + 8 + e]));
+                const float m_tile =
+                    fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7]))) * c;
                 // tile 0 always holds key 0, which every row sees: m_tile is finite there
                 float corr = 1.f;
                 bool rescale = false;
@@ -348,7 +437,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     m = m_tile;
                     rescale = true;
                 }
-                float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                float2 ls2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                 make_float2(0.f, 0.f)};
                 const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
 #pragma unroll
                 for (int e = 0; e < BN; e += 2) {
@@ -357,11 +447,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const float2 pe = (((e >> 1) & 15) < POLY_PAIRS) ? exp2_poly2(x)
                                                                     : make_float2(exp2_approx(x.x), exp2_approx(x.y));
                     const uint32_t p0 = to_tf32_int(pe.x), p1 = to_tf32_int(pe.y);
-                    ls2[(e >> 1) & 1] = __fadd2_rn(ls2[(e >> 1) & 1], make_float2(__uint_as_float(p0), __uint_as_float(p1)));
+                    ls2[(e >> 1) & 3] = __fadd2_rn(ls2[(e >> 1) & 3], make_float2(__uint_as_float(p0), __uint_as_float(p1)));
                     sr[e] = p0;
                     sr[e + 1] = p1;
                 }
-                l = l * corr + ((ls2[0].x + ls2[0].y) + (ls2[1].x + ls2[1].y));
+                {
+                    const float2 s01 = __fadd2_rn(ls2[0], ls2[1]), s23 = __fadd2_rn(ls2[2], ls2[3]);
+                    const float2 s4 = __fadd2_rn(s01, s23);
+                    l = l * corr + (s4.x + s4.y);
+                }
                 // PV(j - 1) must be done before O is rescaled; without a rescale P(j) is handed
                 // to the MMA thread first (its buffer's last reader, PV(j - SBUF), is already
                 // done) and the wait comes after, so PV(j) queues behind PV(j - 1) at once.
@@ -374,32 +468,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // (corr is 1 in the others).
                 const bool any_rescale = __any_sync(0xffffffffu, rescale);
                 if (j > 0 && any_rescale) {
-                    if (!(ok = mbar_wait_warp(&sm.pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1, err))) break;
+                    if (!(ok = mbar_wait_warp(&sm.pv_done[t][(gj - 1) & 1], ((gj - 1) >> 1) & 1, err))) break;
                     tc_fence_after();
                 }
                 if (any_rescale) {
 #pragma unroll
                     for (int cc = 0; cc < D / 32; cc++) {
                         uint32_t o[32];
-                        tmem_ld32(tmem + lane_addr + C::O_COL + cc * 32, o);
+                        tmem_ld32(tmem + lane_addr + tcol + C::O_COL + cc * 32, o);
                         tmem_ld_wait();
 #pragma unroll
                         for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-                        tmem_st32(tmem + lane_addr + C::O_COL + cc * 32, o);
+                        tmem_st32(tmem + lane_addr + tcol + C::O_COL + cc * 32, o);
                     }
                 }
-#pragma unroll
-                for (int q4 = 0; q4 < BN / 32; q4++) {
-                    uint32_t x[32];
-#pragma unroll
-                    for (int e = 0; e < 32; e++) x[e] = sr[q4 * 32 + e];
-                    tmem_st32(s_addr + q4 * 32, x);
-                }
+                tmem_st128(s_addr, sr);  // P over the scores, one store
                 tmem_st_wait();
                 tc_fence_before();
-                mbar_arrive(&sm.p_full[s]);
+                mbar_arrive(&sm.p_full[t][s]);
                 if (j > 0 && !any_rescale) {
-                    if (!(ok = mbar_wait_warp(&sm.pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1, err))) break;
+                    if (!(ok = mbar_wait_warp(&sm.pv_done[t][(gj - 1) & 1], ((gj - 1) >> 1) & 1, err))) break;
                     tc_fence_after();
                 }
             }
@@ -407,7 +495,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (idx + (int)gridDim.x < a.n_items) load_q(idx + gridDim.x);
             // ---- epilogue: O / l -> out[b][i][(kh * group + hg) * D ..]
             const uint32_t g_last = g + n_t - 1;
-            if (!(ok = mbar_wait_warp(&sm.pv_done[g_last & 1], (g_last >> 1) & 1, err))) break;
+            if (!(ok = mbar_wait_warp(&sm.pv_done[t][g_last & 1], (g_last >> 1) & 1, err))) break;
             tc_fence_after();
             const float inv = l > 0.f ? 1.0f / l : 0.f;
             float* orow = a.out + (size_t)b * a.out_bs + (size_t)(valid ? i : 0) * a.out_stride +
@@ -415,7 +503,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int cc = 0; cc < D / 32; cc++) {
                 uint32_t o[32];
-                tmem_ld32(tmem + lane_addr + C::O_COL + cc * 32, o);
+                tmem_ld32(tmem + lane_addr + tcol + C::O_COL + cc * 32, o);
                 tmem_ld_wait();
                 if (valid) {
 #pragma unroll
@@ -457,6 +545,26 @@ bool encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <int D, int NT>
+int launch_kernel(const CUtensorMap& mk, const CUtensorMap& mv, const prefill_tc::Args& a, int grid, cudaStream_t st) {
+    using namespace prefill_tc;
+    static std::mutex mu;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set[dev]) {
+            if (cudaFuncSetAttribute(prefill_tc_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_bytes<D, NT>()) != cudaSuccess)
+                return -1;
+            attr_set[dev] = true;
+        }
+    }
+    prefill_tc_kernel<D, NT><<<grid, Cfg<D, NT>::THREADS, smem_bytes<D, NT>(), st>>>(mk, mv, a);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
 template <int D>
 int launch_d(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaStream_t st) {
     using namespace prefill_tc;
@@ -475,7 +583,21 @@ int launch_d(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaS
     a.n_mt = (int)((p.n_q + qn - 1) / qn);
     a.causal = p.causal;
     a.err = err;
-    const long long n_items = (long long)n_batch * (long long)p.n_head_kv * a.n_mt;
+    const int slots = sm_count > 0 ? sm_count : 148;
+    // d = 64: two query tiles per item unless that leaves a worse last wave. A two-tile item
+    // costs about 1.74 one-tile items (measured over config 3's chunks), so the form with
+    // fewer item-waves by that weight wins: a full 256-query chunk of 16 sequences (256 pairs
+    // = 2 waves against 480 tiles = 4) runs paired, the 208-query last chunk (192 pairs = 2
+    // waves against 384 tiles = 3) unpaired.
+    const long long per_unit = (long long)n_batch * (long long)p.n_head_kv;
+    int nt = 1;
+    if (D == 64) {
+        const long long w1 = (per_unit * a.n_mt + slots - 1) / slots;
+        const long long w2 = (per_unit * ((a.n_mt + 1) / 2) + slots - 1) / slots;
+        if (w2 * 174 < w1 * 100) nt = 2;
+    }
+    a.n_units = (a.n_mt + nt - 1) / nt;
+    const long long n_items = per_unit * a.n_units;
     if (n_items <= 0 || n_items >= (1ll << 31)) return -1;
     a.n_items = (int)n_items;
 
@@ -504,23 +626,11 @@ int launch_d(const FlashParams& p, size_t n_batch, int sm_count, int* err, cudaS
             return -1;
     }
 
-    static std::mutex mu;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (!attr_set[dev]) {
-            if (cudaFuncSetAttribute(prefill_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem_bytes<D>()) != cudaSuccess)
-                return -1;
-            attr_set[dev] = true;
-        }
-    }
-    const int slots = sm_count > 0 ? sm_count : 148;
     const int grid = (int)std::min<long long>(n_items, slots);
-    prefill_tc_kernel<D><<<grid, THREADS, smem_bytes<D>(), st>>>(mk, mv, a);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+    if constexpr (D == 64) {
+        if (nt == 2) return launch_kernel<D, 2>(mk, mv, a, grid, st);
+    }
+    return launch_kernel<D, 1>(mk, mv, a, grid, st);
 }
 
 }  // namespace
