@@ -266,8 +266,10 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
     return r;
 }
 
-__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+__device__ __forceinline__ float ld_cluster(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, const void* dst, int c0, int c1) {
@@ -602,62 +604,44 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
-        // Rank o owns activation rows [o R, (o + 1) R), R = TN / ks. Once every rank's MMAs
-        // are done with its operand ring (first cluster barrier), each scaler stores its
-        // partial rows straight into the owner's ring, as row rk R + (row - o R) of rank
-        // rk's block there: remote stores, which do not wait on the cluster's latency the
-        // way remote loads would. After the second barrier every owner sums its rows from
-        // its own shared memory in rank order (the same order, so the same sums, whatever
-        // the timing), and no CTA touches another's memory again.
-        const int R = TN / a.ks, lr = __ffs(R) - 1;       // ks is a power of two
-        const int c0 = rank * R;
-        cluster_sync();
         if (scaler) {
 #pragma unroll
-            for (int c = 0; c < COLS; c++) {
-                const int row = cbase + c;
-                if (r0 + row >= a.m) break;
-                const int o = row >> lr;
-                st_cluster(cluster_addr(part + (rank * R + (row - o * R)) * PART_LD + jl, o), acc[c]);
-            }
+            for (int c = 0; c < COLS; c++) part[(cbase + c) * PART_LD + jl] = acc[c];
         }
         cluster_sync();
         if (scaler && row_ok) {
-            // a RoPE pair's first row also sums its partner's column. Four rows at a time:
-            // every rank's values of the four are loaded before the first add.
-            const int c_end = min(c0 + R, a.m - r0);
-            for (int cb = c0 + cg; cb < c_end && !second; cb += 8) {
-                float v[4], vb[4];
+            // this CTA's share of the activation rows, summed over the ranks in order; all
+            // ranks' values of a row are loaded before the first add, so the remote loads
+            // overlap instead of waiting one after another
+            const int c0 = (rank * TN) / a.ks, c1 = ((rank + 1) * TN) / a.ks;
+            uint32_t base[MAX_KS];
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    float p[MAX_KS], q[MAX_KS];
-                    const int c = min(cb + 2 * u, c0 + R - 1);
+            for (int rk = 0; rk < MAX_KS; rk++) base[rk] = rk < a.ks ? cluster_addr(part + jl, rk) : 0u;
+            // a RoPE pair's first row also sums its partner's column
+            const uint32_t partner = (uint32_t)half * 4;
+            for (int c = c0 + cg; c < c1 && !second; c += 2) {
+                if (r0 + c >= a.m) break;
+                float p[MAX_KS], q[MAX_KS];
 #pragma unroll
-                    for (int rk = 0; rk < MAX_KS; rk++) {
-                        const float* pr = part + (rk * R + (c - c0)) * PART_LD + jl;
-                        p[rk] = rk < a.ks ? pr[0] : 0.f;
-                        q[rk] = rope_pairs && rk < a.ks ? pr[half] : 0.f;
+                for (int rk = 0; rk < MAX_KS; rk++) {
+                    p[rk] = rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4) : 0.f;
+                    q[rk] = rope_pairs && rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4 + partner) : 0.f;
+                }
+                float v = 0.f, vb = 0.f;
+#pragma unroll
+                for (int rk = 0; rk < MAX_KS; rk++)
+                    if (rk < a.ks) {
+                        v = __fadd_rn(v, p[rk]);
+                        vb = __fadd_rn(vb, q[rk]);
                     }
-                    v[u] = 0.f;
-                    vb[u] = 0.f;
-#pragma unroll
-                    for (int rk = 0; rk < MAX_KS; rk++)
-                        if (rk < a.ks) {
-                            v[u] = __fadd_rn(v[u], p[rk]);
-                            vb[u] = __fadd_rn(vb[u], q[rk]);
-                        }
-                }
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int c = cb + 2 * u;
-                    if (c >= c_end) break;
-                    if (EPI == EPI_PLAIN) finish(a, r0 + c, jrow, v[u]);
-                    else if (EPI == EPI_QKV) finish_qkv(a.pp, r0 + c, sel, jrow, v[u]);
-                    else if (rope_pairs) finish_rope(a.pp, r0 + c, sel, jrow, v[u], vb[u]);
-                    else finish_rope_v(a.pp, r0 + c, jrow, v[u]);
-                }
+                if (EPI == EPI_PLAIN) finish(a, r0 + c, jrow, v);
+                else if (EPI == EPI_QKV) finish_qkv(a.pp, r0 + c, sel, jrow, v);
+                else if (rope_pairs) finish_rope(a.pp, r0 + c, sel, jrow, v, vb);
+                else finish_rope_v(a.pp, r0 + c, jrow, v);
             }
         }
+        // no CTA leaves while another may still read its partial tile
+        cluster_sync();
     }
 
     tc_fence_before();
