@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include <string>
 
 namespace zwg {
@@ -315,18 +316,43 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
     const size_t qbs = b ? b->q_batch_stride : 0, kbs = b ? b->k_batch_stride : 0;
     const size_t vbs = b ? b->v_batch_stride : 0, obs = b ? b->out_batch_stride : 0;
     // items per chunk: at most 256 MB of f32 staging per slot, and about twelve chunks when
-    // the batch allows, so the pipeline's fill and drain are short
+    // the batch allows. The first chunks grow 1, 2, 4, ... up to that size and the last ones
+    // shrink the same way: the copies in of the first chunk run with nothing beside them and
+    // the kernels and copies out of the last one likewise, so each call's fill and drain move
+    // one item, not a full chunk (12 calls of 64 windows: 2 ms per call before).
     const size_t item_bytes = (ex.q + ex.k + ex.v + ex.out) * sizeof(float);
     size_t per = std::max<size_t>(1, (size_t)(256u << 20) / std::max<size_t>(item_bytes, 1));
     per = std::min(per, std::max<size_t>(1, (nb + 11) / 12));
+    std::vector<size_t> ramp;  // 1, 2, 4, ... below per, while both ramps fit in the batch
+    {
+        size_t sum = 0;
+        for (size_t r = 1; r < per && 2 * (sum + r) <= nb; r *= 2) {
+            ramp.push_back(r);
+            sum += r;
+        }
+    }
+    size_t ramp_sum = 0;
+    for (size_t r : ramp) ramp_sum += r;
+    auto chunk_items = [&](size_t chunk, size_t i0) -> size_t {
+        if (chunk < ramp.size()) return ramp[chunk];
+        const size_t left = nb - i0;
+        if (left <= ramp_sum) {
+            // the falling ramp: the largest power of two of the rising one that leaves the
+            // rest to smaller chunks
+            for (size_t k = ramp.size(); k-- > 0;)
+                if (ramp[k] <= left) return ramp[k];
+            return left;
+        }
+        return std::min(per, left - ramp_sum);
+    };
     const zwg_attn_shape& s = *sh;
     const bool tc = (c->math & ZWG_MATH_BF16) && tc_eligible(sh);
     const size_t dq = ex.q, dk = ex.k, dv = ex.v, dout = ex.out;
     cudaError_t e = cudaSuccess;
     int rc = ZWG_OK;
     size_t chunk = 0;
-    for (size_t i0 = 0; i0 < nb && rc == ZWG_OK; i0 += per, chunk++) {
-        const size_t n = std::min(per, nb - i0);
+    for (size_t i0 = 0, n = 0; i0 < nb && rc == ZWG_OK; i0 += n, chunk++) {
+        n = std::min(chunk_items(chunk, i0), nb - i0);
         const int slot = (int)(chunk % Ctx::kSlots);
         zwg_batch db{n, dq, dk, dv, dout};
         Plan pl = plan_for(sh, n, c->sm_count);
@@ -344,13 +370,20 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
             rc = fail("device staging allocation failed");
             break;
         }
-        // ---- copies in
-        for (size_t j = 0; j < n && e == cudaSuccess; j++) {
-            const size_t it = i0 + j;
-            if (dq) e = cudaMemcpyAsync((float*)c->q[slot].ptr + j * dq, q + it * qbs, dq * 4, cudaMemcpyHostToDevice, c->side);
-            if (e == cudaSuccess && dk) e = cudaMemcpyAsync((float*)c->k[slot].ptr + j * dk, k + it * kbs, dk * 4, cudaMemcpyHostToDevice, c->side);
-            if (e == cudaSuccess && dv) e = cudaMemcpyAsync((float*)c->v[slot].ptr + j * dv, v + it * vbs, dv * 4, cudaMemcpyHostToDevice, c->side);
-        }
+        // ---- copies in: one copy per tensor when the chunk's items lie back to back on the
+        // host (batch stride = extent), else one per item (each copy has a fixed cost)
+        auto copy_in = [&](float* dst, const float* src, size_t d, size_t bs) -> cudaError_t {
+            if (!d) return cudaSuccess;
+            if (bs == d || n == 1)
+                return cudaMemcpyAsync(dst, src + i0 * bs, n * d * 4, cudaMemcpyHostToDevice, c->side);
+            cudaError_t r = cudaSuccess;
+            for (size_t j = 0; j < n && r == cudaSuccess; j++)
+                r = cudaMemcpyAsync(dst + j * d, src + (i0 + j) * bs, d * 4, cudaMemcpyHostToDevice, c->side);
+            return r;
+        };
+        e = copy_in((float*)c->q[slot].ptr, q, dq, qbs);
+        if (e == cudaSuccess) e = copy_in((float*)c->k[slot].ptr, k, dk, kbs);
+        if (e == cudaSuccess) e = copy_in((float*)c->v[slot].ptr, v, dv, vbs);
         if (e == cudaSuccess) e = cudaEventRecord(c->ev_in[slot], c->side);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(c->stream, c->ev_in[slot], 0);
         if (e != cudaSuccess) {
@@ -378,10 +411,14 @@ static int host_call(Ctx* c, const zwg_attn_shape* sh, const zwg_batch* b, const
         if ((e = cudaEventRecord(c->ev_comp[slot], st)) == cudaSuccess)
             e = cudaStreamWaitEvent(c->outs, c->ev_comp[slot], 0);
         // ---- copies out: only the head columns of each output row are written, as in the
-        // reference
-        for (size_t j = 0; j < n && e == cudaSuccess; j++)
-            e = cudaMemcpy2DAsync(out + (i0 + j) * obs, s.out_stride * 4, (float*)c->out[slot].ptr + j * dout,
-                                  s.out_stride * 4, s.n_head * s.d * 4, s.n_q, cudaMemcpyDeviceToHost, c->outs);
+        // reference; rows without gaps and items back to back on the host go in one copy
+        if (e == cudaSuccess && s.out_stride == s.n_head * s.d && (obs == dout || n == 1)) {
+            e = cudaMemcpyAsync(out + i0 * obs, c->out[slot].ptr, n * dout * 4, cudaMemcpyDeviceToHost, c->outs);
+        } else {
+            for (size_t j = 0; j < n && e == cudaSuccess; j++)
+                e = cudaMemcpy2DAsync(out + (i0 + j) * obs, s.out_stride * 4, (float*)c->out[slot].ptr + j * dout,
+                                      s.out_stride * 4, s.n_head * s.d * 4, s.n_q, cudaMemcpyDeviceToHost, c->outs);
+        }
         if (e == cudaSuccess) e = cudaEventRecord(c->ev_free[slot], c->outs);
         if (e != cudaSuccess) rc = cuda_fail("device to host copy", e);
     }
