@@ -187,9 +187,11 @@ ZWG_API int zwg_q8_quantize(const float* w, size_t n, size_t k, int8_t* q, float
 ZWG_API int zwg_linear_q8(const float* x, size_t m, size_t k, const int8_t* q, const float* scales,
                           const float* bias, size_t n, float* out, void* stream);
 
-/* Whether the Q8 products of 16 or more rows with k a multiple of 64 (zwg_linear_q8, the
- * decoder / LLM projections and the SiLU pair) run on the tcgen05 kernel (1, the default)
- * or on the register-tiled CUDA-core kernel (0). Process-wide; returns the previous
+/* Where the Q8 products of 16 or more rows with k a multiple of 64 (zwg_linear_q8, the
+ * decoder / LLM projections, the SiLU pair and the q/k/v products) run: 1 (the default) on
+ * the tcgen05 kernel except small products at up to 64 rows (k <= 1024 and at most 1.25 M
+ * weights, faster on the CUDA-core kernel), 2 on the tcgen05 kernel for every such
+ * product, 0 on the register-tiled CUDA-core kernel. Process-wide; returns the previous
  * setting; a negative argument only queries it. */
 ZWG_API int zwg_q8_tensor_cores(int enable);
 

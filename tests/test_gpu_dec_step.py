@@ -72,13 +72,22 @@ def oracle_decoder(Wd, hp):
     return dec
 
 
-@pytest.mark.parametrize("B", [1, 3, 16])
-def test_decoder_forward_greedy(env, B):
+@pytest.mark.parametrize("B,q8_mode", [(1, 1), (3, 1), (16, 1), (16, "always")], ids=["1", "3", "16", "16-tcgen05"])
+def test_decoder_forward_greedy(env, B, q8_mode):
     """A 3-token prompt for B windows with their own audio, then 4 greedy tokens fed back on
     the device (argmax without a penalty): logits within tolerance at every step, identical
-    tokens. At 16 windows every projection runs the tiled Q8 product and q/k/v one launch
-    whose epilogue appends k and v to the caches."""
+    tokens. At 16 windows every projection runs a 16-row Q8 product and q/k/v one launch
+    whose epilogue appends k and v to the caches: by default on the CUDA-core kernel (this
+    model's matrices are small), with the switch at "always" on the tcgen05 kernel."""
     torch, ops = env
+    prev = ops.q8_tensor_cores(q8_mode)
+    try:
+        run_decoder_forward_greedy(torch, ops, B)
+    finally:
+        ops.q8_tensor_cores(prev)
+
+
+def run_decoder_forward_greedy(torch, ops, B):
     hp = small_hp()
     Wd = W.weights_dict(W.synth_model(hp, seed=21))
     rng = np.random.default_rng(22 + B)

@@ -11,7 +11,8 @@ Whisper decoder's q/k/v product in tests/test_gpu_dec_step.py at 16 windows), th
 and 128-row tile forms, partial row and column tiles, k
 split over clusters of CTAs (deterministic), activations over a wide dynamic range, and the
 process-wide switch between the two kernels (which give different roundings, so the
-tensor-core kernel is seen to run)."""
+tensor-core kernel is seen to run). The module runs with the switch at "always" (every covered
+shape on the tcgen05 kernel); the default's routing by size is checked on its own."""
 import numpy as np
 import pytest
 
@@ -30,7 +31,7 @@ def env():
     import torch
 
     from zwhisper_b200 import ops
-    prev = ops.q8_tensor_cores(True)
+    prev = ops.q8_tensor_cores("always")
     yield torch, ops
     ops.q8_tensor_cores(prev)
 
@@ -64,11 +65,11 @@ def test_store_bias_matches_oracle(env, m, n, k, tc):
     x = rng.standard_normal((m, k), dtype=np.float32)
     w = rand_q8(rng, n, k)
     b = rng.standard_normal(n, dtype=np.float32)
-    ops.q8_tensor_cores(tc)
+    ops.q8_tensor_cores("always" if tc else False)
     try:
         got = ops.linear_q8(dev(torch, x), dev(torch, w[0]), dev(torch, w[1]), dev(torch, b)).cpu().numpy()
     finally:
-        ops.q8_tensor_cores(True)
+        ops.q8_tensor_cores("always")
     check(got, q8.linear(x, *w, b), bound(x, w) + np.abs(b))
 
 
@@ -139,16 +140,39 @@ def test_deterministic_and_distinct_from_cuda_cores(env):
     try:
         other = ops.linear_q8(x, tq, ts).cpu()
     finally:
-        ops.q8_tensor_cores(True)
+        ops.q8_tensor_cores("always")
     assert not torch.equal(outs[0], other)
 
 
 def test_switch_round_trips(env):
     torch, ops = env
-    assert ops.q8_tensor_cores() is True
-    assert ops.q8_tensor_cores(False) is True
-    assert ops.q8_tensor_cores() is False
-    assert ops.q8_tensor_cores(True) is False
+    assert ops.q8_tensor_cores() == 2
+    assert ops.q8_tensor_cores(False) == 2
+    assert ops.q8_tensor_cores() == 0
+    assert ops.q8_tensor_cores(True) == 0
+    assert ops.q8_tensor_cores() == 1
+    assert ops.q8_tensor_cores("always") == 1
+
+
+def test_default_mode_routes_by_size(env):
+    """The default setting sends a small product at up to 64 rows (k <= 1024, at most 1.25 M
+    weights) to the CUDA-core kernel and a longer k to the tcgen05 kernel: bit-identical to
+    the kernel forced for each (the two round differently, so the route is visible)."""
+    torch, ops = env
+
+    def run(mode, m, n, k):
+        x = dev(torch, np.random.default_rng(m + n + k).standard_normal((m, k), dtype=np.float32))
+        qo, so = rand_q8(np.random.default_rng(n * k), n, k)
+        ops.q8_tensor_cores(mode)
+        try:
+            return ops.linear_q8(x, dev(torch, qo), dev(torch, so)).cpu()
+        finally:
+            ops.q8_tensor_cores("always")
+
+    for m, n, k, small in ((32, 512, 512, True), (64, 2048, 512, True), (32, 512, 2048, False), (16, 4096, 512, False)):
+        auto, cc, tc = run(1, m, n, k), run(False, m, n, k), run("always", m, n, k)
+        assert not torch.equal(cc, tc), (m, n, k)
+        assert torch.equal(auto, cc if small else tc), (m, n, k, small)
 
 
 @pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "cuda_cores"])
@@ -158,10 +182,10 @@ def test_rope_pair_both_kernels(env, tc):
     tokens of 16 sequences (k split over a cluster) and 60- and 64-token chunks."""
     torch, ops = env
     from tests.test_gpu_llm_step import run_qkv
-    ops.q8_tensor_cores(tc)
+    ops.q8_tensor_cores("always" if tc else False)
     try:
         run_qkv(torch, ops, B=16, H=4, Hkv=2, d=64, n_ctx=32, chunks=[1, 1], seed=4)
         run_qkv(torch, ops, B=8, H=14, Hkv=2, d=64, n_ctx=128, chunks=[60, 1], seed=5)
         run_qkv(torch, ops, B=4, H=14, Hkv=2, d=128, n_ctx=128, chunks=[64, 1], seed=6, bias=False)
     finally:
-        ops.q8_tensor_cores(True)
+        ops.q8_tensor_cores("always")

@@ -716,8 +716,18 @@ int tc_launch(int epi, const float* x, size_t m, size_t k, const int8_t* wq, con
               const size_t* rows, float* out, int sm_count, cudaStream_t st) {
     using namespace q8tc;
     const bool pair = epi == EPI_SILU, sec = epi == EPI_ROPE || epi == EPI_QKV;
-    if (!q8tc::g_enabled.load(std::memory_order_relaxed)) return 1;
+    const int use = q8tc::g_enabled.load(std::memory_order_relaxed);
+    if (!use) return 1;
     if (m < 16 || n == 0 || k == 0 || k % BK) return 1;
+    // by size (the default): at up to 64 rows a short k over a small matrix is faster on the
+    // CUDA-core kernel, which has no fixed cost of TMEM, barriers and a cluster reduction
+    // (measured at 32 rows: 512 x 512 6.7 against 10.4 us, 2048 x 512 8.5 against 12.4,
+    // 896 x 896 at 64 rows 12.4 against 14.4; k 1536 and up, or more weights, favour the
+    // tensor cores: 512 x 2048 12.6 against 14.5, 51864 x 512 37 against 90)
+    if (use == 1 && m <= 64 && k <= 1024) {
+        const size_t w_rows = sec ? rows[0] + rows[1] + rows[2] : pair ? 2 * n : n;
+        if (w_rows * k <= (size_t)1310720) return 1;
+    }
     if (((uintptr_t)x & 15) || ((uintptr_t)wq & 15) || (pair && ((uintptr_t)wu & 15))) return 1;
     if (m > (1u << 30) || n > (1u << 30) || k > (1u << 30)) return 1;
     if (pair && mode != LIN_STORE) return 1;
@@ -845,5 +855,5 @@ int q8_tc_qkv_launch(const PairParams& p, int sm_count, cudaStream_t st) {
 
 extern "C" ZWG_API int zwg_q8_tensor_cores(int enable) {
     if (enable < 0) return zwg::q8tc::g_enabled.load();
-    return zwg::q8tc::g_enabled.exchange(enable ? 1 : 0);
+    return zwg::q8tc::g_enabled.exchange(enable >= 2 ? 2 : enable ? 1 : 0);
 }

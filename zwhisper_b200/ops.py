@@ -143,11 +143,19 @@ def set_math(mode: str, device: int = 0) -> None:
     _lib.check(_lib.load().zwg_set_math(code))
 
 
-def q8_tensor_cores(enable: Optional[bool] = None) -> bool:
-    """Whether Q8 products of 16 or more rows with k a multiple of 64 run on the tcgen05
-    kernel (zwg_q8_tensor_cores, process-wide, default on). With an argument, sets it and
-    returns the previous setting; without, returns the current one."""
-    return bool(_lib.load().zwg_q8_tensor_cores(-1 if enable is None else int(bool(enable))))
+def q8_tensor_cores(enable=None) -> int:
+    """Where Q8 products of 16 or more rows with k a multiple of 64 run (zwg_q8_tensor_cores,
+    process-wide): 1 / True (default) on the tcgen05 kernel except small products at up to
+    64 rows (k <= 1024, at most 1.25 M weights), 2 / "always" on the tcgen05 kernel for every
+    such product, 0 / False on the CUDA-core kernel. With an argument, sets it and returns
+    the previous setting; without, returns the current one."""
+    if enable is None:
+        code = -1
+    elif enable == "always":
+        code = 2
+    else:
+        code = int(enable)
+    return int(_lib.load().zwg_q8_tensor_cores(code))
 
 
 # ---- scratch sizers (src/ops.zig:545-560): device workspace in floats ----------------------
