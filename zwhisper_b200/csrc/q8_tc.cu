@@ -48,6 +48,7 @@
 #include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 #include "api_internal.h"
 #include "chain.cuh"
@@ -610,35 +611,52 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         cluster_sync();
         if (scaler && row_ok) {
-            // this CTA's share of the activation rows, summed over the ranks in order; all
-            // ranks' values of a row are loaded before the first add, so the remote loads
-            // overlap instead of waiting one after another
+            // this CTA's share of the activation rows, summed over the ranks in rank order.
+            // The remote loads of 16 / ks rows (all ks ranks each) are issued before the
+            // first add, so a batch costs one round trip through the cluster, not one per row
+            // (ks is 2, 4 or 8: the batch sizes are compile-time, the arrays registers).
             const int c0 = (rank * TN) / a.ks, c1 = ((rank + 1) * TN) / a.ks;
-            uint32_t base[MAX_KS];
-#pragma unroll
-            for (int rk = 0; rk < MAX_KS; rk++) base[rk] = rk < a.ks ? cluster_addr(part + jl, rk) : 0u;
             // a RoPE pair's first row also sums its partner's column
             const uint32_t partner = (uint32_t)half * 4;
-            for (int c = c0 + cg; c < c1 && !second; c += 2) {
-                if (r0 + c >= a.m) break;
-                float p[MAX_KS], q[MAX_KS];
+            auto reduce = [&](auto ks_c) {
+                constexpr int KS = decltype(ks_c)::value;
+                constexpr int RB = 16 / KS;  // rows per batch
+                uint32_t base[KS];
 #pragma unroll
-                for (int rk = 0; rk < MAX_KS; rk++) {
-                    p[rk] = rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4) : 0.f;
-                    q[rk] = rope_pairs && rk < a.ks ? ld_cluster(base[rk] + c * PART_LD * 4 + partner) : 0.f;
-                }
-                float v = 0.f, vb = 0.f;
+                for (int rk = 0; rk < KS; rk++) base[rk] = cluster_addr(part + jl, rk);
+                for (int cb = c0 + cg; cb < c1 && !second; cb += 2 * RB) {
+                    if (r0 + cb >= a.m) break;
+                    float p[RB][KS], q[RB][KS];
 #pragma unroll
-                for (int rk = 0; rk < MAX_KS; rk++)
-                    if (rk < a.ks) {
-                        v = __fadd_rn(v, p[rk]);
-                        vb = __fadd_rn(vb, q[rk]);
+                    for (int u = 0; u < RB; u++) {
+                        // rows past the share load a row of it (in bounds) and are not used
+                        const int c = min(cb + 2 * u, c1 - 1);
+#pragma unroll
+                        for (int rk = 0; rk < KS; rk++) {
+                            p[u][rk] = ld_cluster(base[rk] + c * PART_LD * 4);
+                            q[u][rk] = rope_pairs ? ld_cluster(base[rk] + c * PART_LD * 4 + partner) : 0.f;
+                        }
                     }
-                if (EPI == EPI_PLAIN) finish(a, r0 + c, jrow, v);
-                else if (EPI == EPI_QKV) finish_qkv(a.pp, r0 + c, sel, jrow, v);
-                else if (rope_pairs) finish_rope(a.pp, r0 + c, sel, jrow, v, vb);
-                else finish_rope_v(a.pp, r0 + c, jrow, v);
-            }
+#pragma unroll
+                    for (int u = 0; u < RB; u++) {
+                        const int c = cb + 2 * u;
+                        if (c >= c1 || r0 + c >= a.m) break;
+                        float v = 0.f, vb = 0.f;
+#pragma unroll
+                        for (int rk = 0; rk < KS; rk++) {
+                            v = __fadd_rn(v, p[u][rk]);
+                            vb = __fadd_rn(vb, q[u][rk]);
+                        }
+                        if (EPI == EPI_PLAIN) finish(a, r0 + c, jrow, v);
+                        else if (EPI == EPI_QKV) finish_qkv(a.pp, r0 + c, sel, jrow, v);
+                        else if (rope_pairs) finish_rope(a.pp, r0 + c, sel, jrow, v, vb);
+                        else finish_rope_v(a.pp, r0 + c, jrow, v);
+                    }
+                }
+            };
+            if (a.ks == 2) reduce(std::integral_constant<int, 2>{});
+            else if (a.ks == 4) reduce(std::integral_constant<int, 4>{});
+            else reduce(std::integral_constant<int, 8>{});
         }
         // no CTA leaves while another may still read its partial tile
         cluster_sync();
