@@ -27,6 +27,7 @@
 //
 // Launched as a programmatic dependent (chain.cuh): the weight rows of the CTA's k range are
 // prefetched into L2 before the wait for the kernel that wrote x.
+#include <type_traits>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -357,19 +358,48 @@ __global__ void __launch_bounds__(BM * 2) q8_gemm_kernel(const float* x, int m, 
     cluster_sync_all();
     const int rows = BM / ks, r0 = kz * rows;
     constexpr int OUTS = PAIR ? BN / 2 : BN;  // outputs per tile row
-    for (int e = t; e < rows * OUTS; e += THREADS) {
-        const int rr = r0 + e / OUTS, cc = e % OUTS;
-        const int row = m0 + rr, col = n0 + cc;
-        float v = 0.f, u = 0.f;
-        for (int q = 0; q < ks; q++) {
-            v = __fadd_rn(v, ld_cluster(cluster_addr(&sm.red[rr][cc], (uint32_t)q)));
-            if (PAIR) u = __fadd_rn(u, ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)));
+    // every rank's values of 16 / ks outputs are loaded before the first add, so a batch
+    // costs one round trip through the cluster instead of one per output (ks is 2, 4 or 8;
+    // the sums keep rank order)
+    auto reduce = [&](auto ks_c) {
+        constexpr int KS = decltype(ks_c)::value;
+        constexpr int EB = 16 / KS;  // outputs per batch
+        const int total = rows * OUTS;
+        for (int e0 = t; e0 < total; e0 += EB * THREADS) {
+            float pv[EB][KS], pu[EB][KS];
+#pragma unroll
+            for (int b = 0; b < EB; b++) {
+                // outputs past the share load one of it (in bounds) and are not used
+                const int e = min(e0 + b * THREADS, total - 1);
+                const int rr = r0 + e / OUTS, cc = e % OUTS;
+#pragma unroll
+                for (int q = 0; q < KS; q++) {
+                    pv[b][q] = ld_cluster(cluster_addr(&sm.red[rr][cc], (uint32_t)q));
+                    pu[b][q] = PAIR ? ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)) : 0.f;
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < EB; b++) {
+                const int e = e0 + b * THREADS;
+                if (e >= total) break;
+                const int rr = r0 + e / OUTS, cc = e % OUTS;
+                const int row = m0 + rr, col = n0 + cc;
+                float v = 0.f, u = 0.f;
+#pragma unroll
+                for (int q = 0; q < KS; q++) {
+                    v = __fadd_rn(v, pv[b][q]);
+                    if (PAIR) u = __fadd_rn(u, pu[b][q]);
+                }
+                if (row < m && col < n) {
+                    if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
+                    else finish_one<MODE, PE>(out, bias, pp, n, row, col, v);
+                }
+            }
         }
-        if (row < m && col < n) {
-            if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
-            else finish_one<MODE, PE>(out, bias, pp, n, row, col, v);
-        }
-    }
+    };
+    if (ks == 2) reduce(std::integral_constant<int, 2>{});
+    else if (ks == 4) reduce(std::integral_constant<int, 4>{});
+    else reduce(std::integral_constant<int, 8>{});
     // no CTA leaves while another may still read its partial tile
     cluster_sync_all();
 }
@@ -545,19 +575,48 @@ __global__ void __launch_bounds__(THREADS) q8_gemm_kernel(const float* x, int m,
     cluster_sync_all();
     const int rows = BM / ks, r0 = kz * rows;
     constexpr int OUTS = PAIR ? BN / 2 : BN;  // outputs per tile row
-    for (int e = t; e < rows * OUTS; e += THREADS) {
-        const int rr = r0 + e / OUTS, cc = e % OUTS;
-        const int row = m0 + rr, col = n0 + cc;
-        float v = 0.f, u = 0.f;
-        for (int q = 0; q < ks; q++) {
-            v = __fadd_rn(v, ld_cluster(cluster_addr(&sm.red[rr][cc], (uint32_t)q)));
-            if (PAIR) u = __fadd_rn(u, ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)));
+    // every rank's values of 16 / ks outputs are loaded before the first add, so a batch
+    // costs one round trip through the cluster instead of one per output (ks is 2, 4 or 8;
+    // the sums keep rank order)
+    auto reduce = [&](auto ks_c) {
+        constexpr int KS = decltype(ks_c)::value;
+        constexpr int EB = 16 / KS;  // outputs per batch
+        const int total = rows * OUTS;
+        for (int e0 = t; e0 < total; e0 += EB * THREADS) {
+            float pv[EB][KS], pu[EB][KS];
+#pragma unroll
+            for (int b = 0; b < EB; b++) {
+                // outputs past the share load one of it (in bounds) and are not used
+                const int e = min(e0 + b * THREADS, total - 1);
+                const int rr = r0 + e / OUTS, cc = e % OUTS;
+#pragma unroll
+                for (int q = 0; q < KS; q++) {
+                    pv[b][q] = ld_cluster(cluster_addr(&sm.red[rr][cc], (uint32_t)q));
+                    pu[b][q] = PAIR ? ld_cluster(cluster_addr(&sm.red[rr][BN / 2 + cc], (uint32_t)q)) : 0.f;
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < EB; b++) {
+                const int e = e0 + b * THREADS;
+                if (e >= total) break;
+                const int rr = r0 + e / OUTS, cc = e % OUTS;
+                const int row = m0 + rr, col = n0 + cc;
+                float v = 0.f, u = 0.f;
+#pragma unroll
+                for (int q = 0; q < KS; q++) {
+                    v = __fadd_rn(v, pv[b][q]);
+                    if (PAIR) u = __fadd_rn(u, pu[b][q]);
+                }
+                if (row < m && col < n) {
+                    if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
+                    else finish_one<MODE, PE>(out, bias, pp, n, row, col, v);
+                }
+            }
         }
-        if (row < m && col < n) {
-            if (PAIR) finish_two<PE>(out, bias, pp, n, row, col, v, u);
-            else finish_one<MODE, PE>(out, bias, pp, n, row, col, v);
-        }
-    }
+    };
+    if (ks == 2) reduce(std::integral_constant<int, 2>{});
+    else if (ks == 4) reduce(std::integral_constant<int, 4>{});
+    else reduce(std::integral_constant<int, 8>{});
     // no CTA leaves while another may still read its partial tile
     cluster_sync_all();
 }
